@@ -1,0 +1,440 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-KV decode hot path.
+
+One step = one attention layer of batched kv4 decode: quantize-on-append of
+one new K/V row per sequence into the layer's cache, then flash-decoding SDPA
+of 32 query heads (8 kv heads, GQA 4) over the 8193-row cache, for B = 8
+sequences (D 128, group 64, fp16, keys with 4 outlier channels x8).  Steps
+cycle through NL distinct layer caches whose total size (NL x 75.5 MB)
+exceeds twice the 126 MB L2, so every step streams its K/V from HBM; after
+each step the layer is trimmed by one token (host bookkeeping only) so every
+step does identical work.
+
+value      aggregate algorithmic HBM GB/s over all ranks (K/V packed codes +
+           scales + biases of 8193 rows, q, output, appended rows) for K steps
+           replayed from CUDA graphs, timed with CUDA events, max over ranks.
+e2e        the same metric through the public Python API per step, with the
+           step's q and new K/V rows copied from pinned host memory and the
+           output copied back inside the timed region.
+roofline   the decode kernel alone: algorithmic bytes per launch / its mean
+           CUDA-event duration inside the timed graphs, against the measured
+           HBM copy bandwidth.
+cpu_baseline / --impl reference
+           the CPU oracle (C restatement of mlx-bun's unfused op graph, all
+           host threads) on a bounded sample of the same workload.
+
+Multi-GPU (torchrun): each rank owns its own shard of sequences (weak
+scaling, no communication on the data path).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mlx-bun_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+CFG = dict(B=8, Hq=32, Hkv=8, D=128, N_prior=8192, bits=4, gs=64, outliers=4)
+METRIC = "quantized-KV decode SDPA achieved HBM GB/s (config 2: B8 Hq32 Hkv8 D128 N8193 kv4 gs64, append+decode per step)"
+UNIT = "GB/s"
+WORKLOAD = "config2-kv4-decode-append"
+FALLBACK_HBM = 6650.0
+
+
+def kv_row_bytes(c):
+    return 2 * (c["D"] * c["bits"] // 8 + 2 * (c["D"] // c["gs"]) * 2)
+
+
+def step_bytes(c):
+    N = c["N_prior"] + 1
+    kv = c["B"] * c["Hkv"] * N * kv_row_bytes(c)
+    q = c["B"] * c["Hq"] * c["D"] * 2
+    app = c["B"] * c["Hkv"] * c["D"] * 2 * 2
+    return kv + 2 * q + app
+
+
+def decode_launch_bytes(c):
+    N = c["N_prior"] + 1
+    return c["B"] * c["Hkv"] * N * kv_row_bytes(c) + 2 * c["B"] * c["Hq"] * c["D"] * 2
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+def traffic_from_profiles():
+    """dram bytes per decode launch from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "attn_decode_config2.md")
+    try:
+        for line in open(p):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip().split()[0])
+    except Exception:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.06)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        mhz = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------ CPU oracle --
+
+def cpu_oracle_sample(K_steps, budget_s, seed=0):
+    """Time the C oracle on (sequence, kv-head) pairs of config 2.
+
+    Returns (GB/s, threads, description).  Each timed call covers `pairs`
+    of the 64 (b, kv-head) pairs of one step (N = 8193 rows, 4 query heads
+    each), sized so K_steps calls take about `budget_s` seconds."""
+    import numpy as np
+    from oracle import oracle as O
+    c = CFG
+    N, D, nrep = c["N_prior"] + 1, c["D"], c["Hq"] // c["Hkv"]
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((1, 1, N, D)).astype(np.float32)
+    k[..., :c["outliers"]] *= 8.0
+    kb = O.to_dtype_bits(k, O.F16)
+    vb = O.to_dtype_bits(rng.standard_normal((1, 1, N, D)).astype(np.float32), O.F16)
+    kq = O.quantize(kb, c["gs"], c["bits"], O.F16)
+    vq = O.quantize(vb, c["gs"], c["bits"], O.F16)
+    threads = O.max_threads()
+    # one pair per thread per call: [threads, 1, N, *] replicated pair data
+    P = max(1, threads)
+    kqP = tuple(np.ascontiguousarray(np.broadcast_to(a, (P,) + a.shape[1:])) for a in kq)
+    vqP = tuple(np.ascontiguousarray(np.broadcast_to(a, (P,) + a.shape[1:])) for a in vq)
+    q = O.to_dtype_bits(rng.standard_normal((P, nrep, 1, D)).astype(np.float32), O.F16)
+    scale = 1.0 / np.sqrt(D)
+    O.sdpa_unfused(q, kqP, vqP, scale, c["gs"], c["bits"], O.F16)  # warm
+    t0 = time.perf_counter()
+    O.sdpa_unfused(q, kqP, vqP, scale, c["gs"], c["bits"], O.F16)
+    t_call = time.perf_counter() - t0
+    # time at most K_steps calls, and no more than budget_s of work
+    steps = max(1, min(K_steps, int(budget_s / max(t_call, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        O.sdpa_unfused(q, kqP, vqP, scale, c["gs"], c["bits"], O.F16)
+    el = time.perf_counter() - t0
+    pairs = P * steps
+    by = pairs * (N * kv_row_bytes(c) + 2 * nrep * D * 2)
+    desc = (f"{pairs} (sequence, kv-head) pairs of config 2 (N=8193, 4 query heads each, "
+            f"{pairs / 64:.2f} layer-steps), C oracle of the unfused op graph, {threads} threads")
+    return by / el / 1e9, threads, desc, el
+
+
+# ------------------------------------------------------------- GPU arm --
+
+def setup_layers(c, NL, device, seed):
+    import torch
+    import kvq
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    B, Hq, Hkv, D, Np = c["B"], c["Hq"], c["Hkv"], c["D"], c["N_prior"]
+    reserve = (Np + 1 + 255) // 256 * 256
+    layers = []
+    for _ in range(NL):
+        cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=reserve)
+        k = torch.randn(B, Hkv, Np, D, generator=g, device=device, dtype=torch.float32)
+        k[..., :c["outliers"]] *= 8.0
+        v = torch.randn(B, Hkv, Np, D, generator=g, device=device, dtype=torch.float32)
+        cache.update_and_fetch_quantized(k.half(), v.half())
+        del k, v
+        kn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
+        kn[..., :c["outliers"]] *= 8.0
+        vn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
+        q = torch.randn(B, Hq, 1, D, generator=g, device=device).half()
+        layers.append(dict(cache=cache, kn=kn, vn=vn, q=q, out=torch.empty_like(q)))
+    torch.cuda.synchronize()
+    return layers
+
+
+def gpu_step(L, scale):
+    import kvq
+    qk, qv = L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])
+    kvq.sdpa_decode(L["q"], qk, qv, scale, out=L["out"])
+    L["cache"].trim(1)
+
+
+def run_gpu(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import kvq
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    c = CFG
+    scale = 1.0 / np.sqrt(c["D"])
+    layer_bytes = c["B"] * c["Hkv"] * (c["N_prior"] + 1) * kv_row_bytes(c)
+    NL = max(4, int(np.ceil(2 * 126e6 * 1.5 / layer_bytes)))
+    layers = setup_layers(c, NL, device, seed=1000 + rank)
+    stream = torch.cuda.Stream(device)
+    # warm-up (also sizes the library-managed workspace before capture)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            gpu_step(layers[i % NL], scale)
+    stream.synchronize()
+
+    # ---- graphs: one replay = NL steps (one pass over the layers); events
+    # around each decode launch give the kernel's own duration.
+    per_graph = NL
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(per_graph)]
+    graph = torch.cuda.CUDAGraph()
+    events_in_graph = True
+    try:
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(per_graph):
+                L = layers[j]
+                qk, qv = L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])
+                ev[j][0].record()
+                kvq.sdpa_decode(L["q"], qk, qv, scale, out=L["out"])
+                ev[j][1].record()
+                L["cache"].trim(1)
+    except Exception:
+        events_in_graph = False
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(per_graph):
+                gpu_step(layers[j], scale)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    reps = max(1, (K + per_graph - 1) // per_graph)
+    K = reps * per_graph
+    clocks = Clocks(local_rank) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+        time.sleep(0.1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kern_ms = []
+    with torch.cuda.stream(stream):
+        e0.record()
+        for r in range(reps):
+            graph.replay()
+            if events_in_graph and r in (0, reps // 2, reps - 1):
+                pass
+        e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = e0.elapsed_time(e1)
+    if events_in_graph:
+        kern_ms = [a.elapsed_time(b) for a, b in ev]  # durations of the last replay
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # ---- kernel-only timing fallback: decode graphs alone
+    if not kern_ms:
+        g2 = torch.cuda.CUDAGraph()
+        views = [L["cache"].fetch() for L in layers]
+        with torch.cuda.graph(g2, stream=stream):
+            for j in range(per_graph):
+                kvq.sdpa_decode(layers[j]["q"], views[j][0], views[j][1], scale,
+                                out=layers[j]["out"])
+        g2.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record()
+            for _ in range(max(1, reps // 4)):
+                g2.replay()
+            b.record()
+        torch.cuda.synchronize()
+        kern_ms = [a.elapsed_time(b) / (max(1, reps // 4) * per_graph)]
+
+    # ---- e2e through the public API with host buffers
+    import kvq as _k  # noqa: F401
+    hq = [torch.empty_like(L["q"], device="cpu").pin_memory() for L in layers]
+    hk = [torch.empty_like(L["kn"], device="cpu").pin_memory() for L in layers]
+    hv = [torch.empty_like(L["vn"], device="cpu").pin_memory() for L in layers]
+    ho = [torch.empty_like(L["q"], device="cpu").pin_memory() for L in layers]
+    for j, L in enumerate(layers):
+        hq[j].copy_(L["q"])
+        hk[j].copy_(L["kn"])
+        hv[j].copy_(L["vn"])
+    K2 = min(K, max(200, NL * 50))
+    K2 = (K2 + NL - 1) // NL * NL
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record()
+        for i in range(K2):
+            j = i % NL
+            L = layers[j]
+            L["q"].copy_(hq[j], non_blocking=True)
+            L["kn"].copy_(hk[j], non_blocking=True)
+            L["vn"].copy_(hv[j], non_blocking=True)
+            qk, qv = L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])
+            kvq.sdpa_decode(L["q"], qk, qv, scale, out=L["out"])
+            L["cache"].trim(1)
+            ho[j].copy_(L["out"], non_blocking=True)
+        f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+
+    # sanity: the benchmarked output is finite
+    if not torch.isfinite(layers[0]["out"].float()).all():
+        raise RuntimeError("non-finite decode output")
+
+    sb = step_bytes(c)
+    value = world * sb * K / (ms_max / 1e3) / 1e9
+    e2e_value = world * sb * K2 / (e2e_ms / 1e3) / 1e9
+    kmean = sum(kern_ms) / len(kern_ms)
+    achieved = decode_launch_bytes(c) / (kmean / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    res = None
+    if rank == 0:
+        res = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5),
+            "us_per_step": round(1e3 * ms_max / K, 3),
+            "tokens_per_s": round(world * c["B"] * K / (ms_max / 1e3), 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes/f16",
+            "data": "synthetic (seeded torch.randn; keys with 4 outlier channels x8)",
+            "config": {"workload": WORKLOAD, "B_per_gpu": c["B"], "Hq": c["Hq"], "Hkv": c["Hkv"],
+                       "head_dim": c["D"], "context": c["N_prior"] + 1, "bits": c["bits"],
+                       "group_size": c["gs"], "layers_cycled": NL,
+                       "l2": f"inputs larger than L2: {NL} distinct layer caches, "
+                             f"{NL * layer_bytes / 1e6:.0f} MB cycled",
+                       "parallelism": f"shard by sequence, {world} GPU(s), no collective",
+                       "timing": "CUDA graphs of NL steps, CUDA events, max over ranks"},
+            "bytes_per_step": sb,
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT,
+                    "h2d_bytes_per_step": int(hq[0].numel() * 2 + hk[0].numel() * 2 + hv[0].numel() * 2),
+                    "d2h_bytes_per_step": int(ho[0].numel() * 2),
+                    "us_per_step": round(1e3 * e2e_ms / K2, 3), "steps": K2,
+                    "path": "kvq Python API per step (eager), pinned host buffers"},
+            "gpu_launches": 3 * K,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind, "kernel": "attn_kernel<4,128,64,1> (decode)",
+                         "kernel_us": round(kmean * 1e3, 3),
+                         "bytes_per_launch": decode_launch_bytes(c),
+                         "traffic": traffic_from_profiles(),
+                         "timing": "CUDA events around each decode launch inside the timed graphs"
+                         if events_in_graph else "decode-only graph replays"},
+            "clocks": clk,
+        }
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="kvq", choices=["kvq", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        K = max(1, args.steps)
+        budget = 60.0
+        gbs, threads, desc, el = cpu_oracle_sample(K, budget)
+        line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": UNIT,
+                "n_gpus": args.gpus, "steps": K, "warmup": args.warmup,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "u4 codes/f16", "data": "synthetic (seeded numpy)",
+                "config": {"workload": WORKLOAD},
+                "cpu_baseline": {"value": round(gbs, 4), "unit": UNIT, "cores": threads,
+                                 "kind": "port", "sample": desc},
+                "e2e": {"value": round(gbs, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "note": "mlx-bun's own CPU path (MLX CPU stream under Bun) cannot run on "
+                        "this box; the C restatement of its op graph is timed instead"}
+        print(json.dumps(line))
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res = run_gpu(args, rank, world, local_rank)
+        if rank == 0:
+            if world == 1 and not args.no_cpu_baseline:
+                gbs, threads, desc, el = cpu_oracle_sample(4, 12.0)
+                res["cpu_baseline"] = {"value": round(gbs, 4), "unit": UNIT, "cores": threads,
+                                       "kind": "port", "sample": desc}
+            print(json.dumps(res))
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,216 @@
+/*
+ * kvq.h — C ABI of libkvq, the B200 (sm_100a) quantized-KV attention library.
+ *
+ * A drop-in for mlx-bun's quantized-KV cache + SDPA hot path.  Every entry
+ * point takes plain integers, f32 scalars and pointers (no doubles by value,
+ * no C++ types), returns int32 status (0 = KVQ_OK) and leaves a message for
+ * kvq_last_error() on failure — the same convention as the mlx-c calls the
+ * reference binds through bun:ffi (src/mlx/ffi.ts:1-11, :270-293, :338-348).
+ * CUDA streams are passed as void* (cudaStream_t); NULL is the legacy
+ * default stream.  All device work is stream-ordered; no call synchronizes
+ * the host except where stated.
+ *
+ * Tensor layout (kept identical to MLX's affine quantized triple,
+ * src/mlx/ops.ts:607-611):
+ *   packed [B, H, rows, D*bits/32] uint32 — element e of a row in word
+ *          e/(32/bits) at bit bits*(e%(32/bits)), LSB first;
+ *   scales [B, H, rows, D/group_size] in the cache dtype (fp16 / bf16);
+ *   biases [B, H, rows, D/group_size] in the cache dtype.
+ * A kvq_qtensor names one such triple by three base pointers and row strides.
+ *
+ * Threading: a kvq_cache is not thread-safe; callers serialize access (the
+ * reference serializes generation the same way, src/model/gemma4-base.ts:43-46).
+ */
+#ifndef KVQ_H
+#define KVQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* mlx_dtype enum values (src/mlx/ffi.ts:297-300). */
+#define KVQ_DTYPE_FLOAT16 9
+#define KVQ_DTYPE_BFLOAT16 12
+
+/* Status codes. */
+#define KVQ_OK 0
+#define KVQ_ERR_ARG 1         /* invalid argument / unsupported shape */
+#define KVQ_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define KVQ_ERR_OOM 3         /* device allocation failed */
+#define KVQ_ERR_STATE 4       /* cache state does not allow the operation */
+#define KVQ_ERR_WORKSPACE 5   /* caller workspace too small */
+
+/* Mask modes for kvq_sdpa_prefill / kvq_debug_scores. */
+#define KVQ_MASK_NONE 0    /* attend every key ("" mode) */
+#define KVQ_MASK_CAUSAL 1  /* bottom-right aligned causal; window > 0 adds a sliding window */
+
+typedef struct kvq_cache kvq_cache;
+
+/* Cache description.  Replaces the constructor arguments of
+ * QuantizedKVCache(groupSize, bits) (src/model/gemma4-base.ts:419-431) and
+ * RotatingQuantizedKVCache(maxSize, groupSize, bits) (:932-951) plus the
+ * shape/dtype the reference takes from the first update. */
+typedef struct kvq_desc {
+  int32_t batch;        /* B */
+  int32_t kv_heads;     /* H (kv heads) */
+  int32_t head_dim;     /* D, same for K and V; multiple of group_size */
+  int32_t bits;         /* 4 or 8 */
+  int32_t group_size;   /* 32, 64 or 128 */
+  int32_t dtype;        /* KVQ_DTYPE_FLOAT16 or KVQ_DTYPE_BFLOAT16 */
+  int32_t max_size;     /* 0: growing QuantizedKVCache; > 0: rotating window of max_size rows */
+  int32_t reserve_rows; /* physical rows per head allocated up front (0: as the reference grows) */
+  int32_t device;       /* CUDA device ordinal the cache lives on */
+} kvq_desc;
+
+/* One quantized tensor [batch, heads, len, D] (a QuantizedTensor view,
+ * src/mlx/ops.ts:607-611).  Strides are in rows; row r of component c starts
+ * at c + r * (row size of c).  Row sizes: packed D*bits/32 uint32, scales and
+ * biases D/group_size dtype elements. */
+typedef struct kvq_qtensor {
+  void* packed;
+  void* scales;
+  void* biases;
+  int64_t batch_stride; /* rows between consecutive batch entries */
+  int64_t head_stride;  /* rows between consecutive heads */
+  int32_t batch;
+  int32_t heads;
+  int32_t len;          /* rows visible to attention */
+  int32_t head_dim;
+  int32_t bits;
+  int32_t group_size;
+  int32_t dtype;
+} kvq_qtensor;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* kvq_last_error(void);
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int32_t kvq_version(void);
+
+/* ---- cache lifecycle ---------------------------------------------------- */
+
+/* Create an empty cache (no device memory until the first append, unless
+ * reserve_rows > 0).  Replaces `new QuantizedKVCache` / `new
+ * RotatingQuantizedKVCache` (src/model/gemma4-base.ts:431, :951). */
+int32_t kvq_cache_create(const kvq_desc* desc, kvq_cache** out);
+
+/* Free the cache and its device memory (QuantizedKVCache.dispose, :593-597).
+ * Synchronizes the cache's device. */
+int32_t kvq_cache_free(kvq_cache* cache);
+
+/* Quantize-on-append: S new K/V rows per (batch, head), written at the
+ * position the reference's state machine picks, including growth in
+ * 256-row steps (QuantizedKVCache.updateAndFetchQuantized, :452-507) and,
+ * for rotating caches, the in-place ring write with wraparound for S == 1
+ * (#updateInPlace, :1026-1086) or the temporal re-layout + trim + concat for
+ * S > 1 (#updateConcat, :1003-1024).
+ * k, v: device pointers to dtype values of logical shape [B, H, S, D] with
+ * element strides k_strides[4] / v_strides[4] for (b, h, s, d); the d stride
+ * must be 1 (so both [B,H,S,D] and [B,S,H,D] inputs work without a copy).
+ * Host-side offset / ring index follow the reference exactly. */
+int32_t kvq_append(kvq_cache* cache, const void* k, const void* v, int32_t S,
+                   const int64_t* k_strides, const int64_t* v_strides, void* stream);
+
+/* Active quantized views after the last append (the [0:offset] slices of
+ * updateAndFetchQuantized, :499-506, or #activeSlices, :1097-1104). */
+int32_t kvq_cache_fetch(const kvq_cache* cache, kvq_qtensor* keys, kvq_qtensor* values);
+
+/* Host state: offset (tokens seen), ring index (rotating caches; equals the
+ * offset-derived write index the reference keeps in `ringIdx`), buffer length
+ * in rows (the reference's keys.packed.shape[2]) and physical capacity. */
+int32_t kvq_cache_state(const kvq_cache* cache, int64_t* offset, int64_t* ring_idx,
+                        int64_t* seq_len, int64_t* capacity);
+
+/* Drop the last n tokens (QuantizedKVCache.trim :589-591; rotating trim
+ * :1137-1163 with the speculative-decode `bypass` form). */
+int32_t kvq_cache_trim(kvq_cache* cache, int32_t n, int32_t bypass);
+
+/* Mask for an N-token step given the cache state (makeMask, :509-519 and
+ * :1113-1122), as a (mode, window) pair for kvq_sdpa_prefill.  window_size
+ * <= 0 means "no window" (the reference's null). */
+int32_t kvq_cache_make_mask(const kvq_cache* cache, int32_t N, int32_t window_size,
+                            int32_t* mask_mode, int32_t* mask_window);
+
+/* ---- conversion --------------------------------------------------------- */
+
+/* Affine group quantize of `rows` contiguous rows of D dtype values into
+ * contiguous packed / scales / biases (mlx_quantize as called by
+ * ops.quantize, src/mlx/ops.ts:615-637; also the bulk step of
+ * KVCache.toQuantized, src/model/gemma4-base.ts:395-404). */
+int32_t kvq_quantize(const void* x, int64_t rows, int32_t head_dim, int32_t group_size,
+                     int32_t bits, int32_t dtype, void* packed, void* scales, void* biases,
+                     void* stream);
+
+/* ---- attention ---------------------------------------------------------- */
+
+/* Workspace bytes kvq_sdpa_decode / kvq_sdpa_decode_partial need for these
+ * shapes.  Replaces nothing in the reference (MLX allocates internally). */
+int32_t kvq_sdpa_decode_workspace(const kvq_qtensor* keys, int32_t q_heads, size_t* bytes);
+
+/* L = 1 attention over a quantized K/V pair (quantizedSdpa's decode cases:
+ * fusedDecodeSdpa, src/model/fused-decode-kernel.ts:274-312, and
+ * quantizedSdpaUnfused with mask "", src/model/gemma4-base.ts:1273-1342).
+ * q:   device [B, q_heads, 1, D] dtype, contiguous; query head h uses kv head
+ *      h / (q_heads / kv_heads).
+ * out: device [B, q_heads, 1, D] dtype.
+ * scale is applied as q * dtype(scale) rounded to dtype, like mulScalar.
+ * seq_lens: NULL, or a DEVICE int32[B] of per-sequence key counts
+ *      (<= keys->len) for ragged batches.
+ * workspace: NULL (library-managed, cached per device) or a device buffer of
+ *      at least kvq_sdpa_decode_workspace() bytes, zero-filled before its
+ *      first use; every call leaves it reusable.  Calls sharing one
+ *      workspace must not overlap on the GPU. */
+int32_t kvq_sdpa_decode(const kvq_qtensor* keys, const kvq_qtensor* values, const void* q,
+                        int32_t q_heads, float scale, const int32_t* seq_lens, void* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same attention, but instead of the normalized output it writes the
+ * log-sum-exp partials of this key range for a context split across GPUs:
+ * m[B*q_heads] (max logit), l[B*q_heads] (sum of exp(s - m)), and
+ * o[B*q_heads, D] (sum of exp(s - m) * v, f32, unnormalized).  No
+ * reference counterpart (the reference is single-device). */
+int32_t kvq_sdpa_decode_partial(const kvq_qtensor* keys, const kvq_qtensor* values,
+                                const void* q, int32_t q_heads, float scale,
+                                const int32_t* seq_lens, float* m, float* l, float* o,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Merge `parts` partial sets laid out part-major (m[parts][rows],
+ * l[parts][rows], o[parts][rows][D]) into out[rows][D] in dtype, in fixed
+ * part order (deterministic, like the reference's merge kernel,
+ * src/model/fused-decode-kernel.ts:205-222). */
+int32_t kvq_sdpa_merge(const float* m, const float* l, const float* o, int32_t parts,
+                       int32_t rows, int32_t head_dim, int32_t dtype, void* out, void* stream);
+
+/* L > 1 attention of L new query rows per head over the cache (chunked
+ * prefill; quantizedSdpaTiled, src/model/gemma4-base.ts:1356-1521, and the
+ * unfused window-mask case).  q: device [B, q_heads, L, D]; out likewise.
+ * Query row i sits at key position keys->len - L + i (bottom-right aligned);
+ * mask_mode KVQ_MASK_CAUSAL keeps keys j <= that position, and window > 0
+ * additionally keeps only j > position - window (createCausalMask,
+ * :1595-1614).  Workspace as for kvq_sdpa_decode (may be NULL). */
+int32_t kvq_sdpa_prefill(const kvq_qtensor* keys, const kvq_qtensor* values, const void* q,
+                         int32_t q_heads, int32_t L, float scale, int32_t mask_mode,
+                         int32_t window, void* out, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Debug: the scaled, masked logits [B, q_heads, L, keys->len] as f32, each
+ * rounded to dtype as the reference's quantized_matmul output is
+ * (src/model/gemma4-base.ts:1307-1330); masked entries are -inf.  Not a hot
+ * path. */
+int32_t kvq_debug_scores(const kvq_qtensor* keys, const void* q, int32_t q_heads, int32_t L,
+                         float scale, int32_t mask_mode, int32_t window, float* scores,
+                         void* stream);
+
+/* Synchronize `stream` and report (then clear) the device error flag that a
+ * kernel raises when a bounded wait on its own TMA copies times out.
+ * workspace: the caller workspace used by the calls, or NULL for the
+ * library-managed one of the current device. */
+int32_t kvq_check_device(void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVQ_H */

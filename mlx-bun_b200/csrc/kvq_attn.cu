@@ -1,0 +1,981 @@
+// kvq_attn.cu — attention over MLX affine-quantized K/V for sm_100a.
+//
+// One kernel serves decode (L = 1), the context-split partial form and an
+// interim chunked prefill.  Work unit: a CTA owns one (batch, kv head, block
+// of 8*NT query rows, key split).  Query rows are (position, head) pairs of
+// the GQA group (row qr -> position qr / nrep, head qr % nrep), so every K/V
+// byte a CTA streams serves all query heads that share it.
+//
+// Data path per warp (W warps per CTA, round-robin over 16-row key tiles):
+//   * TMA bulk copies (cp.async.bulk, 1-D) move the tile's packed K, K
+//     scales, K biases, packed V, V scales, V biases (6 contiguous row
+//     ranges of one (b, h)) into a warp-private STAGES-deep shared-memory
+//     ring; completion is tracked by one mbarrier per stage.  Every wait is
+//     bounded: on timeout the kernel raises a device error flag and returns.
+//   * Codes are dequantised in registers to exact fp16 integers with the
+//     0x6400 (= 1024.0) magic: (bits | 0x6400) - 1024.  Four-bit codes in
+//     odd nibbles are taken unshifted as 16*c and the factor 16 is folded
+//     into the query (QK) or the output tile (PV).  Scales and biases are
+//     factored out of the inner products (qdot factoring, as in mlx-bun's
+//     Metal decode kernel, src/model/fused-decode-kernel.ts:62-114):
+//        q . (s*c + b) = s * (q . c) + b * sum(q)
+//        sum_n p_n (s_n c_n + b_n) = sum_n (p_n s_n) c_n + sum_n p_n b_n
+//     so the tensor cores only see exact integer codes.
+//   * QK^T: mma.m16n8k16 with the 16 key rows as M (codes as A, row-major
+//     pairs along d), the query rows as N (8 per n-tile, q as B, loaded once
+//     per CTA), d as K — one accumulator per quantisation group.
+//   * Online softmax in f32 (exp2 with log2e prescale); scores are rounded
+//     to the cache dtype first, as the reference graph rounds them
+//     (src/model/gemma4-base.ts:1307).
+//   * PV: O^T[d x q] += V^T[d x n] (p*s)^T[n x q]; the probability tile goes
+//     from the QK accumulator layout to the B-operand layout with one
+//     movmatrix.trans per 8x8 block; V codes for a (d, 2 rows) pair are
+//     interleaved with one prmt per 16-bit chunk.
+//   * Splits of the key range merge in fixed order (deterministic) in the
+//     last CTA to finish, found by an atomic ticket — no second launch.
+//
+// Tensor-core choice: decode is HBM-bound with at most 16 query rows per kv
+// head, so the register-sourced mma.sync keeps the dequantised codes in
+// registers (no shared-memory round trip) with ample tensor throughput
+// (2 MMAs per key row).  The tcgen05/TMEM path is the prefill kernel's.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "kvq_internal.h"
+
+namespace kvq {
+namespace {
+
+constexpr float kNeg = -1.0e30f;             // finite "minus infinity" for masked logits
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kTile = 16;                     // key rows per warp tile
+constexpr long long kWaitLimit = 1ll << 30;     // mbarrier polls before declaring a hang
+constexpr uint64_t kWaitNs = 2000000000ull;     // ... or 2 s of %globaltimer, whichever first
+
+struct Params {
+  const uint8_t* kp;
+  const uint16_t* ks;
+  const uint16_t* kb;
+  const uint8_t* vp;
+  const uint16_t* vs;
+  const uint16_t* vb;
+  int64_t k_bstride, k_hstride, v_bstride, v_hstride;  // rows
+  const uint16_t* q;     // [B, Hq, L, D]
+  uint16_t* out;         // [B, Hq, L, D] (mode 0)
+  float* pm;             // mode 1 partials [B*Hq]
+  float* pl;
+  float* po;             // [B*Hq, D]
+  float* ws_o;           // split partials
+  float* ws_ml;
+  unsigned* counters;
+  const int32_t* seq_lens;
+  int* err;
+  float* scores;         // debug: rounded logits [B, Hq, L, N] (nullable)
+  int Hq, Hkv, nrep, N, L, QB, rps, nsplit, mode, mask_mode, window;
+  float scale;
+  int bf16;
+};
+
+// ---------------------------------------------------------------- PTX ----
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait; false on timeout (the caller raises the device error flag).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (long long i = 0; i < kWaitLimit; i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && global_ns() - t0 > kWaitNs) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// (x as f16x2) - (1024, 1024): exact integer codes from the 0x6400 magic.
+__device__ __forceinline__ uint32_t sub1024(uint32_t x) {
+  uint32_t r;
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(0x64006400u));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float dt_to_f(uint16_t v, int bf16) {
+  return bf16 ? __uint_as_float((uint32_t)v << 16) : __half2float(__ushort_as_half(v));
+}
+
+__device__ __forceinline__ uint16_t f_to_dt(float f, int bf16) {
+  return bf16 ? __bfloat16_as_ushort(__float2bfloat16_rn(f)) : __half_as_ushort(__float2half_rn(f));
+}
+
+__device__ __forceinline__ float round_dt(float f, int bf16) {
+  return bf16 ? __bfloat162float(__float2bfloat16_rn(f)) : __half2float(__float2half_rn(f));
+}
+
+// K operand (pairs along d within one row).  4-bit word w holds nibbles
+// e0..e7: x0 = (e0, e4), x1 = 16*(e1, e5), x2 = (e2, e6), x3 = 16*(e3, e7).
+// 8-bit word: x0 = (b0, b1), x1 = (b2, b3).
+template <int BITS>
+__device__ __forceinline__ uint32_t k_extract(uint32_t w, int x) {
+  if (BITS == 4) {
+    const uint32_t s = (x >= 2) ? (w >> 8) : w;
+    const uint32_t m = (x & 1) ? 0x00F000F0u : 0x000F000Fu;
+    return sub1024((s & m) | 0x64006400u);
+  } else {
+    return sub1024(prmt(w, 0x64u, x ? 0x4342u : 0x4140u));
+  }
+}
+
+// V operand: T holds a 16-bit chunk of row r0 (low half) and of row r1 (high
+// half); element j of the chunk as the pair (r0, r1).
+template <int BITS>
+__device__ __forceinline__ uint32_t v_extract(uint32_t T, int j) {
+  if (BITS == 4) {
+    const uint32_t s = (j >= 2) ? (T >> 8) : T;
+    const uint32_t m = (j & 1) ? 0x00F000F0u : 0x000F000Fu;
+    return sub1024((s & m) | 0x64006400u);
+  } else {
+    return sub1024(prmt(T, 0x64u, j ? 0x4341u : 0x4240u));
+  }
+}
+
+template <int NBYTES>
+__device__ __forceinline__ void lds_words(uint32_t* w, const uint8_t* p) {
+  if (NBYTES == 2) {
+    w[0] = *reinterpret_cast<const uint16_t*>(p);
+  } else if (NBYTES == 4) {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  } else if (NBYTES == 8) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    w[0] = u.x;
+    w[1] = u.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < NBYTES / 16; i++) {
+      const uint4 u = *reinterpret_cast<const uint4*>(p + 16 * i);
+      w[4 * i] = u.x;
+      w[4 * i + 1] = u.y;
+      w[4 * i + 2] = u.z;
+      w[4 * i + 3] = u.w;
+    }
+  }
+}
+
+template <int BITS, int D, int GS>
+struct Geo {
+  static constexpr int NG = D / GS;             // quantisation groups per row
+  static constexpr int KRB = D * BITS / 8;      // packed bytes per row
+  static constexpr int SRB = NG * 2;            // scale (or bias) bytes per row
+  static constexpr int GB = GS * BITS / 8;      // packed bytes per group
+  static constexpr int KB = GS * BITS / 32;     // K bytes per lane per (row, group)
+  static constexpr int KW = KB / 4;             // ... as words
+  static constexpr int E = BITS == 4 ? 4 : 2;   // elements per 16-bit chunk
+  static constexpr int C = GS / 8 / E;          // 16-bit V chunks per lane per (row, group)
+  static constexpr int VB = 2 * C;              // V bytes per lane per (row, group)
+  static constexpr int VW = (VB + 3) / 4;
+  static constexpr int MTG = GS / 16;           // PV m-tiles (16 d) per group
+  static constexpr int KSTEPS = D / 16;
+  static constexpr int MT = D / 16;
+  static constexpr int O_KP = 0;
+  static constexpr int O_KS = O_KP + kTile * KRB;
+  static constexpr int O_KB = O_KS + kTile * SRB;
+  static constexpr int O_VP = O_KB + kTile * SRB;
+  static constexpr int O_VS = O_VP + kTile * KRB;
+  static constexpr int O_VB = O_VS + kTile * SRB;
+  static constexpr int STAGE = O_VB + kTile * SRB;
+  static_assert(KB >= 4, "unsupported group size / bits");
+  static_assert((kTile * SRB) % 16 == 0, "scale rows must tile in 16-byte units");
+};
+
+template <int BITS, int D, int GS, int NT, int W, int STAGES>
+struct Smem {
+  using G = Geo<BITS, D, GS>;
+  static constexpr int HQ = 8 * NT;
+  static constexpr int Q_F = 0;                                  // f32 [HQ][D]
+  static constexpr int QSUM = Q_F + HQ * D * 4;                  // f32 [HQ][NG]
+  static constexpr int BARS = (QSUM + HQ * G::NG * 4 + 15) / 16 * 16;
+  static constexpr int STAGES_OFF = (BARS + W * STAGES * 8 + 127) / 128 * 128;
+  static constexpr int STAGE_BYTES = W * STAGES * G::STAGE;
+  static constexpr int MERGE_BYTES = W * HQ * (D + 2) * 4;
+  static constexpr int CTRL = STAGES_OFF + (STAGE_BYTES > MERGE_BYTES ? STAGE_BYTES : MERGE_BYTES);
+  static constexpr int TOTAL = CTRL + 16;
+};
+
+template <int BITS, int D, int GS, int NT, int W, int STAGES>
+__global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
+  using G = Geo<BITS, D, GS>;
+  using S = Smem<BITS, D, GS, NT, W, STAGES>;
+  constexpr int HQ = S::HQ;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* q_f = reinterpret_cast<float*>(smem + S::Q_F);
+  float* qsum = reinterpret_cast<float*>(smem + S::QSUM);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BARS);
+  uint8_t* stages = smem + S::STAGES_OFF;
+  float* mrg = reinterpret_cast<float*>(smem + S::STAGES_OFF);  // aliases stages after the loop
+  int* ctrl = reinterpret_cast<int*>(smem + S::CTRL);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y % p.Hkv;
+  const int qb = blockIdx.y / p.Hkv;
+  const int b = blockIdx.z;
+  const int nrep = p.nrep, L = p.L, bf = p.bf16;
+  const int qrows = nrep * L;
+  const int qr0 = qb * HQ;
+
+  int Nb = p.N;
+  if (p.seq_lens) Nb = min(max(p.seq_lens[b], 0), p.N);
+
+  // Key range of this query block (union over its rows), then this split's share.
+  int lo = 0, hi = Nb;
+  if (p.mask_mode == 1) {
+    const int qr_last = min(qr0 + HQ, qrows) - 1;
+    const int pos_first = Nb - L + qr0 / nrep, pos_last = Nb - L + qr_last / nrep;
+    hi = min(Nb, pos_last + 1);
+    if (p.window > 0) lo = max(0, pos_first - p.window + 1) / kTile * kTile;
+    if (hi < lo) hi = lo;
+  }
+  const int nact = max(1, (hi - lo + p.rps - 1) / p.rps);
+  if (split >= nact) return;
+  const int n0 = lo + split * p.rps;
+  const int n1 = min(n0 + p.rps, hi);
+
+  // ---- stage the query block: q * dtype(scale), rounded to dtype ----
+  const float scale_dt = round_dt(p.scale, bf);
+  for (int i = tid; i < HQ * D; i += W * 32) {
+    const int r = i / D, d = i - r * D;
+    const int qr = qr0 + r;
+    float v = 0.0f;
+    if (qr < qrows) {
+      const int l = qr / nrep, hh = qr - l * nrep;
+      const int hq = kvh * nrep + hh;
+      const uint16_t raw = p.q[(((int64_t)b * p.Hq + hq) * L + l) * D + d];
+      v = round_dt(dt_to_f(raw, bf) * scale_dt, bf);
+    }
+    q_f[i] = v;
+  }
+  if (tid < W * STAGES) mbar_init(&bars[tid], 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncthreads();
+  for (int i = tid; i < HQ * G::NG; i += W * 32) {
+    const int r = i / G::NG, grp = i - r * G::NG;
+    float s = 0.0f;
+    for (int d = 0; d < GS; d++) s += q_f[r * D + grp * GS + d];
+    qsum[i] = s;
+  }
+
+  // ---- per-warp TMA ring over this warp's key tiles ----
+  const int ntiles = (n1 - n0 + kTile - 1) / kTile;
+  const int my_tiles = ntiles > warp ? (ntiles - warp + W - 1) / W : 0;
+  uint8_t* wst = stages + warp * STAGES * G::STAGE;
+  uint64_t* wbar = bars + warp * STAGES;
+  const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
+  const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
+
+  auto issue = [&](int i) {
+    const int s = i % STAGES;
+    const int64_t row = n0 + (int64_t)(warp + i * W) * kTile;
+    uint8_t* st = wst + s * G::STAGE;
+    mbar_expect_tx(&wbar[s], 2 * kTile * (G::KRB + 2 * G::SRB));
+    bulk_g2s(st + G::O_KP, p.kp + (kbase + row) * G::KRB, kTile * G::KRB, &wbar[s]);
+    bulk_g2s(st + G::O_KS, p.ks + (kbase + row) * G::NG, kTile * G::SRB, &wbar[s]);
+    bulk_g2s(st + G::O_KB, p.kb + (kbase + row) * G::NG, kTile * G::SRB, &wbar[s]);
+    bulk_g2s(st + G::O_VP, p.vp + (vbase + row) * G::KRB, kTile * G::KRB, &wbar[s]);
+    bulk_g2s(st + G::O_VS, p.vs + (vbase + row) * G::NG, kTile * G::SRB, &wbar[s]);
+    bulk_g2s(st + G::O_VB, p.vb + (vbase + row) * G::NG, kTile * G::SRB, &wbar[s]);
+  };
+  __syncthreads();  // qsum visible; barriers initialised
+  if (lane == 0)
+    for (int i = 0; i < STAGES && i < my_tiles; i++) issue(i);
+
+  // ---- query fragments (B operand of QK), loaded once ----
+  uint32_t qbf[G::KSTEPS][NT][2];
+#pragma unroll
+  for (int kk = 0; kk < G::KSTEPS; kk++) {
+    const int grp = kk / G::MTG, kin = kk % G::MTG;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      const float* qrow = q_f + (nt * 8 + g) * D;
+#pragma unroll
+      for (int w2 = 0; w2 < 2; w2++) {
+        const int v = 2 * kin + w2;
+        int d_lo, d_hi;
+        float f = 1.0f;
+        if (BITS == 4) {
+          const int wi = v / 4, x = v % 4;
+          const int base = grp * GS + t * (GS / 4) + 8 * wi;
+          d_lo = base + x;
+          d_hi = base + x + 4;
+          if (x & 1) f = 0.0625f;
+        } else {
+          const int wi = v / 2, x = v % 2;
+          const int base = grp * GS + t * (GS / 4) + 4 * wi;
+          d_lo = base + 2 * x;
+          d_hi = base + 2 * x + 1;
+        }
+        qbf[kk][nt][w2] = pack_h2(qrow[d_lo] * f, qrow[d_hi] * f);
+      }
+    }
+  }
+  float qs_r[NT][G::NG][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int grp = 0; grp < G::NG; grp++)
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) qs_r[nt][grp][hh] = qsum[(nt * 8 + 2 * t + hh) * G::NG + grp];
+
+  // Key-index limits of this lane's query columns (inclusive bounds).
+  int klo[NT][2], khi[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      const int qr = qr0 + nt * 8 + 2 * t + hh;
+      int a = 0, z = Nb - 1;
+      if (p.mask_mode == 1 && qr < qrows) {
+        const int pos = Nb - L + qr / nrep;
+        z = min(z, pos);
+        if (p.window > 0) a = max(0, pos - p.window + 1);
+      }
+      klo[nt][hh] = a;
+      khi[nt][hh] = z;
+    }
+
+  float m_run[NT][2], l_run[NT][2], pb[NT][G::NG][2];
+  float o_acc[G::MT][NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      m_run[nt][hh] = kNeg;
+      l_run[nt][hh] = 0.0f;
+#pragma unroll
+      for (int grp = 0; grp < G::NG; grp++) pb[nt][grp][hh] = 0.0f;
+    }
+#pragma unroll
+  for (int mt = 0; mt < G::MT; mt++)
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) o_acc[mt][nt][c] = 0.0f;
+
+  bool hung = false;
+  for (int i = 0; i < my_tiles; i++) {
+    const int s = i % STAGES;
+    // The decision must be warp-uniform: the loop body is full of warp-collective ops.
+    if (!__all_sync(0xffffffffu, mbar_wait(&wbar[s], (uint32_t)((i / STAGES) & 1)))) {
+      hung = true;
+      break;
+    }
+    const uint8_t* st = wst + s * G::STAGE;
+    const int row0 = n0 + (warp + i * W) * kTile;
+
+    // ---------------- scores ----------------
+    float sc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) sc[nt][c] = 0.0f;
+    const uint16_t* ksc = reinterpret_cast<const uint16_t*>(st + G::O_KS);
+    const uint16_t* kbi = reinterpret_cast<const uint16_t*>(st + G::O_KB);
+#pragma unroll
+    for (int grp = 0; grp < G::NG; grp++) {
+      uint32_t kw0[G::KW], kw1[G::KW];
+      lds_words<G::KB>(kw0, st + G::O_KP + g * G::KRB + grp * G::GB + t * G::KB);
+      lds_words<G::KB>(kw1, st + G::O_KP + (g + 8) * G::KRB + grp * G::GB + t * G::KB);
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) acc[nt][c] = 0.0f;
+#pragma unroll
+      for (int kin = 0; kin < G::MTG; kin++) {
+        uint32_t a[4];
+#pragma unroll
+        for (int w2 = 0; w2 < 2; w2++) {
+          const int v = 2 * kin + w2;
+          const int wi = BITS == 4 ? v / 4 : v / 2;
+          const int x = BITS == 4 ? v % 4 : v % 2;
+          a[2 * w2] = k_extract<BITS>(kw0[wi], x);
+          a[2 * w2 + 1] = k_extract<BITS>(kw1[wi], x);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+          mma16816(acc[nt], a, qbf[grp * G::MTG + kin][nt][0], qbf[grp * G::MTG + kin][nt][1]);
+      }
+      const float s0 = dt_to_f(ksc[g * G::NG + grp], bf), b0 = dt_to_f(kbi[g * G::NG + grp], bf);
+      const float s1 = dt_to_f(ksc[(g + 8) * G::NG + grp], bf),
+                  b1 = dt_to_f(kbi[(g + 8) * G::NG + grp], bf);
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        sc[nt][0] += s0 * acc[nt][0] + b0 * qs_r[nt][grp][0];
+        sc[nt][1] += s0 * acc[nt][1] + b0 * qs_r[nt][grp][1];
+        sc[nt][2] += s1 * acc[nt][2] + b1 * qs_r[nt][grp][0];
+        sc[nt][3] += s1 * acc[nt][3] + b1 * qs_r[nt][grp][1];
+      }
+    }
+
+    // ---------------- online softmax ----------------
+    const int r_lo = row0 + g, r_hi = row0 + g + 8;
+    float pr[NT][4];
+    bool rescale = false;
+    float alpha[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        const bool v0 = r_lo < n1 && r_lo >= klo[nt][hh] && r_lo <= khi[nt][hh];
+        const bool v1 = r_hi < n1 && r_hi >= klo[nt][hh] && r_hi <= khi[nt][hh];
+        const float x0 = v0 ? round_dt(sc[nt][hh], bf) : kNeg;
+        const float x1 = v1 ? round_dt(sc[nt][2 + hh], bf) : kNeg;
+        if (p.scores) {
+          const int qr = qr0 + nt * 8 + 2 * t + hh;
+          if (qr < qrows) {
+            const int l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
+            float* srow = p.scores + (((int64_t)b * p.Hq + hq) * L + l) * p.N;
+            if (v0) srow[r_lo] = x0;
+            if (v1) srow[r_hi] = x1;
+          }
+        }
+        float tm = fmaxf(x0, x1);
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
+        const float mn = fmaxf(m_run[nt][hh], tm);
+        const float al = exp2f((m_run[nt][hh] - mn) * kLog2e);
+        rescale |= (mn != m_run[nt][hh]);
+        alpha[nt][hh] = al;
+        const float q0 = v0 ? exp2f((x0 - mn) * kLog2e) : 0.0f;
+        const float q1 = v1 ? exp2f((x1 - mn) * kLog2e) : 0.0f;
+        pr[nt][hh] = q0;
+        pr[nt][2 + hh] = q1;
+        l_run[nt][hh] = l_run[nt][hh] * al + q0 + q1;
+        m_run[nt][hh] = mn;
+      }
+    }
+    if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+        for (int mt = 0; mt < G::MT; mt++) {
+          o_acc[mt][nt][0] *= alpha[nt][0];
+          o_acc[mt][nt][1] *= alpha[nt][1];
+          o_acc[mt][nt][2] *= alpha[nt][0];
+          o_acc[mt][nt][3] *= alpha[nt][1];
+        }
+#pragma unroll
+        for (int grp = 0; grp < G::NG; grp++) {
+          pb[nt][grp][0] *= alpha[nt][0];
+          pb[nt][grp][1] *= alpha[nt][1];
+        }
+      }
+    }
+
+    // ---------------- P V ----------------
+    const uint16_t* vsc = reinterpret_cast<const uint16_t*>(st + G::O_VS);
+    const uint16_t* vbi = reinterpret_cast<const uint16_t*>(st + G::O_VB);
+#pragma unroll
+    for (int grp = 0; grp < G::NG; grp++) {
+      const float vs0 = dt_to_f(vsc[g * G::NG + grp], bf), vb0 = dt_to_f(vbi[g * G::NG + grp], bf);
+      const float vs1 = dt_to_f(vsc[(g + 8) * G::NG + grp], bf),
+                  vb1 = dt_to_f(vbi[(g + 8) * G::NG + grp], bf);
+      uint32_t bfr[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        // p == 0 for masked rows: select, never multiply stale scales.
+        const float p0 = pr[nt][0], p1 = pr[nt][1], p2 = pr[nt][2], p3 = pr[nt][3];
+        pb[nt][grp][0] += (p0 != 0.0f ? p0 * vb0 : 0.0f) + (p2 != 0.0f ? p2 * vb1 : 0.0f);
+        pb[nt][grp][1] += (p1 != 0.0f ? p1 * vb0 : 0.0f) + (p3 != 0.0f ? p3 * vb1 : 0.0f);
+        const uint32_t r0 = pack_h2(p0 != 0.0f ? p0 * vs0 : 0.0f, p1 != 0.0f ? p1 * vs0 : 0.0f);
+        const uint32_t r1 = pack_h2(p2 != 0.0f ? p2 * vs1 : 0.0f, p3 != 0.0f ? p3 * vs1 : 0.0f);
+        bfr[nt][0] = movmatrix_t(r0);
+        bfr[nt][1] = movmatrix_t(r1);
+      }
+      uint32_t vw[4][G::VW];
+      lds_words<G::VB>(vw[0], st + G::O_VP + (2 * t) * G::KRB + grp * G::GB + g * G::VB);
+      lds_words<G::VB>(vw[1], st + G::O_VP + (2 * t + 1) * G::KRB + grp * G::GB + g * G::VB);
+      lds_words<G::VB>(vw[2], st + G::O_VP + (2 * t + 8) * G::KRB + grp * G::GB + g * G::VB);
+      lds_words<G::VB>(vw[3], st + G::O_VP + (2 * t + 9) * G::KRB + grp * G::GB + g * G::VB);
+      uint32_t af[G::MTG][4];
+#pragma unroll
+      for (int c = 0; c < G::C; c++) {
+        const uint32_t sel = (c & 1) ? 0x7632u : 0x5410u;
+        const uint32_t Tlo = prmt(vw[0][c / 2], vw[1][c / 2], sel);
+        const uint32_t Thi = prmt(vw[2][c / 2], vw[3][c / 2], sel);
+#pragma unroll
+        for (int j = 0; j < G::E; j++) {
+          const int sl = c * G::E + j;
+          const int mt = sl % G::MTG, half = sl / G::MTG;
+          af[mt][half] = v_extract<BITS>(Tlo, j);       // a0 (m-row g) / a1 (m-row g+8)
+          af[mt][2 + half] = v_extract<BITS>(Thi, j);   // a2 / a3
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < G::MTG; mt++)
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+          mma16816(o_acc[grp * G::MTG + mt][nt], af[mt], bfr[nt][0], bfr[nt][1]);
+    }
+    __syncwarp();
+    if (lane == 0 && i + STAGES < my_tiles) issue(i + STAGES);
+  }
+  if (hung && lane == 0) atomicExch(p.err, 1);
+
+  // ---- finish the warp: reduce row-lane partials, fold bias sums ----
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      float l = l_run[nt][hh];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      l_run[nt][hh] = l;
+#pragma unroll
+      for (int grp = 0; grp < G::NG; grp++) {
+        float v = pb[nt][grp][hh];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        pb[nt][grp][hh] = v;
+      }
+    }
+  __syncthreads();  // all warps done with their stages: reuse as merge buffer
+  float* wo = mrg + warp * HQ * (D + 2);  // [HQ][D] then m[HQ], l[HQ]
+#pragma unroll
+  for (int mtg = 0; mtg < G::MT; mtg++) {
+    const int grp = mtg / G::MTG, mt = mtg % G::MTG;
+    const float fac = (BITS == 4 && (mt & 1)) ? 0.0625f : 1.0f;
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+      const int sl = half * G::MTG + mt;
+      const int c = sl / G::E, j = sl % G::E;
+      const int d = grp * GS + (g * G::C + c) * G::E + j;
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++)
+          wo[(nt * 8 + 2 * t + hh) * D + d] =
+              o_acc[mtg][nt][half * 2 + hh] * fac + pb[nt][grp][hh];
+    }
+  }
+  if (g == 0) {
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        wo[HQ * D + nt * 8 + 2 * t + hh] = m_run[nt][hh];
+        wo[HQ * D + HQ + nt * 8 + 2 * t + hh] = l_run[nt][hh];
+      }
+  }
+  __syncthreads();
+
+  // ---- combine warps; write the CTA partial or the final result ----
+  const int rows_here = min(HQ, qrows - qr0);
+  const int64_t cta = ((int64_t)b * p.Hkv + kvh) * p.QB + qb;
+  const bool single = nact == 1;
+  for (int i = tid; i < rows_here * D; i += W * 32) {
+    const int r = i / D, d = i - r * D;
+    float M = kNeg;
+#pragma unroll
+    for (int w = 0; w < W; w++) M = fmaxf(M, mrg[w * HQ * (D + 2) + HQ * D + r]);
+    float Lsum = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < W; w++) {
+      const float* ww = mrg + w * HQ * (D + 2);
+      const float e = exp2f((ww[HQ * D + r] - M) * kLog2e);
+      Lsum += ww[HQ * D + HQ + r] * e;
+      O += ww[r * D + d] * e;
+    }
+    const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
+    const int64_t orow = ((int64_t)b * p.Hq + hq) * L + l;
+    if (single) {
+      if (p.mode == 0) {
+        p.out[orow * D + d] = f_to_dt(Lsum > 0.0f ? O / Lsum : 0.0f, bf);
+      } else {
+        p.po[orow * D + d] = O;
+        if (d == 0) {
+          p.pm[orow] = M;
+          p.pl[orow] = Lsum;
+        }
+      }
+    } else {
+      const int64_t slot = (cta * p.nsplit + split) * HQ + r;
+      p.ws_o[slot * D + d] = O;
+      if (d == 0) {
+        p.ws_ml[slot * 2] = M;
+        p.ws_ml[slot * 2 + 1] = Lsum;
+      }
+    }
+  }
+  if (single) return;
+
+  // ---- last CTA of this (b, kv head, query block) merges the splits ----
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&p.counters[cta], 1u);
+    ctrl[0] = (prev == (unsigned)(nact - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!ctrl[0]) return;
+  __threadfence();
+  for (int i = tid; i < rows_here * D; i += W * 32) {
+    const int r = i / D, d = i - r * D;
+    float M = kNeg;
+    for (int sp = 0; sp < nact; sp++)
+      M = fmaxf(M, __ldcg(&p.ws_ml[((cta * p.nsplit + sp) * HQ + r) * 2]));
+    float Lsum = 0.0f, O = 0.0f;
+    for (int sp = 0; sp < nact; sp++) {
+      const int64_t slot = (cta * p.nsplit + sp) * HQ + r;
+      const float e = exp2f((__ldcg(&p.ws_ml[slot * 2]) - M) * kLog2e);
+      Lsum += __ldcg(&p.ws_ml[slot * 2 + 1]) * e;
+      O += __ldcg(&p.ws_o[slot * D + d]) * e;
+    }
+    const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
+    const int64_t orow = ((int64_t)b * p.Hq + hq) * L + l;
+    if (p.mode == 0) {
+      p.out[orow * D + d] = f_to_dt(Lsum > 0.0f ? O / Lsum : 0.0f, bf);
+    } else {
+      p.po[orow * D + d] = O;
+      if (d == 0) {
+        p.pm[orow] = M;
+        p.pl[orow] = Lsum;
+      }
+    }
+  }
+  if (tid == 0) p.counters[cta] = 0u;  // leave the ticket ready for the next call
+}
+
+// Merge of per-device partials (context split).
+__global__ void merge_kernel(const float* __restrict__ m, const float* __restrict__ l,
+                             const float* __restrict__ o, int parts, int rows, int D, int bf,
+                             uint16_t* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)rows * D) return;
+  const int r = (int)(i / D), d = (int)(i - (int64_t)r * D);
+  float M = kNeg;
+  for (int pp = 0; pp < parts; pp++) M = fmaxf(M, m[(int64_t)pp * rows + r]);
+  float Ls = 0.0f, O = 0.0f;
+  for (int pp = 0; pp < parts; pp++) {
+    const float e = exp2f((m[(int64_t)pp * rows + r] - M) * kLog2e);
+    Ls += l[(int64_t)pp * rows + r] * e;
+    O += o[((int64_t)pp * rows + r) * D + d] * e;
+  }
+  out[i] = f_to_dt(Ls > 0.0f ? O / Ls : 0.0f, bf);
+}
+
+__global__ void fill_kernel(float* __restrict__ p, int64_t n, float v) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+
+// ------------------------------------------------------------ host side --
+
+constexpr int kWarps = 4;
+
+template <int BITS, int D, int GS>
+constexpr int stages_for() {
+  return Geo<BITS, D, GS>::STAGE <= 4096 ? 4 : (Geo<BITS, D, GS>::STAGE <= 8192 ? 3 : 2);
+}
+
+struct LaunchShape {
+  int QB, nsplit, rps;
+};
+
+int g_num_sms[64] = {0};
+
+int num_sms(int dev) {
+  if (dev < 0 || dev >= 64) return 148;
+  if (!g_num_sms[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    g_num_sms[dev] = v;
+  }
+  return g_num_sms[dev];
+}
+
+LaunchShape shape_for(int B, int Hkv, int nrep, int L, int N, int NT, int sms) {
+  LaunchShape s;
+  const int HQ = 8 * NT;
+  s.QB = (nrep * L + HQ - 1) / HQ;
+  const int64_t units = (int64_t)B * Hkv * s.QB;
+  const int64_t target = (int64_t)sms * 8;  // ~2 waves of 4 resident CTAs per SM
+  int nsplit = (int)std::max<int64_t>(1, (target + units - 1) / units);
+  const int min_rows = kTile * kWarps * 2;
+  nsplit = std::min(nsplit, std::max(1, (N + min_rows - 1) / min_rows));
+  int rps = (N + nsplit - 1) / nsplit;
+  rps = (rps + kTile * kWarps - 1) / (kTile * kWarps) * (kTile * kWarps);
+  if (rps <= 0) rps = kTile * kWarps;
+  s.rps = rps;
+  s.nsplit = std::max(1, (N + rps - 1) / rps);
+  return s;
+}
+
+size_t ws_bytes_for(int B, int Hkv, const LaunchShape& s, int NT, int D) {
+  if (s.nsplit <= 1) return 256;  // only the error flag
+  const size_t slots = (size_t)B * Hkv * s.QB * s.nsplit * 8 * NT;
+  size_t bytes = 256;                                   // error flag + pad
+  bytes += ((size_t)B * Hkv * s.QB * 4 + 255) / 256 * 256;  // counters
+  bytes += (slots * 2 * 4 + 255) / 256 * 256;               // (m, l)
+  bytes += slots * D * 4;                                   // o
+  return bytes;
+}
+
+template <int BITS, int D, int GS, int NT>
+int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st) {
+  constexpr int ST = stages_for<BITS, D, GS>();
+  using SM = Smem<BITS, D, GS, NT, kWarps, ST>;
+  auto kern = attn_kernel<BITS, D, GS, NT, kWarps, ST>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  KVQ_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    KVQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL));
+    configured[dev] = true;
+  }
+  const dim3 grid(s.nsplit, p.Hkv * s.QB, B);
+  kern<<<grid, kWarps * 32, SM::TOTAL, st>>>(p);
+  KVQ_CUDA_TRY(cudaGetLastError());
+  return KVQ_OK;
+}
+
+template <int BITS, int D, int GS>
+int32_t pick_nt(Params& p, const LaunchShape& s, int NT, int B, cudaStream_t st) {
+  if (NT == 1) return launch_t<BITS, D, GS, 1>(p, s, B, st);
+  return launch_t<BITS, D, GS, 2>(p, s, B, st);
+}
+
+template <int BITS, int D>
+int32_t pick_gs(Params& p, const LaunchShape& s, int GSv, int NT, int B, cudaStream_t st) {
+  switch (GSv) {
+    case 32: return pick_nt<BITS, D, 32>(p, s, NT, B, st);
+    case 64: return pick_nt<BITS, D, 64>(p, s, NT, B, st);
+    case 128:
+      if constexpr (D >= 128) return pick_nt<BITS, D, 128>(p, s, NT, B, st);
+      break;
+  }
+  return fail(KVQ_ERR_ARG, "attention: unsupported group_size for this head_dim");
+}
+
+template <int BITS>
+int32_t pick_d(Params& p, const LaunchShape& s, int Dv, int GSv, int NT, int B, cudaStream_t st) {
+  switch (Dv) {
+    case 64: return pick_gs<BITS, 64>(p, s, GSv, NT, B, st);
+    case 128: return pick_gs<BITS, 128>(p, s, GSv, NT, B, st);
+    case 256: return pick_gs<BITS, 256>(p, s, GSv, NT, B, st);
+  }
+  return fail(KVQ_ERR_ARG, "attention: head_dim must be 64, 128 or 256");
+}
+
+// Validate and fill Params common to every attention launch.
+int32_t prepare(const AttnArgs& a, int L, int mask_mode, int window, Params& p, int& NT) {
+  if (a.Hkv <= 0 || a.Hq <= 0 || a.Hq % a.Hkv) return fail(KVQ_ERR_ARG, "q_heads must be a multiple of kv heads");
+  const int nrep = a.Hq / a.Hkv;
+  NT = nrep * L <= 8 ? 1 : 2;
+  if (L == 1 && nrep > 16) return fail(KVQ_ERR_ARG, "decode: more than 16 query heads per kv head");
+  if (a.bits != 4 && a.bits != 8) return fail(KVQ_ERR_ARG, "bits must be 4 or 8");
+  if (a.gs != 32 && a.gs != 64 && a.gs != 128) return fail(KVQ_ERR_ARG, "group_size must be 32, 64 or 128");
+  if (a.D % a.gs) return fail(KVQ_ERR_ARG, "head_dim must be a multiple of group_size");
+  if (a.dtype != KVQ_DTYPE_FLOAT16 && a.dtype != KVQ_DTYPE_BFLOAT16) return fail(KVQ_ERR_ARG, "dtype must be float16 or bfloat16");
+  // TMA bulk copies read whole 16-row tiles: row strides must keep every tile
+  // 16-byte aligned and inside its head's rows.
+  const int64_t strides[4] = {a.k.batch_stride, a.k.head_stride, a.v.batch_stride, a.v.head_stride};
+  for (int i = 0; i < 4; i++)
+    if (strides[i] % kTile) return fail(KVQ_ERR_ARG, "view row strides must be multiples of 16 rows");
+  const uintptr_t ptrs[6] = {(uintptr_t)a.k.packed, (uintptr_t)a.k.scales, (uintptr_t)a.k.biases,
+                             (uintptr_t)a.v.packed, (uintptr_t)a.v.scales, (uintptr_t)a.v.biases};
+  for (int i = 0; i < 6; i++)
+    if (ptrs[i] % 16) return fail(KVQ_ERR_ARG, "view base pointers must be 16-byte aligned");
+  if (a.N > 0) {
+    // The last tile is read whole: the rows up to the next multiple of 16
+    // must exist.  Views from a kvq_cache always satisfy this.
+    const int64_t need = (int64_t)(a.N + kTile - 1) / kTile * kTile;
+    if (need > a.k.head_stride || need > a.v.head_stride)
+      return fail(KVQ_ERR_ARG, "view head_stride must cover len rounded up to 16 rows");
+  }
+  p = Params{};
+  p.kp = reinterpret_cast<const uint8_t*>(a.k.packed);
+  p.ks = a.k.scales;
+  p.kb = a.k.biases;
+  p.vp = reinterpret_cast<const uint8_t*>(a.v.packed);
+  p.vs = a.v.scales;
+  p.vb = a.v.biases;
+  p.k_bstride = a.k.batch_stride;
+  p.k_hstride = a.k.head_stride;
+  p.v_bstride = a.v.batch_stride;
+  p.v_hstride = a.v.head_stride;
+  p.q = static_cast<const uint16_t*>(a.q);
+  p.seq_lens = a.seq_lens;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.nrep = nrep;
+  p.N = a.N;
+  p.L = L;
+  p.mask_mode = mask_mode;
+  p.window = window;
+  p.scale = a.scale;
+  p.bf16 = a.dtype == KVQ_DTYPE_BFLOAT16;
+  return KVQ_OK;
+}
+
+int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void* out, float* pm,
+            float* pl, float* po, void* ws, size_t ws_bytes, cudaStream_t st,
+            float* scores = nullptr) {
+  Params p;
+  int NT = 1;
+  int32_t rc = prepare(a, L, mask_mode, window, p, NT);
+  if (rc) return rc;
+  if (a.B == 0 || a.Hq == 0) return KVQ_OK;
+  int dev = 0;
+  KVQ_CUDA_TRY(cudaGetDevice(&dev));
+  const LaunchShape s = shape_for(a.B, a.Hkv, p.nrep, L, std::max(a.N, 1), NT, num_sms(dev));
+  const size_t need = ws_bytes_for(a.B, a.Hkv, s, NT, a.D);
+  if (!ws) {
+    ws = managed_workspace(dev, need, st, &rc);
+    if (rc) return rc;
+  } else if (ws_bytes < need) {
+    return fail(KVQ_ERR_WORKSPACE, "workspace smaller than kvq_sdpa_decode_workspace()");
+  }
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  p.err = reinterpret_cast<int*>(w);
+  if (s.nsplit > 1) {
+    const size_t slots = (size_t)a.B * a.Hkv * s.QB * s.nsplit * 8 * NT;
+    size_t off = 256;
+    p.counters = reinterpret_cast<unsigned*>(w + off);
+    off += ((size_t)a.B * a.Hkv * s.QB * 4 + 255) / 256 * 256;
+    p.ws_ml = reinterpret_cast<float*>(w + off);
+    off += (slots * 2 * 4 + 255) / 256 * 256;
+    p.ws_o = reinterpret_cast<float*>(w + off);
+  }
+  p.QB = s.QB;
+  p.rps = s.rps;
+  p.nsplit = s.nsplit;
+  p.mode = mode;
+  p.out = static_cast<uint16_t*>(out);
+  p.pm = pm;
+  p.pl = pl;
+  p.po = po;
+  p.scores = scores;
+  if (a.bits == 4) return pick_d<4>(p, s, a.D, a.gs, NT, a.B, st);
+  return pick_d<8>(p, s, a.D, a.gs, NT, a.B, st);
+}
+
+}  // namespace
+
+size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D) {
+  if (Hkv <= 0 || Hq % Hkv) return 0;
+  const int nrep = Hq / Hkv;
+  const int NT = nrep <= 8 ? 1 : 2;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const LaunchShape s = shape_for(B, Hkv, nrep, 1, std::max(N, 1), NT, num_sms(dev));
+  return ws_bytes_for(B, Hkv, s, NT, D);
+}
+
+int32_t launch_decode(const AttnArgs& a, void* out, float* pm, float* pl, float* po, void* ws,
+                      size_t ws_bytes, cudaStream_t st) {
+  return run(a, 1, 0, 0, out ? 0 : 1, out, pm, pl, po, ws, ws_bytes, st);
+}
+
+int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void* out, void* ws,
+                       size_t ws_bytes, cudaStream_t st) {
+  if (L <= 0) return fail(KVQ_ERR_ARG, "prefill: L must be positive");
+  if (L > a.N) return fail(KVQ_ERR_ARG, "prefill: L exceeds the key length");
+  return run(a, L, mask_mode, window, 0, out, nullptr, nullptr, nullptr, ws, ws_bytes, st);
+}
+
+int32_t launch_merge(const float* m, const float* l, const float* o, int parts, int rows, int D,
+                     int dtype, void* out, cudaStream_t st) {
+  const int64_t n = (int64_t)rows * D;
+  if (n == 0) return KVQ_OK;
+  merge_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+      m, l, o, parts, rows, D, dtype == KVQ_DTYPE_BFLOAT16, static_cast<uint16_t*>(out));
+  KVQ_CUDA_TRY(cudaGetLastError());
+  return KVQ_OK;
+}
+
+int32_t launch_debug_scores(const AttnArgs& a, int L, int mask_mode, int window, float* scores,
+                            cudaStream_t st) {
+  if (L <= 0 || L > a.N) return fail(KVQ_ERR_ARG, "debug scores: bad L");
+  const int64_t n = (int64_t)a.B * a.Hq * L * a.N;
+  if (n == 0) return KVQ_OK;
+  fill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(scores, n, -INFINITY);
+  KVQ_CUDA_TRY(cudaGetLastError());
+  void* tmp = nullptr;
+  const size_t ob = (size_t)a.B * a.Hq * L * a.D * 2;
+  KVQ_CUDA_TRY(cudaMallocAsync(&tmp, ob, st));
+  const int32_t rc = run(a, L, mask_mode, window, 0, tmp, nullptr, nullptr, nullptr, nullptr, 0,
+                         st, scores);
+  cudaError_t e = cudaFreeAsync(tmp, st);
+  if (rc) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync");
+  return KVQ_OK;
+}
+
+}  // namespace kvq

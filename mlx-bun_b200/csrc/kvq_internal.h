@@ -1,0 +1,72 @@
+// kvq_internal.h — shared declarations of libkvq's CUDA translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "kvq.h"
+
+namespace kvq {
+
+// Thread-local error text behind kvq_last_error().
+void set_error(const std::string& msg);
+int32_t fail(int32_t code, const std::string& msg);
+int32_t cuda_fail(cudaError_t e, const char* what);
+
+#define KVQ_CUDA_TRY(expr)                                  \
+  do {                                                      \
+    cudaError_t _e = (expr);                                \
+    if (_e != cudaSuccess) return ::kvq::cuda_fail(_e, #expr); \
+  } while (0)
+
+// Geometry of one quantized row.
+struct RowGeom {
+  int D, bits, gs;
+  int words() const { return D * bits / 32; }       // uint32 per packed row
+  int groups() const { return D / gs; }              // scales (and biases) per row
+};
+
+// Base pointers + row strides of one triple (device side view).
+struct TripleView {
+  uint32_t* packed;
+  uint16_t* scales;
+  uint16_t* biases;
+  int64_t batch_stride;  // rows
+  int64_t head_stride;   // rows
+};
+
+// ---- quantize kernels (kvq_quant.cu) ----
+// Quantize rows of logical shape [B, H, S, D] (element strides in[4], d stride
+// 1) into rows dst_row0 + s of the destination triple.
+int32_t launch_append(const void* x, const int64_t* strides, int B, int H, int S, RowGeom g,
+                      int dtype, TripleView dst, int64_t dst_row0, cudaStream_t st);
+// Contiguous rows -> contiguous triple.
+int32_t launch_quantize_rows(const void* x, int64_t rows, RowGeom g, int dtype, uint32_t* packed,
+                             uint16_t* scales, uint16_t* biases, cudaStream_t st);
+
+// ---- attention (kvq_decode.cu / kvq_prefill.cu) ----
+struct AttnArgs {
+  TripleView k, v;
+  int B, Hkv, Hq, N, D, bits, gs, dtype;
+  float scale;
+  const void* q;
+  const int32_t* seq_lens;  // device, nullable
+};
+
+size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D);
+// mode 0: normalized output in `out` (dtype); mode 1: partials (m, l, o).
+int32_t launch_decode(const AttnArgs& a, void* out, float* pm, float* pl, float* po, void* ws,
+                      size_t ws_bytes, cudaStream_t st);
+int32_t launch_merge(const float* m, const float* l, const float* o, int parts, int rows, int D,
+                     int dtype, void* out, cudaStream_t st);
+int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void* out, void* ws,
+                       size_t ws_bytes, cudaStream_t st);
+int32_t launch_debug_scores(const AttnArgs& a, int L, int mask_mode, int window, float* scores,
+                            cudaStream_t st);
+
+// Library-managed scratch per device (grown on demand, zero-filled).
+void* managed_workspace(int device, size_t bytes, cudaStream_t st, int32_t* status);
+
+}  // namespace kvq

@@ -1,0 +1,344 @@
+"""CPU oracle for the quantized-KV attention path (TEST INFRASTRUCTURE ONLY).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
+may import this module, and only as the checker or the timed CPU baseline.
+The product path (``mlx-bun_b200/kvq``) never imports it.
+
+Two parts:
+
+* ctypes bindings over ``kvq_oracle.c`` (quantize rule, packing, the unfused
+  op graph ``quantizedSdpaUnfused`` with its dtype rounding points);
+* a numpy restatement of the two quantized cache state machines of mlx-bun,
+  line by line from ``src/model/gemma4-base.ts``:
+    - ``QuantizedKVCache``        (:419-598)   growing, 256-row steps
+    - ``RotatingQuantizedKVCache`` (:932-1261) sliding-window ring, keep=0
+
+The oracle's quantize rule is pinned bit-exactly by
+``tests/golden/rotating_kvq_mechanics.npz`` (bf16, gs 32, 8 bit), which was
+extracted from mlx-bun's ``goldens/rotating-kvq.bin``.  fp16 inputs, gs 64,
+4-bit codes and all SDPA outputs are pinned against this restatement only
+(MLX itself cannot run here).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+F16 = 9
+BF16 = 12
+STEP = 256
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        from . import build as _build  # noqa: F401  (package-relative when imported as oracle.oracle)
+        path = _build.build()
+        _lib = ctypes.CDLL(path)
+        u16p = ctypes.POINTER(ctypes.c_uint16)
+        u32p = ctypes.POINTER(ctypes.c_uint32)
+        f32p = ctypes.POINTER(ctypes.c_float)
+        _lib.kvqo_quantize_rows.argtypes = [u16p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_int, u32p, u16p, u16p]
+        _lib.kvqo_dequantize_rows.argtypes = [u32p, u16p, u16p, ctypes.c_int64, ctypes.c_int,
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int, f32p]
+        _lib.kvqo_sdpa_unfused.argtypes = [u16p, ctypes.c_void_p, ctypes.c_void_p] + \
+            [ctypes.c_int] * 10 + [ctypes.c_float, ctypes.c_int, ctypes.c_int,
+                                   ctypes.POINTER(ctypes.c_int32), u16p, f32p, ctypes.c_int]
+        _lib.kvqo_sdpa_unfused.restype = ctypes.c_int
+        _lib.kvqo_max_threads.restype = ctypes.c_int
+    return _lib
+
+
+class _View(ctypes.Structure):
+    _fields_ = [("packed", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+                ("biases", ctypes.c_void_p), ("batch_stride", ctypes.c_int64),
+                ("head_stride", ctypes.c_int64)]
+
+
+def _p(a, t):
+    return a.ctypes.data_as(ctypes.POINTER(t))
+
+
+# ---------------------------------------------------------------- dtypes ---
+
+def to_dtype_bits(x: np.ndarray, dtype: int) -> np.ndarray:
+    """f32 array -> uint16 bit patterns of fp16 (RNE) or bf16 (RNE)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if dtype == F16:
+        return x.astype(np.float16).view(np.uint16)
+    u = x.view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return r.astype(np.uint16)
+
+
+def from_dtype_bits(h: np.ndarray, dtype: int) -> np.ndarray:
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    if dtype == F16:
+        return h.view(np.float16).astype(np.float32)
+    return (h.astype(np.uint32) << 16).view(np.float32)
+
+
+# -------------------------------------------------------------- quantize ---
+
+def quantize(x_bits: np.ndarray, group_size: int, bits: int, dtype: int):
+    """MLX affine quantize of the last axis (ops.ts:615-637).
+
+    x_bits: uint16 dtype bit patterns [..., D].  Returns (packed u32
+    [..., D*bits/32], scales u16 [..., D/gs], biases u16 [..., D/gs]).
+    """
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    D = x.shape[-1]
+    rows = int(np.prod(x.shape[:-1])) if x.ndim > 1 else 1
+    packed = np.zeros(x.shape[:-1] + (D * bits // 32,), np.uint32)
+    scales = np.zeros(x.shape[:-1] + (D // group_size,), np.uint16)
+    biases = np.zeros_like(scales)
+    if rows:
+        lib().kvqo_quantize_rows(_p(x, ctypes.c_uint16), rows, D, group_size, bits, dtype,
+                                 _p(packed, ctypes.c_uint32), _p(scales, ctypes.c_uint16),
+                                 _p(biases, ctypes.c_uint16))
+    return packed, scales, biases
+
+
+def dequantize(packed, scales, biases, group_size: int, bits: int, dtype: int) -> np.ndarray:
+    packed = np.ascontiguousarray(packed, dtype=np.uint32)
+    scales = np.ascontiguousarray(scales, dtype=np.uint16)
+    biases = np.ascontiguousarray(biases, dtype=np.uint16)
+    D = packed.shape[-1] * 32 // bits
+    rows = int(np.prod(packed.shape[:-1]))
+    out = np.zeros(packed.shape[:-1] + (D,), np.float32)
+    if rows:
+        lib().kvqo_dequantize_rows(_p(packed, ctypes.c_uint32), _p(scales, ctypes.c_uint16),
+                                   _p(biases, ctypes.c_uint16), rows, D, group_size, bits, dtype,
+                                   _p(out, ctypes.c_float))
+    return out
+
+
+# ---------------------------------------------------------- unfused SDPA ---
+
+def sdpa_unfused(q_bits, kq, vq, scale: float, group_size: int, bits: int, dtype: int,
+                 mask_mode: int = 0, window: int = 0, seq_lens=None, want_scores=False,
+                 threads: int = 0):
+    """quantizedSdpaUnfused (gemma4-base.ts:1273-1342) on contiguous triples.
+
+    q_bits [B, Hq, L, D] uint16; kq / vq = (packed [B,Hkv,N,*], scales, biases).
+    Returns out bits [B, Hq, L, D] (and f32 masked logits [B, Hq, L, N]).
+    """
+    q = np.ascontiguousarray(q_bits, dtype=np.uint16)
+    B, Hq, L, D = q.shape
+    kp, ks, kb = (np.ascontiguousarray(a) for a in kq)
+    vp, vs, vb = (np.ascontiguousarray(a) for a in vq)
+    Hkv, N = kp.shape[1], kp.shape[2]
+    kv = _View(kp.ctypes.data, ks.ctypes.data, kb.ctypes.data, Hkv * N, N)
+    vv = _View(vp.ctypes.data, vs.ctypes.data, vb.ctypes.data, Hkv * N, N)
+    out = np.zeros((B, Hq, L, D), np.uint16)
+    scores = np.full((B, Hq, L, N), np.nan, np.float32) if want_scores else None
+    sl = None
+    if seq_lens is not None:
+        sl = np.ascontiguousarray(seq_lens, dtype=np.int32)
+    rc = lib().kvqo_sdpa_unfused(
+        _p(q, ctypes.c_uint16), ctypes.byref(kv), ctypes.byref(vv), B, Hq, Hkv, L, N, D,
+        group_size, bits, dtype, ctypes.c_float(scale), mask_mode, window,
+        _p(sl, ctypes.c_int32) if sl is not None else None, _p(out, ctypes.c_uint16),
+        _p(scores, ctypes.c_float) if scores is not None else None, threads)
+    if rc != 0:
+        raise ValueError("oracle sdpa: bad arguments")
+    return (out, scores) if want_scores else out
+
+
+def max_threads() -> int:
+    return lib().kvqo_max_threads()
+
+
+# ------------------------------------------------------ cache mechanics ---
+
+def _zeros(B, H, T, dim, dt):
+    return np.zeros((B, H, T, dim), dt)
+
+
+def _triple_zeros(B, H, T, D, group_size, bits):
+    return [_zeros(B, H, T, D * bits // 32, np.uint32), _zeros(B, H, T, D // group_size, np.uint16),
+            _zeros(B, H, T, D // group_size, np.uint16)]
+
+
+def _cat(a, b):
+    return np.concatenate([a, b], axis=2)
+
+
+class QuantizedKVCache:
+    """Restates QuantizedKVCache (gemma4-base.ts:419-598) over numpy triples."""
+
+    def __init__(self, group_size: int, bits: int, dtype: int):
+        self.group_size, self.bits, self.dtype = group_size, bits, dtype
+        self.keys = None
+        self.values = None
+        self.offset = 0
+
+    def update_and_fetch(self, k_bits: np.ndarray, v_bits: np.ndarray):
+        """updateAndFetchQuantized (:452-507); k/v [B, H, L, D] uint16 bits."""
+        B, H, L, kD = k_bits.shape
+        vD = v_bits.shape[3]
+        prev = self.offset
+        if self.keys is None or prev + L > self.keys[0].shape[2]:
+            new_steps = ((STEP + L - 1) // STEP) * STEP
+            if self.keys is not None and prev % STEP != 0:
+                self.keys = [a[:, :, :prev] for a in self.keys]
+                self.values = [a[:, :, :prev] for a in self.values]
+            nk = _triple_zeros(B, H, new_steps, kD, self.group_size, self.bits)
+            nv = _triple_zeros(B, H, new_steps, vD, self.group_size, self.bits)
+            if self.keys is None:
+                self.keys, self.values = nk, nv
+            else:
+                self.keys = [_cat(a, z) for a, z in zip(self.keys, nk)]
+                self.values = [_cat(a, z) for a, z in zip(self.values, nv)]
+        self.offset += L
+        kq = quantize(k_bits, self.group_size, self.bits, self.dtype)
+        vq = quantize(v_bits, self.group_size, self.bits, self.dtype)
+        for dst, src in ((self.keys, kq), (self.values, vq)):
+            for a, s in zip(dst, src):
+                a[:, :, prev:self.offset] = s
+        return self.fetch()
+
+    def fetch(self):
+        return ([a[:, :, :self.offset] for a in self.keys],
+                [a[:, :, :self.offset] for a in self.values])
+
+    @property
+    def seq_len(self):
+        return 0 if self.keys is None else self.keys[0].shape[2]
+
+    def trim(self, n: int):
+        self.offset = max(0, self.offset - n)
+
+
+class RotatingQuantizedKVCache:
+    """Restates RotatingQuantizedKVCache (gemma4-base.ts:932-1261), keep=0."""
+
+    def __init__(self, max_size: int, group_size: int, bits: int, dtype: int):
+        self.max_size = max_size
+        self.group_size, self.bits, self.dtype = group_size, bits, dtype
+        self.keys = None
+        self.values = None
+        self.offset = 0
+        self.ring_idx = 0
+
+    @property
+    def seq_len(self):
+        return 0 if self.keys is None else self.keys[0].shape[2]
+
+    def _temporal_order(self, t):  # :967-985
+        S = t[0].shape[2]
+        if self.ring_idx == S:
+            return [a[:, :, :S] for a in t]
+        if self.ring_idx < self.offset:
+            return [_cat(a[:, :, self.ring_idx:S], a[:, :, :self.ring_idx]) for a in t]
+        return [a[:, :, :self.ring_idx] for a in t]
+
+    @staticmethod
+    def _trim(trim_size, t, append):  # :987-1001
+        base = [a[:, :, trim_size if trim_size > 0 else 0:] for a in t]
+        if append is None:
+            return base
+        return [_cat(a, b) for a, b in zip(base, append)]
+
+    def _update_concat(self, k, v):  # :1003-1024
+        S = k.shape[2]
+        kq = list(quantize(k, self.group_size, self.bits, self.dtype))
+        vq = list(quantize(v, self.group_size, self.bits, self.dtype))
+        if self.keys is None:
+            self.keys, self.values = kq, vq
+        else:
+            tk = self._temporal_order(self.keys)
+            tv = self._temporal_order(self.values)
+            self.ring_idx = tk[0].shape[2]
+            trim_size = self.ring_idx - self.max_size + 1
+            self.keys = self._trim(trim_size, tk, kq)
+            self.values = self._trim(trim_size, tv, vq)
+        self.offset += S
+        self.ring_idx = self.seq_len
+        return self.active_slices()
+
+    def _update_in_place(self, k, v):  # :1026-1086
+        B, H, S, D = k.shape
+        vD = v.shape[3]
+        prev = self.offset
+        if self.keys is None or (prev >= self.seq_len and self.seq_len < self.max_size):
+            new_size = min(STEP, self.max_size - prev)
+            if new_size <= 0:
+                raise ValueError("rotating cache: non-positive growth")
+            nk = _triple_zeros(B, H, new_size, D, self.group_size, self.bits)
+            nv = _triple_zeros(B, H, new_size, vD, self.group_size, self.bits)
+            if self.keys is None:
+                self.keys, self.values = nk, nv
+            else:
+                self.keys = [_cat(a, z) for a, z in zip(self.keys, nk)]
+                self.values = [_cat(a, z) for a, z in zip(self.values, nv)]
+            self.ring_idx = prev
+        trim_size = self.seq_len - self.max_size
+        if trim_size > 0:
+            self.keys = self._trim(trim_size, self.keys, None)
+            self.values = self._trim(trim_size, self.values, None)
+            self.ring_idx = self.max_size
+        if self.ring_idx == self.max_size:
+            self.ring_idx = 0
+        kq = quantize(k, self.group_size, self.bits, self.dtype)
+        vq = quantize(v, self.group_size, self.bits, self.dtype)
+        self.keys = [a.copy() for a in self.keys]
+        self.values = [a.copy() for a in self.values]
+        for dst, src in ((self.keys, kq), (self.values, vq)):
+            for a, s in zip(dst, src):
+                a[:, :, self.ring_idx:self.ring_idx + S] = s
+        self.offset += S
+        self.ring_idx += S
+        return self.active_slices()
+
+    def active_slices(self):  # :1097-1104
+        up_to = self.offset if self.offset < self.max_size else self.seq_len
+        return ([a[:, :, :up_to] for a in self.keys], [a[:, :, :up_to] for a in self.values])
+
+    def update_and_fetch(self, k_bits, v_bits):  # :1108-1110
+        if k_bits.shape[2] == 1:
+            return self._update_in_place(k_bits, v_bits)
+        return self._update_concat(k_bits, v_bits)
+
+    def is_trimmable(self):
+        return self.offset < self.max_size
+
+    def trim(self, n: int, bypass: bool = False):  # :1137-1163
+        k = min(self.offset, n)
+        if not bypass:
+            self.offset -= k
+            self.ring_idx -= k
+            return
+        self.offset -= k
+        if k > 0 and self.keys is not None:
+            S = self.seq_len
+            self.keys = [a[:, :, :S - k] for a in self.keys]
+            self.values = [a[:, :, :S - k] for a in self.values]
+            self.ring_idx = self.seq_len
+        else:
+            self.ring_idx -= k
+
+
+def make_mask(N: int, offset: int, window):
+    """Mask decision of QuantizedKVCache.makeMask (:509-519) as (mode, window):
+    mode 0 = none, 1 = bottom-right aligned causal (window 0 = unbounded)."""
+    if N == 1:
+        return 0, 0
+    return 1, (window or 0)
+
+
+def make_mask_rotating(N: int, offset: int, max_size: int, window):
+    """RotatingQuantizedKVCache.makeMask (:1113-1122) as (mode, window)."""
+    w = window if window is not None else max_size
+    if N > 1:
+        off = min(max_size - 1, offset)
+        if off + N > w:
+            return 1, w
+        return 1, 0
+    return 0, 0
