@@ -226,30 +226,26 @@ def run_gpu(args, rank, world, local_rank):
             gpu_step(layers[i % NL], scale)
     stream.synchronize()
 
-    # ---- graphs: one replay = NL steps (one pass over the layers); events
-    # around each decode launch give the kernel's own duration.
+    # ---- graphs: one replay = NL steps (one pass over the layers)
     per_graph = NL
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(per_graph)]
     graph = torch.cuda.CUDAGraph()
-    events_in_graph = True
-    try:
-        with torch.cuda.graph(graph, stream=stream):
-            for j in range(per_graph):
-                L = layers[j]
-                qk, qv = L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])
-                ev[j][0].record()
-                kvq.sdpa_decode(L["q"], qk, qv, scale, out=L["out"])
-                ev[j][1].record()
-                L["cache"].trim(1)
-    except Exception:
-        events_in_graph = False
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for j in range(per_graph):
-                gpu_step(layers[j], scale)
+    with torch.cuda.graph(graph, stream=stream):
+        for j in range(per_graph):
+            gpu_step(layers[j], scale)
+    # decode-only graph over the same layers (kernel timing for the roofline)
+    views = []
+    for L in layers:
+        L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])  # leave row 8192 written
+        views.append(L["cache"].fetch())
+    g_dec = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_dec, stream=stream):
+        for j in range(per_graph):
+            kvq.sdpa_decode(layers[j]["q"], views[j][0], views[j][1], scale, out=layers[j]["out"])
+    for L in layers:
+        L["cache"].trim(1)
     for _ in range(3):
         graph.replay()
+        g_dec.replay()
     torch.cuda.synchronize()
 
     K = args.steps
@@ -263,44 +259,27 @@ def run_gpu(args, rank, world, local_rank):
         clocks.start()
         time.sleep(0.1)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kern_ms = []
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record()
         for r in range(reps):
             graph.replay()
-            if events_in_graph and r in (0, reps // 2, reps - 1):
-                pass
         e1.record()
+        # the decode kernel alone, same layers, same stream, right after
+        e2.record()
+        for r in range(reps):
+            g_dec.replay()
+        e3.record()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop() if clocks else None
     ms = e0.elapsed_time(e1)
-    if events_in_graph:
-        kern_ms = [a.elapsed_time(b) for a, b in ev]  # durations of the last replay
+    kern_ms = [e2.elapsed_time(e3) / (reps * per_graph)]
     t = torch.tensor([ms], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-
-    # ---- kernel-only timing fallback: decode graphs alone
-    if not kern_ms:
-        g2 = torch.cuda.CUDAGraph()
-        views = [L["cache"].fetch() for L in layers]
-        with torch.cuda.graph(g2, stream=stream):
-            for j in range(per_graph):
-                kvq.sdpa_decode(layers[j]["q"], views[j][0], views[j][1], scale,
-                                out=layers[j]["out"])
-        g2.replay()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            a.record()
-            for _ in range(max(1, reps // 4)):
-                g2.replay()
-            b.record()
-        torch.cuda.synchronize()
-        kern_ms = [a.elapsed_time(b) / (max(1, reps // 4) * per_graph)]
 
     # ---- e2e through the public API with host buffers
     import kvq as _k  # noqa: F401
@@ -377,8 +356,8 @@ def run_gpu(args, rank, world, local_rank):
                          "kernel_us": round(kmean * 1e3, 3),
                          "bytes_per_launch": decode_launch_bytes(c),
                          "traffic": traffic_from_profiles(),
-                         "timing": "CUDA events around each decode launch inside the timed graphs"
-                         if events_in_graph else "decode-only graph replays"},
+                         "timing": "CUDA events around decode-only graph replays of the same "
+                                   "layers, right after the timed steps, same stream"},
             "clocks": clk,
         }
     return res

@@ -159,9 +159,10 @@ int32_t kvq_sdpa_decode_workspace(const kvq_qtensor* keys, int32_t q_heads, size
  * seq_lens: NULL, or a DEVICE int32[B] of per-sequence key counts
  *      (<= keys->len) for ragged batches.
  * workspace: NULL (library-managed, cached per device) or a device buffer of
- *      at least kvq_sdpa_decode_workspace() bytes, zero-filled before its
- *      first use; every call leaves it reusable.  Calls sharing one
- *      workspace must not overlap on the GPU. */
+ *      at least kvq_sdpa_decode_workspace() bytes whose first 256 KiB are
+ *      zero before its first use (split tickets live there; every call
+ *      leaves them zero again).  Calls sharing one workspace must not
+ *      overlap on the GPU. */
 int32_t kvq_sdpa_decode(const kvq_qtensor* keys, const kvq_qtensor* values, const void* q,
                         int32_t q_heads, float scale, const int32_t* seq_lens, void* out,
                         void* workspace, size_t workspace_bytes, void* stream);
@@ -176,12 +177,16 @@ int32_t kvq_sdpa_decode_partial(const kvq_qtensor* keys, const kvq_qtensor* valu
                                 const int32_t* seq_lens, float* m, float* l, float* o,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
-/* Merge `parts` partial sets laid out part-major (m[parts][rows],
- * l[parts][rows], o[parts][rows][D]) into out[rows][D] in dtype, in fixed
- * part order (deterministic, like the reference's merge kernel,
- * src/model/fused-decode-kernel.ts:205-222). */
+/* Merge `parts` partial sets into out[rows][D] in dtype, in fixed part
+ * order (deterministic, like the reference's merge kernel,
+ * src/model/fused-decode-kernel.ts:205-222).  Part p's values are
+ * m[p*part_stride + r], l[p*part_stride + r] and
+ * o[p*part_stride + r*head_dim + d] (part_stride in floats), so the three
+ * arrays may live inside one packed buffer per part, as gathered from all
+ * ranks of a context split. */
 int32_t kvq_sdpa_merge(const float* m, const float* l, const float* o, int32_t parts,
-                       int32_t rows, int32_t head_dim, int32_t dtype, void* out, void* stream);
+                       int64_t part_stride, int32_t rows, int32_t head_dim, int32_t dtype,
+                       void* out, void* stream);
 
 /* L > 1 attention of L new query rows per head over the cache (chunked
  * prefill; quantizedSdpaTiled, src/model/gemma4-base.ts:1356-1521, and the

@@ -713,18 +713,18 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
 
 // Merge of per-device partials (context split).
 __global__ void merge_kernel(const float* __restrict__ m, const float* __restrict__ l,
-                             const float* __restrict__ o, int parts, int rows, int D, int bf,
-                             uint16_t* __restrict__ out) {
+                             const float* __restrict__ o, int parts, int64_t ps, int rows, int D,
+                             int bf, uint16_t* __restrict__ out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)rows * D) return;
   const int r = (int)(i / D), d = (int)(i - (int64_t)r * D);
   float M = kNeg;
-  for (int pp = 0; pp < parts; pp++) M = fmaxf(M, m[(int64_t)pp * rows + r]);
+  for (int pp = 0; pp < parts; pp++) M = fmaxf(M, m[pp * ps + r]);
   float Ls = 0.0f, O = 0.0f;
   for (int pp = 0; pp < parts; pp++) {
-    const float e = exp2f((m[(int64_t)pp * rows + r] - M) * kLog2e);
-    Ls += l[(int64_t)pp * rows + r] * e;
-    O += o[((int64_t)pp * rows + r) * D + d] * e;
+    const float e = exp2f((m[pp * ps + r] - M) * kLog2e);
+    Ls += l[pp * ps + r] * e;
+    O += o[pp * ps + (int64_t)r * D + d] * e;
   }
   out[i] = f_to_dt(Ls > 0.0f ? O / Ls : 0.0f, bf);
 }
@@ -777,14 +777,19 @@ LaunchShape shape_for(int B, int Hkv, int nrep, int L, int N, int NT, int sms) {
   return s;
 }
 
+// Workspace layout (fixed prefix, so every call finds its tickets at the
+// same place whatever the previous call's shape was):
+//   [0, 256)                      device error flag
+//   [256, 256 + 4*kMaxTickets)    split tickets, zero between calls
+//   then (m, l) and o partials of the splits.
+constexpr int64_t kMaxTickets = 65536;
+constexpr size_t kTicketOff = 256;
+constexpr size_t kPartialOff = kTicketOff + 4 * kMaxTickets;
+
 size_t ws_bytes_for(int B, int Hkv, const LaunchShape& s, int NT, int D) {
-  if (s.nsplit <= 1) return 256;  // only the error flag
+  if (s.nsplit <= 1) return kPartialOff;
   const size_t slots = (size_t)B * Hkv * s.QB * s.nsplit * 8 * NT;
-  size_t bytes = 256;                                   // error flag + pad
-  bytes += ((size_t)B * Hkv * s.QB * 4 + 255) / 256 * 256;  // counters
-  bytes += (slots * 2 * 4 + 255) / 256 * 256;               // (m, l)
-  bytes += slots * D * 4;                                   // o
-  return bytes;
+  return kPartialOff + (slots * 2 * 4 + 255) / 256 * 256 + slots * D * 4;
 }
 
 template <int BITS, int D, int GS, int NT>
@@ -894,7 +899,11 @@ int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void*
   if (a.B == 0 || a.Hq == 0) return KVQ_OK;
   int dev = 0;
   KVQ_CUDA_TRY(cudaGetDevice(&dev));
-  const LaunchShape s = shape_for(a.B, a.Hkv, p.nrep, L, std::max(a.N, 1), NT, num_sms(dev));
+  LaunchShape s = shape_for(a.B, a.Hkv, p.nrep, L, std::max(a.N, 1), NT, num_sms(dev));
+  if ((int64_t)a.B * a.Hkv * s.QB > kMaxTickets) {  // too many merge groups: no key split
+    s.nsplit = 1;
+    s.rps = std::max(a.N, 1);
+  }
   const size_t need = ws_bytes_for(a.B, a.Hkv, s, NT, a.D);
   if (!ws) {
     ws = managed_workspace(dev, need, st, &rc);
@@ -906,12 +915,9 @@ int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void*
   p.err = reinterpret_cast<int*>(w);
   if (s.nsplit > 1) {
     const size_t slots = (size_t)a.B * a.Hkv * s.QB * s.nsplit * 8 * NT;
-    size_t off = 256;
-    p.counters = reinterpret_cast<unsigned*>(w + off);
-    off += ((size_t)a.B * a.Hkv * s.QB * 4 + 255) / 256 * 256;
-    p.ws_ml = reinterpret_cast<float*>(w + off);
-    off += (slots * 2 * 4 + 255) / 256 * 256;
-    p.ws_o = reinterpret_cast<float*>(w + off);
+    p.counters = reinterpret_cast<unsigned*>(w + kTicketOff);
+    p.ws_ml = reinterpret_cast<float*>(w + kPartialOff);
+    p.ws_o = reinterpret_cast<float*>(w + kPartialOff + (slots * 2 * 4 + 255) / 256 * 256);
   }
   p.QB = s.QB;
   p.rps = s.rps;
@@ -934,7 +940,8 @@ size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D) {
   const int NT = nrep <= 8 ? 1 : 2;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  const LaunchShape s = shape_for(B, Hkv, nrep, 1, std::max(N, 1), NT, num_sms(dev));
+  LaunchShape s = shape_for(B, Hkv, nrep, 1, std::max(N, 1), NT, num_sms(dev));
+  if ((int64_t)B * Hkv * s.QB > kMaxTickets) s.nsplit = 1;
   return ws_bytes_for(B, Hkv, s, NT, D);
 }
 
@@ -950,12 +957,12 @@ int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void
   return run(a, L, mask_mode, window, 0, out, nullptr, nullptr, nullptr, ws, ws_bytes, st);
 }
 
-int32_t launch_merge(const float* m, const float* l, const float* o, int parts, int rows, int D,
-                     int dtype, void* out, cudaStream_t st) {
+int32_t launch_merge(const float* m, const float* l, const float* o, int parts, int64_t pstride,
+                     int rows, int D, int dtype, void* out, cudaStream_t st) {
   const int64_t n = (int64_t)rows * D;
   if (n == 0) return KVQ_OK;
   merge_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
-      m, l, o, parts, rows, D, dtype == KVQ_DTYPE_BFLOAT16, static_cast<uint16_t*>(out));
+      m, l, o, parts, pstride, rows, D, dtype == KVQ_DTYPE_BFLOAT16, static_cast<uint16_t*>(out));
   KVQ_CUDA_TRY(cudaGetLastError());
   return KVQ_OK;
 }

@@ -578,12 +578,15 @@ int32_t kvq_sdpa_decode_partial(const kvq_qtensor* keys, const kvq_qtensor* valu
                        static_cast<cudaStream_t>(stream));
 }
 
-int32_t kvq_sdpa_merge(const float* m, const float* l, const float* o, int32_t parts, int32_t rows,
-                       int32_t head_dim, int32_t dtype, void* out, void* stream) {
+int32_t kvq_sdpa_merge(const float* m, const float* l, const float* o, int32_t parts,
+                       int64_t part_stride, int32_t rows, int32_t head_dim, int32_t dtype,
+                       void* out, void* stream) {
   if (!m || !l || !o || !out) return fail(KVQ_ERR_ARG, "NULL argument");
-  if (parts <= 0 || rows < 0 || head_dim <= 0) return fail(KVQ_ERR_ARG, "bad sizes");
+  if (parts <= 0 || rows < 0 || head_dim <= 0 || part_stride < 0) return fail(KVQ_ERR_ARG, "bad sizes");
+  if (parts > 1 && part_stride < (int64_t)rows) return fail(KVQ_ERR_ARG, "part_stride smaller than rows");
   if (dtype != KVQ_DTYPE_FLOAT16 && dtype != KVQ_DTYPE_BFLOAT16) return fail(KVQ_ERR_ARG, "bad dtype");
-  return launch_merge(m, l, o, parts, rows, head_dim, dtype, out, static_cast<cudaStream_t>(stream));
+  return launch_merge(m, l, o, parts, part_stride, rows, head_dim, dtype, out,
+                      static_cast<cudaStream_t>(stream));
 }
 
 int32_t kvq_sdpa_prefill(const kvq_qtensor* keys, const kvq_qtensor* values, const void* q,

@@ -59,8 +59,8 @@ size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D);
 // mode 0: normalized output in `out` (dtype); mode 1: partials (m, l, o).
 int32_t launch_decode(const AttnArgs& a, void* out, float* pm, float* pl, float* po, void* ws,
                       size_t ws_bytes, cudaStream_t st);
-int32_t launch_merge(const float* m, const float* l, const float* o, int parts, int rows, int D,
-                     int dtype, void* out, cudaStream_t st);
+int32_t launch_merge(const float* m, const float* l, const float* o, int parts, int64_t pstride,
+                     int rows, int D, int dtype, void* out, cudaStream_t st);
 int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void* out, void* ws,
                        size_t ws_bytes, cudaStream_t st);
 int32_t launch_debug_scores(const AttnArgs& a, int L, int mask_mode, int window, float* scores,

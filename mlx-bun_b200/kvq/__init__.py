@@ -7,10 +7,10 @@ decoding, chunked prefill, context-split partials and their merge.
 from ._lib import KvqError, lib
 from .cache import Mask, QuantizedKVCache, QuantizedTensor, RotatingQuantizedKVCache
 from .sdpa import (debug_scores, decode_workspace_bytes, quantize, quantized_sdpa, sdpa_decode,
-                   sdpa_decode_partial, sdpa_merge, sdpa_prefill)
+                   sdpa_decode_partial, sdpa_merge, sdpa_merge_packed, sdpa_prefill)
 
 __all__ = [
     "KvqError", "lib", "Mask", "QuantizedKVCache", "QuantizedTensor", "RotatingQuantizedKVCache",
     "debug_scores", "decode_workspace_bytes", "quantize", "quantized_sdpa", "sdpa_decode",
-    "sdpa_decode_partial", "sdpa_merge", "sdpa_prefill",
+    "sdpa_decode_partial", "sdpa_merge", "sdpa_merge_packed", "sdpa_prefill",
 ]

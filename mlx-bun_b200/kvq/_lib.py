@@ -79,7 +79,7 @@ def lib():
                                   ctypes.c_size_t, vp]),
         "kvq_sdpa_decode_partial": (i32, [P(QTensor), P(QTensor), vp, i32, f32, vp, vp, vp, vp,
                                           vp, ctypes.c_size_t, vp]),
-        "kvq_sdpa_merge": (i32, [vp, vp, vp, i32, i32, i32, i32, vp, vp]),
+        "kvq_sdpa_merge": (i32, [vp, vp, vp, i32, i64, i32, i32, i32, vp, vp]),
         "kvq_sdpa_prefill": (i32, [P(QTensor), P(QTensor), vp, i32, i32, f32, i32, i32, vp, vp,
                                    ctypes.c_size_t, vp]),
         "kvq_debug_scores": (i32, [P(QTensor), vp, i32, i32, f32, i32, i32, vp, vp]),

@@ -63,14 +63,25 @@ def sdpa_decode(q: torch.Tensor, keys: QuantizedTensor, values: QuantizedTensor,
 
 
 def sdpa_decode_partial(q: torch.Tensor, keys: QuantizedTensor, values: QuantizedTensor,
-                        scale: float, seq_lens: torch.Tensor | None = None, stream=None):
-    """Log-sum-exp partials (m [B*Hq], l [B*Hq], o [B*Hq, D]) of this key range."""
+                        scale: float, seq_lens: torch.Tensor | None = None,
+                        packed_out: torch.Tensor | None = None, stream=None):
+    """Log-sum-exp partials of this key range.
+
+    Returns (m [B*Hq], l [B*Hq], o [B*Hq, D]) float32.  With `packed_out`
+    (a float32 tensor of B*Hq*(D+2) elements) they are written into it as
+    [m | l | o] — the per-part layout sdpa_merge_packed expects — and the
+    returned tensors are views of it."""
     B, Hq, L, D = _check_q(q, keys)
     if L != 1:
         raise ValueError("partials are defined for one query row per head")
-    m = torch.empty(B * Hq, dtype=torch.float32, device=q.device)
-    l = torch.empty_like(m)
-    o = torch.empty(B * Hq, D, dtype=torch.float32, device=q.device)
+    R = B * Hq
+    if packed_out is None:
+        packed_out = torch.empty(R * (D + 2), dtype=torch.float32, device=q.device)
+    if packed_out.numel() != R * (D + 2) or packed_out.dtype != torch.float32 or \
+            not packed_out.is_contiguous():
+        raise ValueError("packed_out must be a contiguous float32 tensor of B*Hq*(D+2) elements")
+    flat = packed_out.view(-1)
+    m, l, o = flat[:R], flat[R:2 * R], flat[2 * R:].view(R, D)
     sl = seq_lens.data_ptr() if seq_lens is not None else None
     check(lib().kvq_sdpa_decode_partial(ctypes.byref(keys.qt), ctypes.byref(values.qt),
                                         q.data_ptr(), Hq, ctypes.c_float(scale), sl, m.data_ptr(),
@@ -86,8 +97,27 @@ def sdpa_merge(m: torch.Tensor, l: torch.Tensor, o: torch.Tensor, dtype: torch.d
         if t.dtype != torch.float32 or not t.is_contiguous() or not t.is_cuda:
             raise ValueError("partials must be contiguous CUDA float32 tensors")
     out = torch.empty(R, D, dtype=dtype, device=o.device)
-    check(lib().kvq_sdpa_merge(m.data_ptr(), l.data_ptr(), o.data_ptr(), P, R, D,
-                               dtype_code(dtype), out.data_ptr(), _stream(o, stream)))
+    # three separate arrays: one stride per array is not expressible, so merge
+    # through a packed copy [P, R*(D+2)]
+    packed = torch.cat([m, l, o.reshape(P, R * D)], dim=1).contiguous()
+    return sdpa_merge_packed(packed, R, D, dtype, out=out, stream=stream)
+
+
+def sdpa_merge_packed(packed: torch.Tensor, rows: int, head_dim: int, dtype: torch.dtype,
+                      out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Merge partials packed per part as [m (rows) | l (rows) | o (rows*D)]:
+    packed [P, rows*(head_dim+2)] float32 -> out [rows, head_dim] dtype."""
+    if packed.dtype != torch.float32 or not packed.is_contiguous() or not packed.is_cuda:
+        raise ValueError("packed partials must be a contiguous CUDA float32 tensor")
+    P = packed.shape[0]
+    ps = rows * (head_dim + 2)
+    if packed.numel() != P * ps:
+        raise ValueError("packed partials have the wrong size")
+    if out is None:
+        out = torch.empty(rows, head_dim, dtype=dtype, device=packed.device)
+    base = packed.data_ptr()
+    check(lib().kvq_sdpa_merge(base, base + 4 * rows, base + 8 * rows, P, ps, rows, head_dim,
+                               dtype_code(dtype), out.data_ptr(), _stream(packed, stream)))
     return out
 
 

@@ -48,7 +48,7 @@ def lib():
         _lib.kvqo_dequantize_rows.argtypes = [u32p, u16p, u16p, ctypes.c_int64, ctypes.c_int,
                                               ctypes.c_int, ctypes.c_int, ctypes.c_int, f32p]
         _lib.kvqo_sdpa_unfused.argtypes = [u16p, ctypes.c_void_p, ctypes.c_void_p] + \
-            [ctypes.c_int] * 10 + [ctypes.c_float, ctypes.c_int, ctypes.c_int,
+            [ctypes.c_int] * 9 + [ctypes.c_float, ctypes.c_int, ctypes.c_int,
                                    ctypes.POINTER(ctypes.c_int32), u16p, f32p, ctypes.c_int]
         _lib.kvqo_sdpa_unfused.restype = ctypes.c_int
         _lib.kvqo_max_threads.restype = ctypes.c_int
