@@ -6,38 +6,42 @@
 // the GQA group (row qr -> position qr / nrep, head qr % nrep), so every K/V
 // byte a CTA streams serves all query heads that share it.
 //
-// Data path per warp (W warps per CTA, round-robin over 16-row key tiles):
-//   * TMA bulk copies (cp.async.bulk, 1-D) move the tile's packed K, K
-//     scales, K biases, packed V, V scales, V biases (6 contiguous row
-//     ranges of one (b, h)) into a warp-private STAGES-deep shared-memory
-//     ring; completion is tracked by one mbarrier per stage.  Every wait is
-//     bounded: on timeout the kernel raises a device error flag and returns.
-//   * Codes are dequantised in registers to exact fp16 integers with the
-//     0x6400 (= 1024.0) magic: (bits | 0x6400) - 1024.  Four-bit codes in
-//     odd nibbles are taken unshifted as 16*c and the factor 16 is folded
-//     into the query (QK) or the output tile (PV).  Scales and biases are
-//     factored out of the inner products (qdot factoring, as in mlx-bun's
-//     Metal decode kernel, src/model/fused-decode-kernel.ts:62-114):
+// CTA = W consumer warps + 1 producer warp (warp specialised):
+//   * the producer streams the split's key rows in chunks of CH = W*RW rows:
+//     six TMA bulk copies (cp.async.bulk, 1-D) per chunk — packed K, K
+//     scales, K biases, packed V, V scales, V biases, each a contiguous row
+//     range of one (b, h) — into a STAGES-deep shared-memory ring, with one
+//     `full` mbarrier (transaction bytes) and one `empty` mbarrier (W
+//     consumer arrivals) per stage.  Every wait is bounded: on timeout the
+//     kernel raises a device error flag and leaves its loops.
+//   * consumer warp w takes rows [w*RW, (w+1)*RW) of every chunk.
+// Per consumer slice (RW = 16 or 32 key rows):
+//   * codes become exact fp16 integers in registers with the 0x6400 (=1024)
+//     magic: (bits | 0x6400) - 1024 = c.  Four-bit codes in odd nibbles are
+//     taken unshifted (1024 + 16c) and the factor 16 is folded into the
+//     query.  Scales and biases are factored out of the inner products
+//     (qdot factoring, as in mlx-bun's Metal decode kernel,
+//     src/model/fused-decode-kernel.ts:62-114):
 //        q . (s*c + b) = s * (q . c) + b * sum(q)
 //        sum_n p_n (s_n c_n + b_n) = sum_n (p_n s_n) c_n + sum_n p_n b_n
-//     so the tensor cores only see exact integer codes.
-//   * QK^T: mma.m16n8k16 with the 16 key rows as M (codes as A, row-major
-//     pairs along d), the query rows as N (8 per n-tile, q as B, loaded once
-//     per CTA), d as K — one accumulator per quantisation group.
-//   * Online softmax in f32 (exp2 with log2e prescale); scores are rounded
-//     to the cache dtype first, as the reference graph rounds them
+//   * QK^T: mma.m16n8k16, key rows as M (codes as A, pairs along d), query
+//     rows as N (8 per n-tile; q as B, loaded once per CTA), d as K; one
+//     accumulator per quantisation group.
+//   * online softmax in f32 with ex2.approx; scores are first rounded to the
+//     cache dtype, as the reference graph rounds them
 //     (src/model/gemma4-base.ts:1307).
 //   * PV: O^T[d x q] += V^T[d x n] (p*s)^T[n x q]; the probability tile goes
 //     from the QK accumulator layout to the B-operand layout with one
-//     movmatrix.trans per 8x8 block; V codes for a (d, 2 rows) pair are
-//     interleaved with one prmt per 16-bit chunk.
-//   * Splits of the key range merge in fixed order (deterministic) in the
+//     movmatrix.trans per 8x8 block; V codes of a (d, 2 rows) pair are
+//     interleaved with one prmt per 16-bit chunk and made exact with one
+//     f16x2 subtract.
+//   * splits of the key range merge in fixed order (deterministic) in the
 //     last CTA to finish, found by an atomic ticket — no second launch.
 //
 // Tensor-core choice: decode is HBM-bound with at most 16 query rows per kv
 // head, so the register-sourced mma.sync keeps the dequantised codes in
-// registers (no shared-memory round trip) with ample tensor throughput
-// (2 MMAs per key row).  The tcgen05/TMEM path is the prefill kernel's.
+// registers (no shared-memory round trip); tensor throughput is not the
+// limit (2 MMAs per key row).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -50,9 +54,9 @@ namespace {
 
 constexpr float kNeg = -1.0e30f;             // finite "minus infinity" for masked logits
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kTile = 16;                     // key rows per warp tile
-constexpr long long kWaitLimit = 1ll << 30;     // mbarrier polls before declaring a hang
-constexpr uint64_t kWaitNs = 2000000000ull;     // ... or 2 s of %globaltimer, whichever first
+constexpr int kTile = 16;                     // rows per MMA tile; row-alignment unit
+constexpr long long kWaitLimit = 1ll << 30;   // mbarrier polls before declaring a hang
+constexpr uint64_t kWaitNs = 2000000000ull;   // ... or 2 s of %globaltimer, whichever first
 
 struct Params {
   const uint8_t* kp;
@@ -92,6 +96,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
@@ -158,6 +166,13 @@ __device__ __forceinline__ uint32_t sub1024(uint32_t x) {
   return r;
 }
 
+// 2^x (approximate; flushes results below 2^-126 to zero).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -175,9 +190,11 @@ __device__ __forceinline__ float round_dt(float f, int bf16) {
   return bf16 ? __bfloat162float(__float2bfloat16_rn(f)) : __half2float(__float2half_rn(f));
 }
 
-// K operand (pairs along d within one row).  4-bit word w holds nibbles
-// e0..e7: x0 = (e0, e4), x1 = 16*(e1, e5), x2 = (e2, e6), x3 = 16*(e3, e7).
-// 8-bit word: x0 = (b0, b1), x1 = (b2, b3).
+// K operand (pairs along d within one row), exact: a 4-bit word w holds
+// nibbles e0..e7: x0 = (e0, e4), x1 = 16*(e1, e5), x2 = (e2, e6), x3 =
+// 16*(e3, e7); an 8-bit word: x0 = (b0, b1), x1 = (b2, b3).  (Keeping the
+// 1024 offset and cancelling it in the accumulator loses ~10 bits of the
+// 4-bit products, enough to flip the dtype rounding of large logits.)
 template <int BITS>
 __device__ __forceinline__ uint32_t k_extract(uint32_t w, int x) {
   if (BITS == 4) {
@@ -190,7 +207,7 @@ __device__ __forceinline__ uint32_t k_extract(uint32_t w, int x) {
 }
 
 // V operand: T holds a 16-bit chunk of row r0 (low half) and of row r1 (high
-// half); element j of the chunk as the pair (r0, r1).
+// half); element j of the chunk as the exact pair (r0, r1).
 template <int BITS>
 __device__ __forceinline__ uint32_t v_extract(uint32_t T, int j) {
   if (BITS == 4) {
@@ -224,6 +241,18 @@ __device__ __forceinline__ void lds_words(uint32_t* w, const uint8_t* p) {
   }
 }
 
+// All NG scales (or biases) of one row as f32.
+template <int NG>
+__device__ __forceinline__ void lds_scales(float* out, const uint16_t* row, int bf) {
+  uint32_t w[(NG + 1) / 2];
+  lds_words<NG * 2>(w, reinterpret_cast<const uint8_t*>(row));
+#pragma unroll
+  for (int i = 0; i < NG; i++) {
+    const uint16_t h = (uint16_t)((i & 1) ? (w[i / 2] >> 16) : (w[i / 2] & 0xffffu));
+    out[i] = dt_to_f(h, bf);
+  }
+}
+
 template <int BITS, int D, int GS>
 struct Geo {
   static constexpr int NG = D / GS;             // quantisation groups per row
@@ -239,45 +268,52 @@ struct Geo {
   static constexpr int MTG = GS / 16;           // PV m-tiles (16 d) per group
   static constexpr int KSTEPS = D / 16;
   static constexpr int MT = D / 16;
-  static constexpr int O_KP = 0;
-  static constexpr int O_KS = O_KP + kTile * KRB;
-  static constexpr int O_KB = O_KS + kTile * SRB;
-  static constexpr int O_VP = O_KB + kTile * SRB;
-  static constexpr int O_VS = O_VP + kTile * KRB;
-  static constexpr int O_VB = O_VS + kTile * SRB;
-  static constexpr int STAGE = O_VB + kTile * SRB;
+  static constexpr int ROWB = 2 * KRB + 4 * SRB;  // bytes per key row (K and V triples)
   static_assert(KB >= 4, "unsupported group size / bits");
-  static_assert((kTile * SRB) % 16 == 0, "scale rows must tile in 16-byte units");
 };
 
-template <int BITS, int D, int GS, int NT, int W, int STAGES>
+template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
 struct Smem {
   using G = Geo<BITS, D, GS>;
   static constexpr int HQ = 8 * NT;
-  static constexpr int Q_F = 0;                                  // f32 [HQ][D]
-  static constexpr int QSUM = Q_F + HQ * D * 4;                  // f32 [HQ][NG]
-  static constexpr int BARS = (QSUM + HQ * G::NG * 4 + 15) / 16 * 16;
-  static constexpr int STAGES_OFF = (BARS + W * STAGES * 8 + 127) / 128 * 128;
-  static constexpr int STAGE_BYTES = W * STAGES * G::STAGE;
+  static constexpr int CH = W * RW;                            // key rows per chunk
+  static constexpr int O_KP = 0;                               // offsets inside a stage
+  static constexpr int O_KS = O_KP + CH * G::KRB;
+  static constexpr int O_KB = O_KS + CH * G::SRB;
+  static constexpr int O_VP = O_KB + CH * G::SRB;
+  static constexpr int O_VS = O_VP + CH * G::KRB;
+  static constexpr int O_VB = O_VS + CH * G::SRB;
+  static constexpr int STAGE = O_VB + CH * G::SRB;
+  static constexpr int Q_F = 0;                                // f32 [HQ][D]
+  static constexpr int QSUM = Q_F + HQ * D * 4;                // f32 [HQ][NG]
+  static constexpr int BARS = (QSUM + HQ * G::NG * 4 + 15) / 16 * 16;  // full[ST], empty[ST]
+  static constexpr int CTRL = BARS + 2 * STAGES * 8;
+  static constexpr int STAGES_OFF = (CTRL + 16 + 127) / 128 * 128;
+  static constexpr int STAGE_BYTES = STAGES * STAGE;
   static constexpr int MERGE_BYTES = W * HQ * (D + 2) * 4;
-  static constexpr int CTRL = STAGES_OFF + (STAGE_BYTES > MERGE_BYTES ? STAGE_BYTES : MERGE_BYTES);
-  static constexpr int TOTAL = CTRL + 16;
+  static constexpr int TOTAL =
+      STAGES_OFF + (STAGE_BYTES > MERGE_BYTES ? STAGE_BYTES : MERGE_BYTES);
+  static_assert((CH * G::SRB) % 16 == 0, "scale rows must tile in 16-byte units");
 };
 
-template <int BITS, int D, int GS, int NT, int W, int STAGES>
-__global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
+template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
+__global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
   using G = Geo<BITS, D, GS>;
-  using S = Smem<BITS, D, GS, NT, W, STAGES>;
+  using S = Smem<BITS, D, GS, NT, W, RW, STAGES>;
   constexpr int HQ = S::HQ;
+  constexpr int CH = S::CH;
+  constexpr int MTS = RW / 16;  // 16-row m-tiles per consumer slice
   extern __shared__ __align__(128) uint8_t smem[];
   float* q_f = reinterpret_cast<float*>(smem + S::Q_F);
   float* qsum = reinterpret_cast<float*>(smem + S::QSUM);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BARS);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BARS);
+  uint64_t* empty = full + STAGES;
+  int* ctrl = reinterpret_cast<int*>(smem + S::CTRL);
   uint8_t* stages = smem + S::STAGES_OFF;
   float* mrg = reinterpret_cast<float*>(smem + S::STAGES_OFF);  // aliases stages after the loop
-  int* ctrl = reinterpret_cast<int*>(smem + S::CTRL);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const bool producer = warp == W;
   const int split = blockIdx.x;
   const int kvh = blockIdx.y % p.Hkv;
   const int qb = blockIdx.y / p.Hkv;
@@ -302,10 +338,53 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
   if (split >= nact) return;
   const int n0 = lo + split * p.rps;
   const int n1 = min(n0 + p.rps, hi);
+  const int nchunks = (n1 - n0 + CH - 1) / CH;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], W);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Causal bounds shared by every column of the block (fast-path test).
+  int kz_min = Nb - 1, ka_max = 0;
+  if (p.mask_mode == 1) {
+    const int qr_last = min(qr0 + HQ, qrows) - 1;
+    kz_min = min(kz_min, Nb - L + qr0 / nrep);
+    if (p.window > 0) ka_max = max(0, Nb - L + qr_last / nrep - p.window + 1);
+  }
+  __syncthreads();
+
+  bool hung = false;
+  const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
+  const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
+  // Producer: one chunk of CH key rows into stage c % STAGES.  Stages are
+  // only reused after the `empty` barrier shows all consumers are done.
+  auto produce = [&](int c) -> bool {
+    const int s = c % STAGES;
+    if (c >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1))) return false;
+    const int64_t row = n0 + (int64_t)c * CH;
+    const int rows = min(CH, n1 - (int)(row));
+    const uint32_t cr = (uint32_t)((rows + kTile - 1) / kTile * kTile);
+    uint8_t* st = stages + s * S::STAGE;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(&full[s], cr * G::ROWB);
+    bulk_g2s(st + S::O_KP, p.kp + (kbase + row) * G::KRB, cr * G::KRB, &full[s]);
+    bulk_g2s(st + S::O_KS, p.ks + (kbase + row) * G::NG, cr * G::SRB, &full[s]);
+    bulk_g2s(st + S::O_KB, p.kb + (kbase + row) * G::NG, cr * G::SRB, &full[s]);
+    bulk_g2s(st + S::O_VP, p.vp + (vbase + row) * G::KRB, cr * G::KRB, &full[s]);
+    bulk_g2s(st + S::O_VS, p.vs + (vbase + row) * G::NG, cr * G::SRB, &full[s]);
+    bulk_g2s(st + S::O_VB, p.vb + (vbase + row) * G::NG, cr * G::SRB, &full[s]);
+    return true;
+  };
+  // Prologue before any block-wide barrier: fill the ring (no waits needed).
+  if (producer && lane == 0)
+    for (int c = 0; c < STAGES && c < nchunks; c++) produce(c);
 
   // ---- stage the query block: q * dtype(scale), rounded to dtype ----
   const float scale_dt = round_dt(p.scale, bf);
-  for (int i = tid; i < HQ * D; i += W * 32) {
+  for (int i = tid; i < HQ * D; i += (W + 1) * 32) {
     const int r = i / D, d = i - r * D;
     const int qr = qr0 + r;
     float v = 0.0f;
@@ -317,93 +396,14 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
     }
     q_f[i] = v;
   }
-  if (tid < W * STAGES) mbar_init(&bars[tid], 1);
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   __syncthreads();
-  for (int i = tid; i < HQ * G::NG; i += W * 32) {
+  for (int i = tid; i < HQ * G::NG; i += (W + 1) * 32) {
     const int r = i / G::NG, grp = i - r * G::NG;
     float s = 0.0f;
     for (int d = 0; d < GS; d++) s += q_f[r * D + grp * GS + d];
     qsum[i] = s;
   }
-
-  // ---- per-warp TMA ring over this warp's key tiles ----
-  const int ntiles = (n1 - n0 + kTile - 1) / kTile;
-  const int my_tiles = ntiles > warp ? (ntiles - warp + W - 1) / W : 0;
-  uint8_t* wst = stages + warp * STAGES * G::STAGE;
-  uint64_t* wbar = bars + warp * STAGES;
-  const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
-  const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
-
-  auto issue = [&](int i) {
-    const int s = i % STAGES;
-    const int64_t row = n0 + (int64_t)(warp + i * W) * kTile;
-    uint8_t* st = wst + s * G::STAGE;
-    mbar_expect_tx(&wbar[s], 2 * kTile * (G::KRB + 2 * G::SRB));
-    bulk_g2s(st + G::O_KP, p.kp + (kbase + row) * G::KRB, kTile * G::KRB, &wbar[s]);
-    bulk_g2s(st + G::O_KS, p.ks + (kbase + row) * G::NG, kTile * G::SRB, &wbar[s]);
-    bulk_g2s(st + G::O_KB, p.kb + (kbase + row) * G::NG, kTile * G::SRB, &wbar[s]);
-    bulk_g2s(st + G::O_VP, p.vp + (vbase + row) * G::KRB, kTile * G::KRB, &wbar[s]);
-    bulk_g2s(st + G::O_VS, p.vs + (vbase + row) * G::NG, kTile * G::SRB, &wbar[s]);
-    bulk_g2s(st + G::O_VB, p.vb + (vbase + row) * G::NG, kTile * G::SRB, &wbar[s]);
-  };
-  __syncthreads();  // qsum visible; barriers initialised
-  if (lane == 0)
-    for (int i = 0; i < STAGES && i < my_tiles; i++) issue(i);
-
-  // ---- query fragments (B operand of QK), loaded once ----
-  uint32_t qbf[G::KSTEPS][NT][2];
-#pragma unroll
-  for (int kk = 0; kk < G::KSTEPS; kk++) {
-    const int grp = kk / G::MTG, kin = kk % G::MTG;
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      const float* qrow = q_f + (nt * 8 + g) * D;
-#pragma unroll
-      for (int w2 = 0; w2 < 2; w2++) {
-        const int v = 2 * kin + w2;
-        int d_lo, d_hi;
-        float f = 1.0f;
-        if (BITS == 4) {
-          const int wi = v / 4, x = v % 4;
-          const int base = grp * GS + t * (GS / 4) + 8 * wi;
-          d_lo = base + x;
-          d_hi = base + x + 4;
-          if (x & 1) f = 0.0625f;
-        } else {
-          const int wi = v / 2, x = v % 2;
-          const int base = grp * GS + t * (GS / 4) + 4 * wi;
-          d_lo = base + 2 * x;
-          d_hi = base + 2 * x + 1;
-        }
-        qbf[kk][nt][w2] = pack_h2(qrow[d_lo] * f, qrow[d_hi] * f);
-      }
-    }
-  }
-  float qs_r[NT][G::NG][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-    for (int grp = 0; grp < G::NG; grp++)
-#pragma unroll
-      for (int hh = 0; hh < 2; hh++) qs_r[nt][grp][hh] = qsum[(nt * 8 + 2 * t + hh) * G::NG + grp];
-
-  // Key-index limits of this lane's query columns (inclusive bounds).
-  int klo[NT][2], khi[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-      const int qr = qr0 + nt * 8 + 2 * t + hh;
-      int a = 0, z = Nb - 1;
-      if (p.mask_mode == 1 && qr < qrows) {
-        const int pos = Nb - L + qr / nrep;
-        z = min(z, pos);
-        if (p.window > 0) a = max(0, pos - p.window + 1);
-      }
-      klo[nt][hh] = a;
-      khi[nt][hh] = z;
-    }
+  __syncthreads();
 
   float m_run[NT][2], l_run[NT][2], pb[NT][G::NG][2];
   float o_acc[G::MT][NT][4];
@@ -423,169 +423,289 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
 #pragma unroll
       for (int c = 0; c < 4; c++) o_acc[mt][nt][c] = 0.0f;
 
-  bool hung = false;
-  for (int i = 0; i < my_tiles; i++) {
-    const int s = i % STAGES;
-    // The decision must be warp-uniform: the loop body is full of warp-collective ops.
-    if (!__all_sync(0xffffffffu, mbar_wait(&wbar[s], (uint32_t)((i / STAGES) & 1)))) {
-      hung = true;
-      break;
-    }
-    const uint8_t* st = wst + s * G::STAGE;
-    const int row0 = n0 + (warp + i * W) * kTile;
-
-    // ---------------- scores ----------------
-    float sc[NT][4];
+  if (producer) {
+    // ---------------- producer: keep the ring full ----------------
+    if (lane == 0)
+      for (int c = STAGES; c < nchunks; c++)
+        if (!produce(c)) {
+          hung = true;
+          break;
+        }
+  } else {
+    // ---- query fragments (B operand of QK), loaded once ----
+    uint32_t qbf[G::KSTEPS][NT][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++)
+    for (int kk = 0; kk < G::KSTEPS; kk++) {
+      const int grp = kk / G::MTG, kin = kk % G::MTG;
 #pragma unroll
-      for (int c = 0; c < 4; c++) sc[nt][c] = 0.0f;
-    const uint16_t* ksc = reinterpret_cast<const uint16_t*>(st + G::O_KS);
-    const uint16_t* kbi = reinterpret_cast<const uint16_t*>(st + G::O_KB);
-#pragma unroll
-    for (int grp = 0; grp < G::NG; grp++) {
-      uint32_t kw0[G::KW], kw1[G::KW];
-      lds_words<G::KB>(kw0, st + G::O_KP + g * G::KRB + grp * G::GB + t * G::KB);
-      lds_words<G::KB>(kw1, st + G::O_KP + (g + 8) * G::KRB + grp * G::GB + t * G::KB);
-      float acc[NT][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) acc[nt][c] = 0.0f;
-#pragma unroll
-      for (int kin = 0; kin < G::MTG; kin++) {
-        uint32_t a[4];
+      for (int nt = 0; nt < NT; nt++) {
+        const float* qrow = q_f + (nt * 8 + g) * D;
 #pragma unroll
         for (int w2 = 0; w2 < 2; w2++) {
           const int v = 2 * kin + w2;
-          const int wi = BITS == 4 ? v / 4 : v / 2;
-          const int x = BITS == 4 ? v % 4 : v % 2;
-          a[2 * w2] = k_extract<BITS>(kw0[wi], x);
-          a[2 * w2 + 1] = k_extract<BITS>(kw1[wi], x);
+          int d_lo, d_hi;
+          float f = 1.0f;
+          if (BITS == 4) {
+            const int wi = v / 4, x = v % 4;
+            const int base = grp * GS + t * (GS / 4) + 8 * wi;
+            d_lo = base + x;
+            d_hi = base + x + 4;
+            if (x & 1) f = 0.0625f;
+          } else {
+            const int wi = v / 2, x = v % 2;
+            const int base = grp * GS + t * (GS / 4) + 4 * wi;
+            d_lo = base + 2 * x;
+            d_hi = base + 2 * x + 1;
+          }
+          qbf[kk][nt][w2] = pack_h2(qrow[d_lo] * f, qrow[d_hi] * f);
         }
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-          mma16816(acc[nt], a, qbf[grp * G::MTG + kin][nt][0], qbf[grp * G::MTG + kin][nt][1]);
-      }
-      const float s0 = dt_to_f(ksc[g * G::NG + grp], bf), b0 = dt_to_f(kbi[g * G::NG + grp], bf);
-      const float s1 = dt_to_f(ksc[(g + 8) * G::NG + grp], bf),
-                  b1 = dt_to_f(kbi[(g + 8) * G::NG + grp], bf);
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++) {
-        sc[nt][0] += s0 * acc[nt][0] + b0 * qs_r[nt][grp][0];
-        sc[nt][1] += s0 * acc[nt][1] + b0 * qs_r[nt][grp][1];
-        sc[nt][2] += s1 * acc[nt][2] + b1 * qs_r[nt][grp][0];
-        sc[nt][3] += s1 * acc[nt][3] + b1 * qs_r[nt][grp][1];
       }
     }
-
-    // ---------------- online softmax ----------------
-    const int r_lo = row0 + g, r_hi = row0 + g + 8;
-    float pr[NT][4];
-    bool rescale = false;
-    float alpha[NT][2];
+    float qs_r[NT][G::NG][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int grp = 0; grp < G::NG; grp++)
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+          qs_r[nt][grp][hh] = qsum[(nt * 8 + 2 * t + hh) * G::NG + grp];
+        }
+
+    // Key-index limits of this lane's query columns (inclusive bounds).
+    int klo[NT][2], khi[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
       for (int hh = 0; hh < 2; hh++) {
-        const bool v0 = r_lo < n1 && r_lo >= klo[nt][hh] && r_lo <= khi[nt][hh];
-        const bool v1 = r_hi < n1 && r_hi >= klo[nt][hh] && r_hi <= khi[nt][hh];
-        const float x0 = v0 ? round_dt(sc[nt][hh], bf) : kNeg;
-        const float x1 = v1 ? round_dt(sc[nt][2 + hh], bf) : kNeg;
-        if (p.scores) {
-          const int qr = qr0 + nt * 8 + 2 * t + hh;
-          if (qr < qrows) {
-            const int l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
-            float* srow = p.scores + (((int64_t)b * p.Hq + hq) * L + l) * p.N;
-            if (v0) srow[r_lo] = x0;
-            if (v1) srow[r_hi] = x1;
+        const int qr = qr0 + nt * 8 + 2 * t + hh;
+        int a = 0, z = Nb - 1;
+        if (p.mask_mode == 1 && qr < qrows) {
+          const int pos = Nb - L + qr / nrep;
+          z = min(z, pos);
+          if (p.window > 0) a = max(0, pos - p.window + 1);
+        }
+        klo[nt][hh] = a;
+        khi[nt][hh] = z;
+      }
+
+    for (int c = 0; c < nchunks; c++) {
+      const int s = c % STAGES;
+      // The decision must be warp-uniform: the slice is full of warp-collective ops.
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)((c / STAGES) & 1)))) {
+        hung = true;
+        break;
+      }
+      const uint8_t* st = stages + s * S::STAGE;
+      const int srow0 = n0 + c * CH + warp * RW;  // first key row of this slice
+      if (srow0 < n1) {
+        const bool fast = !p.scores && srow0 + RW <= n1 && srow0 + RW - 1 <= kz_min &&
+                          srow0 >= ka_max;
+        const int r_base = warp * RW;  // slice rows inside the chunk
+
+        // ---------------- scores ----------------
+        float sc[MTS][NT][4];
+#pragma unroll
+        for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int cc = 0; cc < 4; cc++) sc[mt][nt][cc] = 0.0f;
+#pragma unroll
+        for (int mt = 0; mt < MTS; mt++) {
+          const int R0 = r_base + mt * 16 + g, R1 = R0 + 8;
+          float ks0[G::NG], kb0[G::NG], ks1[G::NG], kb1[G::NG];
+          lds_scales<G::NG>(ks0, reinterpret_cast<const uint16_t*>(st + S::O_KS) + R0 * G::NG, bf);
+          lds_scales<G::NG>(kb0, reinterpret_cast<const uint16_t*>(st + S::O_KB) + R0 * G::NG, bf);
+          lds_scales<G::NG>(ks1, reinterpret_cast<const uint16_t*>(st + S::O_KS) + R1 * G::NG, bf);
+          lds_scales<G::NG>(kb1, reinterpret_cast<const uint16_t*>(st + S::O_KB) + R1 * G::NG, bf);
+#pragma unroll
+          for (int grp = 0; grp < G::NG; grp++) {
+            uint32_t kw0[G::KW], kw1[G::KW];
+            lds_words<G::KB>(kw0, st + S::O_KP + R0 * G::KRB + grp * G::GB + t * G::KB);
+            lds_words<G::KB>(kw1, st + S::O_KP + R1 * G::KRB + grp * G::GB + t * G::KB);
+            float acc[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+              acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+            }
+#pragma unroll
+            for (int kin = 0; kin < G::MTG; kin++) {
+              uint32_t a[4];
+#pragma unroll
+              for (int w2 = 0; w2 < 2; w2++) {
+                const int v = 2 * kin + w2;
+                const int wi = BITS == 4 ? v / 4 : v / 2;
+                const int x = BITS == 4 ? v % 4 : v % 2;
+                a[2 * w2] = k_extract<BITS>(kw0[wi], x);
+                a[2 * w2 + 1] = k_extract<BITS>(kw1[wi], x);
+              }
+#pragma unroll
+              for (int nt = 0; nt < NT; nt++)
+                mma16816(acc[nt], a, qbf[grp * G::MTG + kin][nt][0],
+                         qbf[grp * G::MTG + kin][nt][1]);
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+              sc[mt][nt][0] = fmaf(ks0[grp], acc[nt][0], fmaf(kb0[grp], qs_r[nt][grp][0], sc[mt][nt][0]));
+              sc[mt][nt][1] = fmaf(ks0[grp], acc[nt][1], fmaf(kb0[grp], qs_r[nt][grp][1], sc[mt][nt][1]));
+              sc[mt][nt][2] = fmaf(ks1[grp], acc[nt][2], fmaf(kb1[grp], qs_r[nt][grp][0], sc[mt][nt][2]));
+              sc[mt][nt][3] = fmaf(ks1[grp], acc[nt][3], fmaf(kb1[grp], qs_r[nt][grp][1], sc[mt][nt][3]));
+            }
           }
         }
-        float tm = fmaxf(x0, x1);
-        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
-        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
-        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
-        const float mn = fmaxf(m_run[nt][hh], tm);
-        const float al = exp2f((m_run[nt][hh] - mn) * kLog2e);
-        rescale |= (mn != m_run[nt][hh]);
-        alpha[nt][hh] = al;
-        const float q0 = v0 ? exp2f((x0 - mn) * kLog2e) : 0.0f;
-        const float q1 = v1 ? exp2f((x1 - mn) * kLog2e) : 0.0f;
-        pr[nt][hh] = q0;
-        pr[nt][2 + hh] = q1;
-        l_run[nt][hh] = l_run[nt][hh] * al + q0 + q1;
-        m_run[nt][hh] = mn;
-      }
-    }
-    if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-        for (int mt = 0; mt < G::MT; mt++) {
-          o_acc[mt][nt][0] *= alpha[nt][0];
-          o_acc[mt][nt][1] *= alpha[nt][1];
-          o_acc[mt][nt][2] *= alpha[nt][0];
-          o_acc[mt][nt][3] *= alpha[nt][1];
-        }
-#pragma unroll
-        for (int grp = 0; grp < G::NG; grp++) {
-          pb[nt][grp][0] *= alpha[nt][0];
-          pb[nt][grp][1] *= alpha[nt][1];
-        }
-      }
-    }
 
-    // ---------------- P V ----------------
-    const uint16_t* vsc = reinterpret_cast<const uint16_t*>(st + G::O_VS);
-    const uint16_t* vbi = reinterpret_cast<const uint16_t*>(st + G::O_VB);
+        // ---------------- online softmax ----------------
+        float pr[MTS][NT][4];
+        float alpha[NT][2];
+        bool rescale = false;
 #pragma unroll
-    for (int grp = 0; grp < G::NG; grp++) {
-      const float vs0 = dt_to_f(vsc[g * G::NG + grp], bf), vb0 = dt_to_f(vbi[g * G::NG + grp], bf);
-      const float vs1 = dt_to_f(vsc[(g + 8) * G::NG + grp], bf),
-                  vb1 = dt_to_f(vbi[(g + 8) * G::NG + grp], bf);
-      uint32_t bfr[NT][2];
+        for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
-      for (int nt = 0; nt < NT; nt++) {
-        // p == 0 for masked rows: select, never multiply stale scales.
-        const float p0 = pr[nt][0], p1 = pr[nt][1], p2 = pr[nt][2], p3 = pr[nt][3];
-        pb[nt][grp][0] += (p0 != 0.0f ? p0 * vb0 : 0.0f) + (p2 != 0.0f ? p2 * vb1 : 0.0f);
-        pb[nt][grp][1] += (p1 != 0.0f ? p1 * vb0 : 0.0f) + (p3 != 0.0f ? p3 * vb1 : 0.0f);
-        const uint32_t r0 = pack_h2(p0 != 0.0f ? p0 * vs0 : 0.0f, p1 != 0.0f ? p1 * vs0 : 0.0f);
-        const uint32_t r1 = pack_h2(p2 != 0.0f ? p2 * vs1 : 0.0f, p3 != 0.0f ? p3 * vs1 : 0.0f);
-        bfr[nt][0] = movmatrix_t(r0);
-        bfr[nt][1] = movmatrix_t(r1);
-      }
-      uint32_t vw[4][G::VW];
-      lds_words<G::VB>(vw[0], st + G::O_VP + (2 * t) * G::KRB + grp * G::GB + g * G::VB);
-      lds_words<G::VB>(vw[1], st + G::O_VP + (2 * t + 1) * G::KRB + grp * G::GB + g * G::VB);
-      lds_words<G::VB>(vw[2], st + G::O_VP + (2 * t + 8) * G::KRB + grp * G::GB + g * G::VB);
-      lds_words<G::VB>(vw[3], st + G::O_VP + (2 * t + 9) * G::KRB + grp * G::GB + g * G::VB);
-      uint32_t af[G::MTG][4];
+          for (int hh = 0; hh < 2; hh++) {
+            float x[MTS][2];
+            bool vv[MTS][2];
 #pragma unroll
-      for (int c = 0; c < G::C; c++) {
-        const uint32_t sel = (c & 1) ? 0x7632u : 0x5410u;
-        const uint32_t Tlo = prmt(vw[0][c / 2], vw[1][c / 2], sel);
-        const uint32_t Thi = prmt(vw[2][c / 2], vw[3][c / 2], sel);
+            for (int mt = 0; mt < MTS; mt++) {
 #pragma unroll
-        for (int j = 0; j < G::E; j++) {
-          const int sl = c * G::E + j;
-          const int mt = sl % G::MTG, half = sl / G::MTG;
-          af[mt][half] = v_extract<BITS>(Tlo, j);       // a0 (m-row g) / a1 (m-row g+8)
-          af[mt][2 + half] = v_extract<BITS>(Thi, j);   // a2 / a3
+              for (int e = 0; e < 2; e++) {
+                const int r = srow0 + mt * 16 + g + 8 * e;
+                const float rs = round_dt(sc[mt][nt][2 * e + hh], bf);
+                if (fast) {
+                  vv[mt][e] = true;
+                  x[mt][e] = rs;
+                } else {
+                  vv[mt][e] = r < n1 && r >= klo[nt][hh] && r <= khi[nt][hh];
+                  x[mt][e] = vv[mt][e] ? rs : kNeg;
+                  if (p.scores && vv[mt][e]) {
+                    const int qr = qr0 + nt * 8 + 2 * t + hh;
+                    if (qr < qrows) {
+                      const int l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
+                      p.scores[(((int64_t)b * p.Hq + hq) * L + l) * p.N + r] = rs;
+                    }
+                  }
+                }
+              }
+            }
+            float tm = x[0][0];
+#pragma unroll
+            for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+              for (int e = 0; e < 2; e++) tm = fmaxf(tm, x[mt][e]);
+            tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
+            tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
+            tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
+            const float mn = fmaxf(m_run[nt][hh], tm);
+            const float mls = mn * kLog2e;
+            // (m_old - m_new) first: exactly 0 when the max is unchanged, even at
+            // the -1e30 sentinel (an fma against the rounded product would leave
+            // its rounding residual, ~1e23 there, and 2^that is inf).
+            const float al = ex2((m_run[nt][hh] - mn) * kLog2e);
+            rescale |= (mn != m_run[nt][hh]);
+            alpha[nt][hh] = al;
+            float lsum = 0.0f;
+#pragma unroll
+            for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+              for (int e = 0; e < 2; e++) {
+                const float pe = ex2(fmaf(x[mt][e], kLog2e, -mls));
+                const float pv = (fast || vv[mt][e]) ? pe : 0.0f;
+                pr[mt][nt][2 * e + hh] = pv;
+                lsum += pv;
+              }
+            l_run[nt][hh] = fmaf(l_run[nt][hh], al, lsum);
+            m_run[nt][hh] = mn;
+          }
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+            for (int mt = 0; mt < G::MT; mt++) {
+              o_acc[mt][nt][0] *= alpha[nt][0];
+              o_acc[mt][nt][1] *= alpha[nt][1];
+              o_acc[mt][nt][2] *= alpha[nt][0];
+              o_acc[mt][nt][3] *= alpha[nt][1];
+            }
+#pragma unroll
+            for (int grp = 0; grp < G::NG; grp++) {
+              pb[nt][grp][0] *= alpha[nt][0];
+              pb[nt][grp][1] *= alpha[nt][1];
+            }
+          }
+        }
+
+        // ---------------- P V ----------------
+#pragma unroll
+        for (int kk = 0; kk < MTS; kk++) {  // 16-row k-steps of the slice
+          const int R0 = r_base + kk * 16 + g, R1 = R0 + 8;
+          float vs0[G::NG], vb0[G::NG], vs1[G::NG], vb1[G::NG];
+          lds_scales<G::NG>(vs0, reinterpret_cast<const uint16_t*>(st + S::O_VS) + R0 * G::NG, bf);
+          lds_scales<G::NG>(vb0, reinterpret_cast<const uint16_t*>(st + S::O_VB) + R0 * G::NG, bf);
+          lds_scales<G::NG>(vs1, reinterpret_cast<const uint16_t*>(st + S::O_VS) + R1 * G::NG, bf);
+          lds_scales<G::NG>(vb1, reinterpret_cast<const uint16_t*>(st + S::O_VB) + R1 * G::NG, bf);
+          const int vr = r_base + kk * 16 + 2 * t;
+#pragma unroll
+          for (int grp = 0; grp < G::NG; grp++) {
+            uint32_t bfr[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+              // p == 0 for masked rows: select, never multiply stale scales.
+              const float p0 = pr[kk][nt][0], p1 = pr[kk][nt][1], p2 = pr[kk][nt][2],
+                          p3 = pr[kk][nt][3];
+              float q0, q1, q2, q3;
+              if (fast) {
+                pb[nt][grp][0] = fmaf(p0, vb0[grp], fmaf(p2, vb1[grp], pb[nt][grp][0]));
+                pb[nt][grp][1] = fmaf(p1, vb0[grp], fmaf(p3, vb1[grp], pb[nt][grp][1]));
+                q0 = p0 * vs0[grp];
+                q1 = p1 * vs0[grp];
+                q2 = p2 * vs1[grp];
+                q3 = p3 * vs1[grp];
+              } else {
+                pb[nt][grp][0] += (p0 != 0.0f ? p0 * vb0[grp] : 0.0f) + (p2 != 0.0f ? p2 * vb1[grp] : 0.0f);
+                pb[nt][grp][1] += (p1 != 0.0f ? p1 * vb0[grp] : 0.0f) + (p3 != 0.0f ? p3 * vb1[grp] : 0.0f);
+                q0 = p0 != 0.0f ? p0 * vs0[grp] : 0.0f;
+                q1 = p1 != 0.0f ? p1 * vs0[grp] : 0.0f;
+                q2 = p2 != 0.0f ? p2 * vs1[grp] : 0.0f;
+                q3 = p3 != 0.0f ? p3 * vs1[grp] : 0.0f;
+              }
+              bfr[nt][0] = movmatrix_t(pack_h2(q0, q1));
+              bfr[nt][1] = movmatrix_t(pack_h2(q2, q3));
+            }
+            uint32_t vw[4][G::VW];
+            const uint8_t* vrow = st + S::O_VP + grp * G::GB + g * G::VB;
+            lds_words<G::VB>(vw[0], vrow + (vr)*G::KRB);
+            lds_words<G::VB>(vw[1], vrow + (vr + 1) * G::KRB);
+            lds_words<G::VB>(vw[2], vrow + (vr + 8) * G::KRB);
+            lds_words<G::VB>(vw[3], vrow + (vr + 9) * G::KRB);
+            uint32_t af[G::MTG][4];
+#pragma unroll
+            for (int cc = 0; cc < G::C; cc++) {
+              const uint32_t sel = (cc & 1) ? 0x7632u : 0x5410u;
+              const uint32_t Tlo = prmt(vw[0][cc / 2], vw[1][cc / 2], sel);
+              const uint32_t Thi = prmt(vw[2][cc / 2], vw[3][cc / 2], sel);
+#pragma unroll
+              for (int j = 0; j < G::E; j++) {
+                const int sl = cc * G::E + j;
+                const int mt = sl % G::MTG, half = sl / G::MTG;
+                af[mt][half] = v_extract<BITS>(Tlo, j);      // a0 (m-row g) / a1 (m-row g+8)
+                af[mt][2 + half] = v_extract<BITS>(Thi, j);  // a2 / a3
+              }
+            }
+#pragma unroll
+            for (int mt = 0; mt < G::MTG; mt++)
+#pragma unroll
+              for (int nt = 0; nt < NT; nt++)
+                mma16816(o_acc[grp * G::MTG + mt][nt], af[mt], bfr[nt][0], bfr[nt][1]);
+          }
         }
       }
-#pragma unroll
-      for (int mt = 0; mt < G::MTG; mt++)
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-          mma16816(o_acc[grp * G::MTG + mt][nt], af[mt], bfr[nt][0], bfr[nt][1]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if (lane == 0 && i + STAGES < my_tiles) issue(i + STAGES);
   }
   if (hung && lane == 0) atomicExch(p.err, 1);
 
-  // ---- finish the warp: reduce row-lane partials, fold bias sums ----
+  // ---- finish each consumer warp: reduce row-lane partials, fold bias sums ----
 #pragma unroll
   for (int nt = 0; nt < NT; nt++)
 #pragma unroll
@@ -604,33 +724,35 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
         pb[nt][grp][hh] = v;
       }
     }
-  __syncthreads();  // all warps done with their stages: reuse as merge buffer
-  float* wo = mrg + warp * HQ * (D + 2);  // [HQ][D] then m[HQ], l[HQ]
+  __syncthreads();  // every stage consumed: reuse the ring as the merge buffer
+  if (!producer) {
+    float* wo = mrg + warp * HQ * (D + 2);  // [HQ][D] then m[HQ], l[HQ]
 #pragma unroll
-  for (int mtg = 0; mtg < G::MT; mtg++) {
-    const int grp = mtg / G::MTG, mt = mtg % G::MTG;
-    const float fac = (BITS == 4 && (mt & 1)) ? 0.0625f : 1.0f;
+    for (int mtg = 0; mtg < G::MT; mtg++) {
+      const int grp = mtg / G::MTG, mt = mtg % G::MTG;
+      const float fac = (BITS == 4 && (mt & 1)) ? 0.0625f : 1.0f;
 #pragma unroll
-    for (int half = 0; half < 2; half++) {
-      const int sl = half * G::MTG + mt;
-      const int c = sl / G::E, j = sl % G::E;
-      const int d = grp * GS + (g * G::C + c) * G::E + j;
+      for (int half = 0; half < 2; half++) {
+        const int sl = half * G::MTG + mt;
+        const int cc = sl / G::E, j = sl % G::E;
+        const int d = grp * GS + (g * G::C + cc) * G::E + j;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++)
+            wo[(nt * 8 + 2 * t + hh) * D + d] =
+                o_acc[mtg][nt][half * 2 + hh] * fac + pb[nt][grp][hh];
+      }
+    }
+    if (g == 0) {
 #pragma unroll
       for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++)
-          wo[(nt * 8 + 2 * t + hh) * D + d] =
-              o_acc[mtg][nt][half * 2 + hh] * fac + pb[nt][grp][hh];
+        for (int hh = 0; hh < 2; hh++) {
+          wo[HQ * D + nt * 8 + 2 * t + hh] = m_run[nt][hh];
+          wo[HQ * D + HQ + nt * 8 + 2 * t + hh] = l_run[nt][hh];
+        }
     }
-  }
-  if (g == 0) {
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int hh = 0; hh < 2; hh++) {
-        wo[HQ * D + nt * 8 + 2 * t + hh] = m_run[nt][hh];
-        wo[HQ * D + HQ + nt * 8 + 2 * t + hh] = l_run[nt][hh];
-      }
   }
   __syncthreads();
 
@@ -638,7 +760,7 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
   const int rows_here = min(HQ, qrows - qr0);
   const int64_t cta = ((int64_t)b * p.Hkv + kvh) * p.QB + qb;
   const bool single = nact == 1;
-  for (int i = tid; i < rows_here * D; i += W * 32) {
+  for (int i = tid; i < rows_here * D; i += (W + 1) * 32) {
     const int r = i / D, d = i - r * D;
     float M = kNeg;
 #pragma unroll
@@ -647,7 +769,7 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
 #pragma unroll
     for (int w = 0; w < W; w++) {
       const float* ww = mrg + w * HQ * (D + 2);
-      const float e = exp2f((ww[HQ * D + r] - M) * kLog2e);
+      const float e = ex2((ww[HQ * D + r] - M) * kLog2e);
       Lsum += ww[HQ * D + HQ + r] * e;
       O += ww[r * D + d] * e;
     }
@@ -684,7 +806,7 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
   __syncthreads();
   if (!ctrl[0]) return;
   __threadfence();
-  for (int i = tid; i < rows_here * D; i += W * 32) {
+  for (int i = tid; i < rows_here * D; i += (W + 1) * 32) {
     const int r = i / D, d = i - r * D;
     float M = kNeg;
     for (int sp = 0; sp < nact; sp++)
@@ -692,7 +814,7 @@ __global__ void __launch_bounds__(W * 32) attn_kernel(const Params p) {
     float Lsum = 0.0f, O = 0.0f;
     for (int sp = 0; sp < nact; sp++) {
       const int64_t slot = (cta * p.nsplit + sp) * HQ + r;
-      const float e = exp2f((__ldcg(&p.ws_ml[slot * 2]) - M) * kLog2e);
+      const float e = ex2((__ldcg(&p.ws_ml[slot * 2]) - M) * kLog2e);
       Lsum += __ldcg(&p.ws_ml[slot * 2 + 1]) * e;
       O += __ldcg(&p.ws_o[slot * D + d]) * e;
     }
@@ -722,7 +844,7 @@ __global__ void merge_kernel(const float* __restrict__ m, const float* __restric
   for (int pp = 0; pp < parts; pp++) M = fmaxf(M, m[pp * ps + r]);
   float Ls = 0.0f, O = 0.0f;
   for (int pp = 0; pp < parts; pp++) {
-    const float e = exp2f((m[pp * ps + r] - M) * kLog2e);
+    const float e = ex2((m[pp * ps + r] - M) * kLog2e);
     Ls += l[pp * ps + r] * e;
     O += o[pp * ps + (int64_t)r * D + d] * e;
   }
@@ -736,11 +858,18 @@ __global__ void fill_kernel(float* __restrict__ p, int64_t n, float v) {
 
 // ------------------------------------------------------------ host side --
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 4;  // consumer warps per CTA (+1 producer)
 
-template <int BITS, int D, int GS>
+// Rows per consumer slice: 32 when registers allow, else 16.
+template <int D, int NT>
+constexpr int rows_per_warp() {
+  return (D * NT <= 128) ? 32 : 16;
+}
+
+template <int BITS, int D, int GS, int RW>
 constexpr int stages_for() {
-  return Geo<BITS, D, GS>::STAGE <= 4096 ? 4 : (Geo<BITS, D, GS>::STAGE <= 8192 ? 3 : 2);
+  constexpr int stage = kWarps * RW * Geo<BITS, D, GS>::ROWB;
+  return stage <= 12 * 1024 ? 4 : (stage <= 24 * 1024 ? 3 : 2);
 }
 
 struct LaunchShape {
@@ -760,18 +889,21 @@ int num_sms(int dev) {
   return g_num_sms[dev];
 }
 
+// Key split: enough CTAs for a few resident waves; splits are a multiple of
+// the largest chunk (128 key rows) so every split streams whole chunks.
 LaunchShape shape_for(int B, int Hkv, int nrep, int L, int N, int NT, int sms) {
   LaunchShape s;
   const int HQ = 8 * NT;
+  const int CH = kWarps * 32;
   s.QB = (nrep * L + HQ - 1) / HQ;
   const int64_t units = (int64_t)B * Hkv * s.QB;
-  const int64_t target = (int64_t)sms * 8;  // ~2 waves of 4 resident CTAs per SM
+  const int64_t target = (int64_t)sms * 6;
   int nsplit = (int)std::max<int64_t>(1, (target + units - 1) / units);
-  const int min_rows = kTile * kWarps * 2;
+  const int min_rows = 2 * CH;
   nsplit = std::min(nsplit, std::max(1, (N + min_rows - 1) / min_rows));
   int rps = (N + nsplit - 1) / nsplit;
-  rps = (rps + kTile * kWarps - 1) / (kTile * kWarps) * (kTile * kWarps);
-  if (rps <= 0) rps = kTile * kWarps;
+  rps = (rps + CH - 1) / CH * CH;
+  if (rps <= 0) rps = CH;
   s.rps = rps;
   s.nsplit = std::max(1, (N + rps - 1) / rps);
   return s;
@@ -794,9 +926,10 @@ size_t ws_bytes_for(int B, int Hkv, const LaunchShape& s, int NT, int D) {
 
 template <int BITS, int D, int GS, int NT>
 int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st) {
-  constexpr int ST = stages_for<BITS, D, GS>();
-  using SM = Smem<BITS, D, GS, NT, kWarps, ST>;
-  auto kern = attn_kernel<BITS, D, GS, NT, kWarps, ST>;
+  constexpr int RW = rows_per_warp<D, NT>();
+  constexpr int ST = stages_for<BITS, D, GS, RW>();
+  using SM = Smem<BITS, D, GS, NT, kWarps, RW, ST>;
+  auto kern = attn_kernel<BITS, D, GS, NT, kWarps, RW, ST>;
   static bool configured[64] = {false};
   int dev = 0;
   KVQ_CUDA_TRY(cudaGetDevice(&dev));
@@ -805,7 +938,7 @@ int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st) {
     configured[dev] = true;
   }
   const dim3 grid(s.nsplit, p.Hkv * s.QB, B);
-  kern<<<grid, kWarps * 32, SM::TOTAL, st>>>(p);
+  kern<<<grid, (kWarps + 1) * 32, SM::TOTAL, st>>>(p);
   KVQ_CUDA_TRY(cudaGetLastError());
   return KVQ_OK;
 }
