@@ -1,837 +1,10 @@
-// kvq_attn.cu — attention over MLX affine-quantized K/V for sm_100a.
-//
-// One kernel serves decode (L = 1), the context-split partial form and an
-// interim chunked prefill.  Work unit: a CTA owns one (batch, kv head, block
-// of 8*NT query rows, key split).  Query rows are (position, head) pairs of
-// the GQA group (row qr -> position qr / nrep, head qr % nrep), so every K/V
-// byte a CTA streams serves all query heads that share it.
-//
-// CTA = W consumer warps + 1 producer warp (warp specialised):
-//   * the producer streams the split's key rows in chunks of CH = W*RW rows:
-//     six TMA bulk copies (cp.async.bulk, 1-D) per chunk — packed K, K
-//     scales, K biases, packed V, V scales, V biases, each a contiguous row
-//     range of one (b, h) — into a STAGES-deep shared-memory ring, with one
-//     `full` mbarrier (transaction bytes) and one `empty` mbarrier (W
-//     consumer arrivals) per stage.  Every wait is bounded: on timeout the
-//     kernel raises a device error flag and leaves its loops.
-//   * consumer warp w takes rows [w*RW, (w+1)*RW) of every chunk.
-// Per consumer slice (RW = 16 or 32 key rows):
-//   * codes become exact fp16 integers in registers with the 0x6400 (=1024)
-//     magic: (bits | 0x6400) - 1024 = c.  Four-bit codes in odd nibbles are
-//     taken unshifted (1024 + 16c) and the factor 16 is folded into the
-//     query.  Scales and biases are factored out of the inner products
-//     (qdot factoring, as in mlx-bun's Metal decode kernel,
-//     src/model/fused-decode-kernel.ts:62-114):
-//        q . (s*c + b) = s * (q . c) + b * sum(q)
-//        sum_n p_n (s_n c_n + b_n) = sum_n (p_n s_n) c_n + sum_n p_n b_n
-//   * QK^T: mma.m16n8k16, key rows as M (codes as A, pairs along d), query
-//     rows as N (8 per n-tile; q as B, loaded once per CTA), d as K; one
-//     accumulator per quantisation group.
-//   * online softmax in f32 with ex2.approx; scores are first rounded to the
-//     cache dtype, as the reference graph rounds them
-//     (src/model/gemma4-base.ts:1307).
-//   * PV: O^T[d x q] += V^T[d x n] (p*s)^T[n x q]; the probability tile goes
-//     from the QK accumulator layout to the B-operand layout with one
-//     movmatrix.trans per 8x8 block; V codes of a (d, 2 rows) pair are
-//     interleaved with one prmt per 16-bit chunk and made exact with one
-//     f16x2 subtract.
-//   * splits of the key range merge in fixed order (deterministic) in the
-//     last CTA to finish, found by an atomic ticket — no second launch.
-//
-// Tensor-core choice: decode is HBM-bound with at most 16 query rows per kv
-// head, so the register-sourced mma.sync keeps the dequantised codes in
-// registers (no shared-memory round trip); tensor throughput is not the
-// limit (2 MMAs per key row).
-#include <cuda_bf16.h>
-#include <cuda_fp16.h>
-
-#include <algorithm>
-
-#include "kvq_internal.h"
+// kvq_attn.cu — host side of the attention entry points: argument checks,
+// launch shapes, workspace, split merge kernel and debug scores.  The kernel
+// itself is kvq_attn_impl.cuh, instantiated in kvq_attn_b4.cu / kvq_attn_b8.cu.
+#include "kvq_attn_impl.cuh"
 
 namespace kvq {
-namespace {
-
-constexpr float kNeg = -1.0e30f;             // finite "minus infinity" for masked logits
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kTile = 16;                     // rows per MMA tile; row-alignment unit
-constexpr long long kWaitLimit = 1ll << 30;   // mbarrier polls before declaring a hang
-constexpr uint64_t kWaitNs = 2000000000ull;   // ... or 2 s of %globaltimer, whichever first
-
-struct Params {
-  const uint8_t* kp;
-  const uint16_t* ks;
-  const uint16_t* kb;
-  const uint8_t* vp;
-  const uint16_t* vs;
-  const uint16_t* vb;
-  int64_t k_bstride, k_hstride, v_bstride, v_hstride;  // rows
-  const uint16_t* q;     // [B, Hq, L, D]
-  uint16_t* out;         // [B, Hq, L, D] (mode 0)
-  float* pm;             // mode 1 partials [B*Hq]
-  float* pl;
-  float* po;             // [B*Hq, D]
-  float* ws_o;           // split partials
-  float* ws_ml;
-  unsigned* counters;
-  const int32_t* seq_lens;
-  int* err;
-  float* scores;         // debug: rounded logits [B, Hq, L, N] (nullable)
-  int Hq, Hkv, nrep, N, L, QB, rps, nsplit, mode, mask_mode, window;
-  float scale;
-  int bf16;
-};
-
-// ---------------------------------------------------------------- PTX ----
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bounded wait; false on timeout (the caller raises the device error flag).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (long long i = 0; i < kWaitLimit; i++) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 255 && global_ns() - t0 > kWaitNs) return false;
-  }
-  return false;
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
-                                         uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
-  uint32_t y;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-  return r;
-}
-
-// (x as f16x2) - (1024, 1024): exact integer codes from the 0x6400 magic.
-__device__ __forceinline__ uint32_t sub1024(uint32_t x) {
-  uint32_t r;
-  asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(0x64006400u));
-  return r;
-}
-
-// 2^x (approximate; flushes results below 2^-126 to zero).
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-  const __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-__device__ __forceinline__ float dt_to_f(uint16_t v, int bf16) {
-  return bf16 ? __uint_as_float((uint32_t)v << 16) : __half2float(__ushort_as_half(v));
-}
-
-__device__ __forceinline__ uint16_t f_to_dt(float f, int bf16) {
-  return bf16 ? __bfloat16_as_ushort(__float2bfloat16_rn(f)) : __half_as_ushort(__float2half_rn(f));
-}
-
-__device__ __forceinline__ float round_dt(float f, int bf16) {
-  return bf16 ? __bfloat162float(__float2bfloat16_rn(f)) : __half2float(__float2half_rn(f));
-}
-
-// K operand (pairs along d within one row), exact: a 4-bit word w holds
-// nibbles e0..e7: x0 = (e0, e4), x1 = 16*(e1, e5), x2 = (e2, e6), x3 =
-// 16*(e3, e7); an 8-bit word: x0 = (b0, b1), x1 = (b2, b3).  (Keeping the
-// 1024 offset and cancelling it in the accumulator loses ~10 bits of the
-// 4-bit products, enough to flip the dtype rounding of large logits.)
-template <int BITS>
-__device__ __forceinline__ uint32_t k_extract(uint32_t w, int x) {
-  if (BITS == 4) {
-    const uint32_t s = (x >= 2) ? (w >> 8) : w;
-    const uint32_t m = (x & 1) ? 0x00F000F0u : 0x000F000Fu;
-    return sub1024((s & m) | 0x64006400u);
-  } else {
-    return sub1024(prmt(w, 0x64u, x ? 0x4342u : 0x4140u));
-  }
-}
-
-// V operand: T holds a 16-bit chunk of row r0 (low half) and of row r1 (high
-// half); element j of the chunk as the exact pair (r0, r1).
-template <int BITS>
-__device__ __forceinline__ uint32_t v_extract(uint32_t T, int j) {
-  if (BITS == 4) {
-    const uint32_t s = (j >= 2) ? (T >> 8) : T;
-    const uint32_t m = (j & 1) ? 0x00F000F0u : 0x000F000Fu;
-    return sub1024((s & m) | 0x64006400u);
-  } else {
-    return sub1024(prmt(T, 0x64u, j ? 0x4341u : 0x4240u));
-  }
-}
-
-template <int NBYTES>
-__device__ __forceinline__ void lds_words(uint32_t* w, const uint8_t* p) {
-  if (NBYTES == 2) {
-    w[0] = *reinterpret_cast<const uint16_t*>(p);
-  } else if (NBYTES == 4) {
-    w[0] = *reinterpret_cast<const uint32_t*>(p);
-  } else if (NBYTES == 8) {
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
-    w[0] = u.x;
-    w[1] = u.y;
-  } else {
-#pragma unroll
-    for (int i = 0; i < NBYTES / 16; i++) {
-      const uint4 u = *reinterpret_cast<const uint4*>(p + 16 * i);
-      w[4 * i] = u.x;
-      w[4 * i + 1] = u.y;
-      w[4 * i + 2] = u.z;
-      w[4 * i + 3] = u.w;
-    }
-  }
-}
-
-// All NG scales (or biases) of one row as f32.
-template <int NG>
-__device__ __forceinline__ void lds_scales(float* out, const uint16_t* row, int bf) {
-  uint32_t w[(NG + 1) / 2];
-  lds_words<NG * 2>(w, reinterpret_cast<const uint8_t*>(row));
-#pragma unroll
-  for (int i = 0; i < NG; i++) {
-    const uint16_t h = (uint16_t)((i & 1) ? (w[i / 2] >> 16) : (w[i / 2] & 0xffffu));
-    out[i] = dt_to_f(h, bf);
-  }
-}
-
-template <int BITS, int D, int GS>
-struct Geo {
-  static constexpr int NG = D / GS;             // quantisation groups per row
-  static constexpr int KRB = D * BITS / 8;      // packed bytes per row
-  static constexpr int SRB = NG * 2;            // scale (or bias) bytes per row
-  static constexpr int GB = GS * BITS / 8;      // packed bytes per group
-  static constexpr int KB = GS * BITS / 32;     // K bytes per lane per (row, group)
-  static constexpr int KW = KB / 4;             // ... as words
-  static constexpr int E = BITS == 4 ? 4 : 2;   // elements per 16-bit chunk
-  static constexpr int C = GS / 8 / E;          // 16-bit V chunks per lane per (row, group)
-  static constexpr int VB = 2 * C;              // V bytes per lane per (row, group)
-  static constexpr int VW = (VB + 3) / 4;
-  static constexpr int MTG = GS / 16;           // PV m-tiles (16 d) per group
-  static constexpr int KSTEPS = D / 16;
-  static constexpr int MT = D / 16;
-  static constexpr int ROWB = 2 * KRB + 4 * SRB;  // bytes per key row (K and V triples)
-  static_assert(KB >= 4, "unsupported group size / bits");
-};
-
-template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
-struct Smem {
-  using G = Geo<BITS, D, GS>;
-  static constexpr int HQ = 8 * NT;
-  static constexpr int CH = W * RW;                            // key rows per chunk
-  static constexpr int O_KP = 0;                               // offsets inside a stage
-  static constexpr int O_KS = O_KP + CH * G::KRB;
-  static constexpr int O_KB = O_KS + CH * G::SRB;
-  static constexpr int O_VP = O_KB + CH * G::SRB;
-  static constexpr int O_VS = O_VP + CH * G::KRB;
-  static constexpr int O_VB = O_VS + CH * G::SRB;
-  static constexpr int STAGE = O_VB + CH * G::SRB;
-  static constexpr int Q_F = 0;                                // f32 [HQ][D]
-  static constexpr int QSUM = Q_F + HQ * D * 4;                // f32 [HQ][NG]
-  static constexpr int BARS = (QSUM + HQ * G::NG * 4 + 15) / 16 * 16;  // full[ST], empty[ST]
-  static constexpr int CTRL = BARS + 2 * STAGES * 8;
-  static constexpr int STAGES_OFF = (CTRL + 16 + 127) / 128 * 128;
-  static constexpr int STAGE_BYTES = STAGES * STAGE;
-  static constexpr int MERGE_BYTES = W * HQ * (D + 2) * 4;
-  static constexpr int TOTAL =
-      STAGES_OFF + (STAGE_BYTES > MERGE_BYTES ? STAGE_BYTES : MERGE_BYTES);
-  static_assert((CH * G::SRB) % 16 == 0, "scale rows must tile in 16-byte units");
-};
-
-template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
-__global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
-  using G = Geo<BITS, D, GS>;
-  using S = Smem<BITS, D, GS, NT, W, RW, STAGES>;
-  constexpr int HQ = S::HQ;
-  constexpr int CH = S::CH;
-  constexpr int MTS = RW / 16;  // 16-row m-tiles per consumer slice
-  extern __shared__ __align__(128) uint8_t smem[];
-  float* q_f = reinterpret_cast<float*>(smem + S::Q_F);
-  float* qsum = reinterpret_cast<float*>(smem + S::QSUM);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BARS);
-  uint64_t* empty = full + STAGES;
-  int* ctrl = reinterpret_cast<int*>(smem + S::CTRL);
-  uint8_t* stages = smem + S::STAGES_OFF;
-  float* mrg = reinterpret_cast<float*>(smem + S::STAGES_OFF);  // aliases stages after the loop
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
-  const bool producer = warp == W;
-  const int split = blockIdx.x;
-  const int kvh = blockIdx.y % p.Hkv;
-  const int qb = blockIdx.y / p.Hkv;
-  const int b = blockIdx.z;
-  const int nrep = p.nrep, L = p.L, bf = p.bf16;
-  const int qrows = nrep * L;
-  const int qr0 = qb * HQ;
-
-  int Nb = p.N;
-  if (p.seq_lens) Nb = min(max(p.seq_lens[b], 0), p.N);
-
-  // Key range of this query block (union over its rows), then this split's share.
-  int lo = 0, hi = Nb;
-  if (p.mask_mode == 1) {
-    const int qr_last = min(qr0 + HQ, qrows) - 1;
-    const int pos_first = Nb - L + qr0 / nrep, pos_last = Nb - L + qr_last / nrep;
-    hi = min(Nb, pos_last + 1);
-    if (p.window > 0) lo = max(0, pos_first - p.window + 1) / kTile * kTile;
-    if (hi < lo) hi = lo;
-  }
-  const int nact = max(1, (hi - lo + p.rps - 1) / p.rps);
-  if (split >= nact) return;
-  const int n0 = lo + split * p.rps;
-  const int n1 = min(n0 + p.rps, hi);
-  const int nchunks = (n1 - n0 + CH - 1) / CH;
-
-  if (tid == 0) {
-    for (int s = 0; s < STAGES; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], W);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  // Causal bounds shared by every column of the block (fast-path test).
-  int kz_min = Nb - 1, ka_max = 0;
-  if (p.mask_mode == 1) {
-    const int qr_last = min(qr0 + HQ, qrows) - 1;
-    kz_min = min(kz_min, Nb - L + qr0 / nrep);
-    if (p.window > 0) ka_max = max(0, Nb - L + qr_last / nrep - p.window + 1);
-  }
-  __syncthreads();
-
-  bool hung = false;
-  const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
-  const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
-  // Producer: one chunk of CH key rows into stage c % STAGES.  Stages are
-  // only reused after the `empty` barrier shows all consumers are done.
-  auto produce = [&](int c) -> bool {
-    const int s = c % STAGES;
-    if (c >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1))) return false;
-    const int64_t row = n0 + (int64_t)c * CH;
-    const int rows = min(CH, n1 - (int)(row));
-    const uint32_t cr = (uint32_t)((rows + kTile - 1) / kTile * kTile);
-    uint8_t* st = stages + s * S::STAGE;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(&full[s], cr * G::ROWB);
-    bulk_g2s(st + S::O_KP, p.kp + (kbase + row) * G::KRB, cr * G::KRB, &full[s]);
-    bulk_g2s(st + S::O_KS, p.ks + (kbase + row) * G::NG, cr * G::SRB, &full[s]);
-    bulk_g2s(st + S::O_KB, p.kb + (kbase + row) * G::NG, cr * G::SRB, &full[s]);
-    bulk_g2s(st + S::O_VP, p.vp + (vbase + row) * G::KRB, cr * G::KRB, &full[s]);
-    bulk_g2s(st + S::O_VS, p.vs + (vbase + row) * G::NG, cr * G::SRB, &full[s]);
-    bulk_g2s(st + S::O_VB, p.vb + (vbase + row) * G::NG, cr * G::SRB, &full[s]);
-    return true;
-  };
-  // Prologue before any block-wide barrier: fill the ring (no waits needed).
-  if (producer && lane == 0)
-    for (int c = 0; c < STAGES && c < nchunks; c++) produce(c);
-
-  // ---- stage the query block: q * dtype(scale), rounded to dtype ----
-  const float scale_dt = round_dt(p.scale, bf);
-  for (int i = tid; i < HQ * D; i += (W + 1) * 32) {
-    const int r = i / D, d = i - r * D;
-    const int qr = qr0 + r;
-    float v = 0.0f;
-    if (qr < qrows) {
-      const int l = qr / nrep, hh = qr - l * nrep;
-      const int hq = kvh * nrep + hh;
-      const uint16_t raw = p.q[(((int64_t)b * p.Hq + hq) * L + l) * D + d];
-      v = round_dt(dt_to_f(raw, bf) * scale_dt, bf);
-    }
-    q_f[i] = v;
-  }
-  __syncthreads();
-  for (int i = tid; i < HQ * G::NG; i += (W + 1) * 32) {
-    const int r = i / G::NG, grp = i - r * G::NG;
-    float s = 0.0f;
-    for (int d = 0; d < GS; d++) s += q_f[r * D + grp * GS + d];
-    qsum[i] = s;
-  }
-  __syncthreads();
-
-  float m_run[NT][2], l_run[NT][2], pb[NT][G::NG][2];
-  float o_acc[G::MT][NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-      m_run[nt][hh] = kNeg;
-      l_run[nt][hh] = 0.0f;
-#pragma unroll
-      for (int grp = 0; grp < G::NG; grp++) pb[nt][grp][hh] = 0.0f;
-    }
-#pragma unroll
-  for (int mt = 0; mt < G::MT; mt++)
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int c = 0; c < 4; c++) o_acc[mt][nt][c] = 0.0f;
-
-  if (producer) {
-    // ---------------- producer: keep the ring full ----------------
-    if (lane == 0)
-      for (int c = STAGES; c < nchunks; c++)
-        if (!produce(c)) {
-          hung = true;
-          break;
-        }
-  } else {
-    // ---- query fragments (B operand of QK), loaded once ----
-    uint32_t qbf[G::KSTEPS][NT][2];
-#pragma unroll
-    for (int kk = 0; kk < G::KSTEPS; kk++) {
-      const int grp = kk / G::MTG, kin = kk % G::MTG;
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++) {
-        const float* qrow = q_f + (nt * 8 + g) * D;
-#pragma unroll
-        for (int w2 = 0; w2 < 2; w2++) {
-          const int v = 2 * kin + w2;
-          int d_lo, d_hi;
-          float f = 1.0f;
-          if (BITS == 4) {
-            const int wi = v / 4, x = v % 4;
-            const int base = grp * GS + t * (GS / 4) + 8 * wi;
-            d_lo = base + x;
-            d_hi = base + x + 4;
-            if (x & 1) f = 0.0625f;
-          } else {
-            const int wi = v / 2, x = v % 2;
-            const int base = grp * GS + t * (GS / 4) + 4 * wi;
-            d_lo = base + 2 * x;
-            d_hi = base + 2 * x + 1;
-          }
-          qbf[kk][nt][w2] = pack_h2(qrow[d_lo] * f, qrow[d_hi] * f);
-        }
-      }
-    }
-    float qs_r[NT][G::NG][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int grp = 0; grp < G::NG; grp++)
-#pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-          qs_r[nt][grp][hh] = qsum[(nt * 8 + 2 * t + hh) * G::NG + grp];
-        }
-
-    // Key-index limits of this lane's query columns (inclusive bounds).
-    int klo[NT][2], khi[NT][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int hh = 0; hh < 2; hh++) {
-        const int qr = qr0 + nt * 8 + 2 * t + hh;
-        int a = 0, z = Nb - 1;
-        if (p.mask_mode == 1 && qr < qrows) {
-          const int pos = Nb - L + qr / nrep;
-          z = min(z, pos);
-          if (p.window > 0) a = max(0, pos - p.window + 1);
-        }
-        klo[nt][hh] = a;
-        khi[nt][hh] = z;
-      }
-
-    for (int c = 0; c < nchunks; c++) {
-      const int s = c % STAGES;
-      // The decision must be warp-uniform: the slice is full of warp-collective ops.
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)((c / STAGES) & 1)))) {
-        hung = true;
-        break;
-      }
-      const uint8_t* st = stages + s * S::STAGE;
-      const int srow0 = n0 + c * CH + warp * RW;  // first key row of this slice
-      if (srow0 < n1) {
-        const bool fast = !p.scores && srow0 + RW <= n1 && srow0 + RW - 1 <= kz_min &&
-                          srow0 >= ka_max;
-        const int r_base = warp * RW;  // slice rows inside the chunk
-
-        // ---------------- scores ----------------
-        float sc[MTS][NT][4];
-#pragma unroll
-        for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-          for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int cc = 0; cc < 4; cc++) sc[mt][nt][cc] = 0.0f;
-#pragma unroll
-        for (int mt = 0; mt < MTS; mt++) {
-          const int R0 = r_base + mt * 16 + g, R1 = R0 + 8;
-          float ks0[G::NG], kb0[G::NG], ks1[G::NG], kb1[G::NG];
-          lds_scales<G::NG>(ks0, reinterpret_cast<const uint16_t*>(st + S::O_KS) + R0 * G::NG, bf);
-          lds_scales<G::NG>(kb0, reinterpret_cast<const uint16_t*>(st + S::O_KB) + R0 * G::NG, bf);
-          lds_scales<G::NG>(ks1, reinterpret_cast<const uint16_t*>(st + S::O_KS) + R1 * G::NG, bf);
-          lds_scales<G::NG>(kb1, reinterpret_cast<const uint16_t*>(st + S::O_KB) + R1 * G::NG, bf);
-#pragma unroll
-          for (int grp = 0; grp < G::NG; grp++) {
-            uint32_t kw0[G::KW], kw1[G::KW];
-            lds_words<G::KB>(kw0, st + S::O_KP + R0 * G::KRB + grp * G::GB + t * G::KB);
-            lds_words<G::KB>(kw1, st + S::O_KP + R1 * G::KRB + grp * G::GB + t * G::KB);
-            float acc[NT][4];
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-              acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
-            }
-#pragma unroll
-            for (int kin = 0; kin < G::MTG; kin++) {
-              uint32_t a[4];
-#pragma unroll
-              for (int w2 = 0; w2 < 2; w2++) {
-                const int v = 2 * kin + w2;
-                const int wi = BITS == 4 ? v / 4 : v / 2;
-                const int x = BITS == 4 ? v % 4 : v % 2;
-                a[2 * w2] = k_extract<BITS>(kw0[wi], x);
-                a[2 * w2 + 1] = k_extract<BITS>(kw1[wi], x);
-              }
-#pragma unroll
-              for (int nt = 0; nt < NT; nt++)
-                mma16816(acc[nt], a, qbf[grp * G::MTG + kin][nt][0],
-                         qbf[grp * G::MTG + kin][nt][1]);
-            }
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-              sc[mt][nt][0] = fmaf(ks0[grp], acc[nt][0], fmaf(kb0[grp], qs_r[nt][grp][0], sc[mt][nt][0]));
-              sc[mt][nt][1] = fmaf(ks0[grp], acc[nt][1], fmaf(kb0[grp], qs_r[nt][grp][1], sc[mt][nt][1]));
-              sc[mt][nt][2] = fmaf(ks1[grp], acc[nt][2], fmaf(kb1[grp], qs_r[nt][grp][0], sc[mt][nt][2]));
-              sc[mt][nt][3] = fmaf(ks1[grp], acc[nt][3], fmaf(kb1[grp], qs_r[nt][grp][1], sc[mt][nt][3]));
-            }
-          }
-        }
-
-        // ---------------- online softmax ----------------
-        float pr[MTS][NT][4];
-        float alpha[NT][2];
-        bool rescale = false;
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-          for (int hh = 0; hh < 2; hh++) {
-            float x[MTS][2];
-            bool vv[MTS][2];
-#pragma unroll
-            for (int mt = 0; mt < MTS; mt++) {
-#pragma unroll
-              for (int e = 0; e < 2; e++) {
-                const int r = srow0 + mt * 16 + g + 8 * e;
-                const float rs = round_dt(sc[mt][nt][2 * e + hh], bf);
-                if (fast) {
-                  vv[mt][e] = true;
-                  x[mt][e] = rs;
-                } else {
-                  vv[mt][e] = r < n1 && r >= klo[nt][hh] && r <= khi[nt][hh];
-                  x[mt][e] = vv[mt][e] ? rs : kNeg;
-                  if (p.scores && vv[mt][e]) {
-                    const int qr = qr0 + nt * 8 + 2 * t + hh;
-                    if (qr < qrows) {
-                      const int l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
-                      p.scores[(((int64_t)b * p.Hq + hq) * L + l) * p.N + r] = rs;
-                    }
-                  }
-                }
-              }
-            }
-            float tm = x[0][0];
-#pragma unroll
-            for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-              for (int e = 0; e < 2; e++) tm = fmaxf(tm, x[mt][e]);
-            tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
-            tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
-            tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
-            const float mn = fmaxf(m_run[nt][hh], tm);
-            const float mls = mn * kLog2e;
-            // (m_old - m_new) first: exactly 0 when the max is unchanged, even at
-            // the -1e30 sentinel (an fma against the rounded product would leave
-            // its rounding residual, ~1e23 there, and 2^that is inf).
-            const float al = ex2((m_run[nt][hh] - mn) * kLog2e);
-            rescale |= (mn != m_run[nt][hh]);
-            alpha[nt][hh] = al;
-            float lsum = 0.0f;
-#pragma unroll
-            for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-              for (int e = 0; e < 2; e++) {
-                const float pe = ex2(fmaf(x[mt][e], kLog2e, -mls));
-                const float pv = (fast || vv[mt][e]) ? pe : 0.0f;
-                pr[mt][nt][2 * e + hh] = pv;
-                lsum += pv;
-              }
-            l_run[nt][hh] = fmaf(l_run[nt][hh], al, lsum);
-            m_run[nt][hh] = mn;
-          }
-        }
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-          for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-            for (int mt = 0; mt < G::MT; mt++) {
-              o_acc[mt][nt][0] *= alpha[nt][0];
-              o_acc[mt][nt][1] *= alpha[nt][1];
-              o_acc[mt][nt][2] *= alpha[nt][0];
-              o_acc[mt][nt][3] *= alpha[nt][1];
-            }
-#pragma unroll
-            for (int grp = 0; grp < G::NG; grp++) {
-              pb[nt][grp][0] *= alpha[nt][0];
-              pb[nt][grp][1] *= alpha[nt][1];
-            }
-          }
-        }
-
-        // ---------------- P V ----------------
-#pragma unroll
-        for (int kk = 0; kk < MTS; kk++) {  // 16-row k-steps of the slice
-          const int R0 = r_base + kk * 16 + g, R1 = R0 + 8;
-          float vs0[G::NG], vb0[G::NG], vs1[G::NG], vb1[G::NG];
-          lds_scales<G::NG>(vs0, reinterpret_cast<const uint16_t*>(st + S::O_VS) + R0 * G::NG, bf);
-          lds_scales<G::NG>(vb0, reinterpret_cast<const uint16_t*>(st + S::O_VB) + R0 * G::NG, bf);
-          lds_scales<G::NG>(vs1, reinterpret_cast<const uint16_t*>(st + S::O_VS) + R1 * G::NG, bf);
-          lds_scales<G::NG>(vb1, reinterpret_cast<const uint16_t*>(st + S::O_VB) + R1 * G::NG, bf);
-          const int vr = r_base + kk * 16 + 2 * t;
-#pragma unroll
-          for (int grp = 0; grp < G::NG; grp++) {
-            uint32_t bfr[NT][2];
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-              // p == 0 for masked rows: select, never multiply stale scales.
-              const float p0 = pr[kk][nt][0], p1 = pr[kk][nt][1], p2 = pr[kk][nt][2],
-                          p3 = pr[kk][nt][3];
-              float q0, q1, q2, q3;
-              if (fast) {
-                pb[nt][grp][0] = fmaf(p0, vb0[grp], fmaf(p2, vb1[grp], pb[nt][grp][0]));
-                pb[nt][grp][1] = fmaf(p1, vb0[grp], fmaf(p3, vb1[grp], pb[nt][grp][1]));
-                q0 = p0 * vs0[grp];
-                q1 = p1 * vs0[grp];
-                q2 = p2 * vs1[grp];
-                q3 = p3 * vs1[grp];
-              } else {
-                pb[nt][grp][0] += (p0 != 0.0f ? p0 * vb0[grp] : 0.0f) + (p2 != 0.0f ? p2 * vb1[grp] : 0.0f);
-                pb[nt][grp][1] += (p1 != 0.0f ? p1 * vb0[grp] : 0.0f) + (p3 != 0.0f ? p3 * vb1[grp] : 0.0f);
-                q0 = p0 != 0.0f ? p0 * vs0[grp] : 0.0f;
-                q1 = p1 != 0.0f ? p1 * vs0[grp] : 0.0f;
-                q2 = p2 != 0.0f ? p2 * vs1[grp] : 0.0f;
-                q3 = p3 != 0.0f ? p3 * vs1[grp] : 0.0f;
-              }
-              bfr[nt][0] = movmatrix_t(pack_h2(q0, q1));
-              bfr[nt][1] = movmatrix_t(pack_h2(q2, q3));
-            }
-            uint32_t vw[4][G::VW];
-            const uint8_t* vrow = st + S::O_VP + grp * G::GB + g * G::VB;
-            lds_words<G::VB>(vw[0], vrow + (vr)*G::KRB);
-            lds_words<G::VB>(vw[1], vrow + (vr + 1) * G::KRB);
-            lds_words<G::VB>(vw[2], vrow + (vr + 8) * G::KRB);
-            lds_words<G::VB>(vw[3], vrow + (vr + 9) * G::KRB);
-            uint32_t af[G::MTG][4];
-#pragma unroll
-            for (int cc = 0; cc < G::C; cc++) {
-              const uint32_t sel = (cc & 1) ? 0x7632u : 0x5410u;
-              const uint32_t Tlo = prmt(vw[0][cc / 2], vw[1][cc / 2], sel);
-              const uint32_t Thi = prmt(vw[2][cc / 2], vw[3][cc / 2], sel);
-#pragma unroll
-              for (int j = 0; j < G::E; j++) {
-                const int sl = cc * G::E + j;
-                const int mt = sl % G::MTG, half = sl / G::MTG;
-                af[mt][half] = v_extract<BITS>(Tlo, j);      // a0 (m-row g) / a1 (m-row g+8)
-                af[mt][2 + half] = v_extract<BITS>(Thi, j);  // a2 / a3
-              }
-            }
-#pragma unroll
-            for (int mt = 0; mt < G::MTG; mt++)
-#pragma unroll
-              for (int nt = 0; nt < NT; nt++)
-                mma16816(o_acc[grp * G::MTG + mt][nt], af[mt], bfr[nt][0], bfr[nt][1]);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-  }
-  if (hung && lane == 0) atomicExch(p.err, 1);
-
-  // ---- finish each consumer warp: reduce row-lane partials, fold bias sums ----
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-      float l = l_run[nt][hh];
-      l += __shfl_xor_sync(0xffffffffu, l, 4);
-      l += __shfl_xor_sync(0xffffffffu, l, 8);
-      l += __shfl_xor_sync(0xffffffffu, l, 16);
-      l_run[nt][hh] = l;
-#pragma unroll
-      for (int grp = 0; grp < G::NG; grp++) {
-        float v = pb[nt][grp][hh];
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        v += __shfl_xor_sync(0xffffffffu, v, 8);
-        v += __shfl_xor_sync(0xffffffffu, v, 16);
-        pb[nt][grp][hh] = v;
-      }
-    }
-  __syncthreads();  // every stage consumed: reuse the ring as the merge buffer
-  if (!producer) {
-    float* wo = mrg + warp * HQ * (D + 2);  // [HQ][D] then m[HQ], l[HQ]
-#pragma unroll
-    for (int mtg = 0; mtg < G::MT; mtg++) {
-      const int grp = mtg / G::MTG, mt = mtg % G::MTG;
-      const float fac = (BITS == 4 && (mt & 1)) ? 0.0625f : 1.0f;
-#pragma unroll
-      for (int half = 0; half < 2; half++) {
-        const int sl = half * G::MTG + mt;
-        const int cc = sl / G::E, j = sl % G::E;
-        const int d = grp * GS + (g * G::C + cc) * G::E + j;
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-          for (int hh = 0; hh < 2; hh++)
-            wo[(nt * 8 + 2 * t + hh) * D + d] =
-                o_acc[mtg][nt][half * 2 + hh] * fac + pb[nt][grp][hh];
-      }
-    }
-    if (g == 0) {
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-          wo[HQ * D + nt * 8 + 2 * t + hh] = m_run[nt][hh];
-          wo[HQ * D + HQ + nt * 8 + 2 * t + hh] = l_run[nt][hh];
-        }
-    }
-  }
-  __syncthreads();
-
-  // ---- combine warps; write the CTA partial or the final result ----
-  const int rows_here = min(HQ, qrows - qr0);
-  const int64_t cta = ((int64_t)b * p.Hkv + kvh) * p.QB + qb;
-  const bool single = nact == 1;
-  for (int i = tid; i < rows_here * D; i += (W + 1) * 32) {
-    const int r = i / D, d = i - r * D;
-    float M = kNeg;
-#pragma unroll
-    for (int w = 0; w < W; w++) M = fmaxf(M, mrg[w * HQ * (D + 2) + HQ * D + r]);
-    float Lsum = 0.0f, O = 0.0f;
-#pragma unroll
-    for (int w = 0; w < W; w++) {
-      const float* ww = mrg + w * HQ * (D + 2);
-      const float e = ex2((ww[HQ * D + r] - M) * kLog2e);
-      Lsum += ww[HQ * D + HQ + r] * e;
-      O += ww[r * D + d] * e;
-    }
-    const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
-    const int64_t orow = ((int64_t)b * p.Hq + hq) * L + l;
-    if (single) {
-      if (p.mode == 0) {
-        p.out[orow * D + d] = f_to_dt(Lsum > 0.0f ? O / Lsum : 0.0f, bf);
-      } else {
-        p.po[orow * D + d] = O;
-        if (d == 0) {
-          p.pm[orow] = M;
-          p.pl[orow] = Lsum;
-        }
-      }
-    } else {
-      const int64_t slot = (cta * p.nsplit + split) * HQ + r;
-      p.ws_o[slot * D + d] = O;
-      if (d == 0) {
-        p.ws_ml[slot * 2] = M;
-        p.ws_ml[slot * 2 + 1] = Lsum;
-      }
-    }
-  }
-  if (single) return;
-
-  // ---- last CTA of this (b, kv head, query block) merges the splits ----
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned prev = atomicAdd(&p.counters[cta], 1u);
-    ctrl[0] = (prev == (unsigned)(nact - 1)) ? 1 : 0;
-  }
-  __syncthreads();
-  if (!ctrl[0]) return;
-  __threadfence();
-  for (int i = tid; i < rows_here * D; i += (W + 1) * 32) {
-    const int r = i / D, d = i - r * D;
-    float M = kNeg;
-    for (int sp = 0; sp < nact; sp++)
-      M = fmaxf(M, __ldcg(&p.ws_ml[((cta * p.nsplit + sp) * HQ + r) * 2]));
-    float Lsum = 0.0f, O = 0.0f;
-    for (int sp = 0; sp < nact; sp++) {
-      const int64_t slot = (cta * p.nsplit + sp) * HQ + r;
-      const float e = ex2((__ldcg(&p.ws_ml[slot * 2]) - M) * kLog2e);
-      Lsum += __ldcg(&p.ws_ml[slot * 2 + 1]) * e;
-      O += __ldcg(&p.ws_o[slot * D + d]) * e;
-    }
-    const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
-    const int64_t orow = ((int64_t)b * p.Hq + hq) * L + l;
-    if (p.mode == 0) {
-      p.out[orow * D + d] = f_to_dt(Lsum > 0.0f ? O / Lsum : 0.0f, bf);
-    } else {
-      p.po[orow * D + d] = O;
-      if (d == 0) {
-        p.pm[orow] = M;
-        p.pl[orow] = Lsum;
-      }
-    }
-  }
-  if (tid == 0) p.counters[cta] = 0u;  // leave the ticket ready for the next call
-}
+namespace attn {
 
 // Merge of per-device partials (context split).
 __global__ void merge_kernel(const float* __restrict__ m, const float* __restrict__ l,
@@ -848,7 +21,7 @@ __global__ void merge_kernel(const float* __restrict__ m, const float* __restric
     Ls += l[pp * ps + r] * e;
     O += o[pp * ps + (int64_t)r * D + d] * e;
   }
-  out[i] = f_to_dt(Ls > 0.0f ? O / Ls : 0.0f, bf);
+  out[i] = bf ? f_to_dt<true>(Ls > 0.0f ? O / Ls : 0.0f) : f_to_dt<false>(Ls > 0.0f ? O / Ls : 0.0f);
 }
 
 __global__ void fill_kernel(float* __restrict__ p, int64_t n, float v) {
@@ -856,120 +29,6 @@ __global__ void fill_kernel(float* __restrict__ p, int64_t n, float v) {
   if (i < n) p[i] = v;
 }
 
-// ------------------------------------------------------------ host side --
-
-constexpr int kWarps = 4;  // consumer warps per CTA (+1 producer)
-
-// Rows per consumer slice: 32 when registers allow, else 16.
-template <int D, int NT>
-constexpr int rows_per_warp() {
-  return (D * NT <= 128) ? 32 : 16;
-}
-
-template <int BITS, int D, int GS, int RW>
-constexpr int stages_for() {
-  constexpr int stage = kWarps * RW * Geo<BITS, D, GS>::ROWB;
-  return stage <= 12 * 1024 ? 4 : (stage <= 24 * 1024 ? 3 : 2);
-}
-
-struct LaunchShape {
-  int QB, nsplit, rps;
-};
-
-int g_num_sms[64] = {0};
-
-int num_sms(int dev) {
-  if (dev < 0 || dev >= 64) return 148;
-  if (!g_num_sms[dev]) {
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
-      v = 148;
-    g_num_sms[dev] = v;
-  }
-  return g_num_sms[dev];
-}
-
-// Key split: enough CTAs for a few resident waves; splits are a multiple of
-// the largest chunk (128 key rows) so every split streams whole chunks.
-LaunchShape shape_for(int B, int Hkv, int nrep, int L, int N, int NT, int sms) {
-  LaunchShape s;
-  const int HQ = 8 * NT;
-  const int CH = kWarps * 32;
-  s.QB = (nrep * L + HQ - 1) / HQ;
-  const int64_t units = (int64_t)B * Hkv * s.QB;
-  const int64_t target = (int64_t)sms * 6;
-  int nsplit = (int)std::max<int64_t>(1, (target + units - 1) / units);
-  const int min_rows = 2 * CH;
-  nsplit = std::min(nsplit, std::max(1, (N + min_rows - 1) / min_rows));
-  int rps = (N + nsplit - 1) / nsplit;
-  rps = (rps + CH - 1) / CH * CH;
-  if (rps <= 0) rps = CH;
-  s.rps = rps;
-  s.nsplit = std::max(1, (N + rps - 1) / rps);
-  return s;
-}
-
-// Workspace layout (fixed prefix, so every call finds its tickets at the
-// same place whatever the previous call's shape was):
-//   [0, 256)                      device error flag
-//   [256, 256 + 4*kMaxTickets)    split tickets, zero between calls
-//   then (m, l) and o partials of the splits.
-constexpr int64_t kMaxTickets = 65536;
-constexpr size_t kTicketOff = 256;
-constexpr size_t kPartialOff = kTicketOff + 4 * kMaxTickets;
-
-size_t ws_bytes_for(int B, int Hkv, const LaunchShape& s, int NT, int D) {
-  if (s.nsplit <= 1) return kPartialOff;
-  const size_t slots = (size_t)B * Hkv * s.QB * s.nsplit * 8 * NT;
-  return kPartialOff + (slots * 2 * 4 + 255) / 256 * 256 + slots * D * 4;
-}
-
-template <int BITS, int D, int GS, int NT>
-int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st) {
-  constexpr int RW = rows_per_warp<D, NT>();
-  constexpr int ST = stages_for<BITS, D, GS, RW>();
-  using SM = Smem<BITS, D, GS, NT, kWarps, RW, ST>;
-  auto kern = attn_kernel<BITS, D, GS, NT, kWarps, RW, ST>;
-  static bool configured[64] = {false};
-  int dev = 0;
-  KVQ_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    KVQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL));
-    configured[dev] = true;
-  }
-  const dim3 grid(s.nsplit, p.Hkv * s.QB, B);
-  kern<<<grid, (kWarps + 1) * 32, SM::TOTAL, st>>>(p);
-  KVQ_CUDA_TRY(cudaGetLastError());
-  return KVQ_OK;
-}
-
-template <int BITS, int D, int GS>
-int32_t pick_nt(Params& p, const LaunchShape& s, int NT, int B, cudaStream_t st) {
-  if (NT == 1) return launch_t<BITS, D, GS, 1>(p, s, B, st);
-  return launch_t<BITS, D, GS, 2>(p, s, B, st);
-}
-
-template <int BITS, int D>
-int32_t pick_gs(Params& p, const LaunchShape& s, int GSv, int NT, int B, cudaStream_t st) {
-  switch (GSv) {
-    case 32: return pick_nt<BITS, D, 32>(p, s, NT, B, st);
-    case 64: return pick_nt<BITS, D, 64>(p, s, NT, B, st);
-    case 128:
-      if constexpr (D >= 128) return pick_nt<BITS, D, 128>(p, s, NT, B, st);
-      break;
-  }
-  return fail(KVQ_ERR_ARG, "attention: unsupported group_size for this head_dim");
-}
-
-template <int BITS>
-int32_t pick_d(Params& p, const LaunchShape& s, int Dv, int GSv, int NT, int B, cudaStream_t st) {
-  switch (Dv) {
-    case 64: return pick_gs<BITS, 64>(p, s, GSv, NT, B, st);
-    case 128: return pick_gs<BITS, 128>(p, s, GSv, NT, B, st);
-    case 256: return pick_gs<BITS, 256>(p, s, GSv, NT, B, st);
-  }
-  return fail(KVQ_ERR_ARG, "attention: head_dim must be 64, 128 or 256");
-}
 
 // Validate and fill Params common to every attention launch.
 int32_t prepare(const AttnArgs& a, int L, int mask_mode, int window, Params& p, int& NT) {
@@ -1032,7 +91,14 @@ int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void*
   if (a.B == 0 || a.Hq == 0) return KVQ_OK;
   int dev = 0;
   KVQ_CUDA_TRY(cudaGetDevice(&dev));
-  LaunchShape s = shape_for(a.B, a.Hkv, p.nrep, L, std::max(a.N, 1), NT, num_sms(dev));
+  int occ = 1;
+  {
+    LaunchShape probe{1, 1, 1};
+    rc = a.bits == 4 ? dispatch_b4(p, probe, a.D, a.gs, NT, a.B, st, &occ)
+                     : dispatch_b8(p, probe, a.D, a.gs, NT, a.B, st, &occ);
+    if (rc) return rc;
+  }
+  LaunchShape s = shape_for(a.B, a.Hkv, p.nrep, L, std::max(a.N, 1), NT, num_sms(dev) * occ);
   if ((int64_t)a.B * a.Hkv * s.QB > kMaxTickets) {  // too many merge groups: no key split
     s.nsplit = 1;
     s.rps = std::max(a.N, 1);
@@ -1061,11 +127,13 @@ int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void*
   p.pl = pl;
   p.po = po;
   p.scores = scores;
-  if (a.bits == 4) return pick_d<4>(p, s, a.D, a.gs, NT, a.B, st);
-  return pick_d<8>(p, s, a.D, a.gs, NT, a.B, st);
+  if (a.bits == 4) return dispatch_b4(p, s, a.D, a.gs, NT, a.B, st, nullptr);
+  return dispatch_b8(p, s, a.D, a.gs, NT, a.B, st, nullptr);
 }
 
-}  // namespace
+}  // namespace attn
+
+using namespace attn;
 
 size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D) {
   if (Hkv <= 0 || Hq % Hkv) return 0;
@@ -1073,7 +141,9 @@ size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D) {
   const int NT = nrep <= 8 ? 1 : 2;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  LaunchShape s = shape_for(B, Hkv, nrep, 1, std::max(N, 1), NT, num_sms(dev));
+  // Upper bound over every kernel instance: the split count shape_for can
+  // reach with the largest possible residency (its cap is 256 rows a split).
+  LaunchShape s = shape_for(B, Hkv, nrep, 1, std::max(N, 1), NT, num_sms(dev) * 64);
   if ((int64_t)B * Hkv * s.QB > kMaxTickets) s.nsplit = 1;
   return ws_bytes_for(B, Hkv, s, NT, D);
 }
