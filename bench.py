@@ -349,7 +349,7 @@ def run_gpu(args, rank, world, local_rank):
                     "d2h_bytes_per_step": int(ho[0].numel() * 2),
                     "us_per_step": round(1e3 * e2e_ms / K2, 3), "steps": K2,
                     "path": "kvq Python API per step (eager), pinned host buffers"},
-            "gpu_launches": 3 * K,
+            "gpu_launches": 2 * K,  # one fused K/V append + one decode per step
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_kind": peak_kind, "kernel": "attn_kernel<4,128,64,1> (decode)",
@@ -363,6 +363,32 @@ def run_gpu(args, rank, world, local_rank):
     return res
 
 
+def profile_run(args):
+    """Fixed small workload for ncu: 3 config-2 layers (227 MB, above L2),
+    `--steps` launches of one kernel, cycling layers."""
+    import numpy as np
+    import torch
+    import kvq
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    layers = setup_layers(CFG, 3, device, seed=7)
+    scale = 1.0 / np.sqrt(CFG["D"])
+    views = []
+    for L in layers:
+        views.append(L["cache"].update_and_fetch_quantized(L["kn"], L["vn"]))
+        L["cache"].trim(1)
+    for i in range(args.steps):
+        L = layers[i % 3]
+        if args.profile == "decode":
+            kvq.sdpa_decode(L["q"], views[i % 3][0], views[i % 3][1], scale, out=L["out"])
+        else:
+            L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])
+            L["cache"].trim(1)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": args.profile, "launches": args.steps,
+                      "out_mean_abs": float(layers[0]["out"].float().abs().mean())}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -370,7 +396,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="kvq", choices=["kvq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["decode", "append"], default=None,
+                    help="run only the named kernel over 3 config-2 layers, `--steps` "
+                         "launches, no timing (a small, fixed workload for ncu captures)")
     args = ap.parse_args()
+    if args.profile:
+        return profile_run(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -237,9 +237,8 @@ int32_t grow_to(kvq_cache* c, int64_t keep, int64_t new_len, cudaStream_t st) {
 int32_t quantize_into(kvq_cache* c, const void* k, const void* v, int S, const int64_t* ks,
                       const int64_t* vs, int64_t dst_row, cudaStream_t st) {
   RowGeom g{c->d.head_dim, c->d.bits, c->d.group_size};
-  int32_t rc = launch_append(k, ks, c->d.batch, c->d.kv_heads, S, g, c->d.dtype, c->k, dst_row, st);
-  if (rc) return rc;
-  return launch_append(v, vs, c->d.batch, c->d.kv_heads, S, g, c->d.dtype, c->v, dst_row, st);
+  return launch_append_kv(k, ks, v, vs, c->d.batch, c->d.kv_heads, S, g, c->d.dtype, c->k, c->v,
+                          dst_row, st);
 }
 
 int32_t check_desc(const kvq_desc* d) {

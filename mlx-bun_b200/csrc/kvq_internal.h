@@ -38,10 +38,12 @@ struct TripleView {
 };
 
 // ---- quantize kernels (kvq_quant.cu) ----
-// Quantize rows of logical shape [B, H, S, D] (element strides in[4], d stride
-// 1) into rows dst_row0 + s of the destination triple.
-int32_t launch_append(const void* x, const int64_t* strides, int B, int H, int S, RowGeom g,
-                      int dtype, TripleView dst, int64_t dst_row0, cudaStream_t st);
+// Quantize K and V rows of logical shape [B, H, S, D] (element strides
+// (b, h, s), d stride 1) into rows dst_row0 + s of the two destination
+// triples, in one launch.
+int32_t launch_append_kv(const void* k, const int64_t* k_strides, const void* v,
+                         const int64_t* v_strides, int B, int H, int S, RowGeom g, int dtype,
+                         TripleView dk, TripleView dv, int64_t dst_row0, cudaStream_t st);
 // Contiguous rows -> contiguous triple.
 int32_t launch_quantize_rows(const void* x, int64_t rows, RowGeom g, int dtype, uint32_t* packed,
                              uint16_t* scales, uint16_t* biases, cudaStream_t st);

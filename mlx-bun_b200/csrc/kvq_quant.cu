@@ -9,9 +9,11 @@
 // group writes the dtype-rounded scale and the bias.  Divisions are IEEE
 // (no fast-math) so the codes are bit-identical to the CPU restatement.
 //
-// The kernel is HBM-bound and tiny on the decode path (S = 1 row per head);
-// for whole-cache conversion it reads 2 B and writes bits/8 + 4/gs B per
-// element with 16-byte loads when the input rows are 16-byte aligned.
+// One launch carries up to two jobs (the K and the V rows of an append,
+// selected by blockIdx.y): on the decode path the work is a few rows and the
+// launch itself is the cost.  For whole-cache conversion the kernel is
+// HBM-bound: 2 B read and bits/8 + 4/gs B written per element, with 16-byte
+// loads when the input rows are 16-byte aligned.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -21,6 +23,21 @@ namespace kvq {
 namespace {
 
 constexpr float kEps = 1e-7f;  // constant-group guard shared with the oracle
+
+struct Job {
+  const uint16_t* x;
+  int64_t sb, sh, ss;  // element strides of (b, h, s); d stride is 1
+  uint32_t* packed;
+  uint16_t* scales;
+  uint16_t* biases;
+  int64_t dst_bstride, dst_hstride, dst_row0;  // rows
+};
+
+struct Jobs {
+  Job j[2];
+  int H, S, words;
+  int64_t total_rows;
+};
 
 template <bool BF16>
 __device__ __forceinline__ float load_f(const uint16_t* p) {
@@ -44,22 +61,21 @@ __device__ __forceinline__ float word_to_f(uint32_t w, int half) {
 
 // BITS: 4 or 8.  TPG: threads per group (gs * BITS / 32).  VEC: 16-B loads.
 template <int BITS, int TPG, bool BF16, bool VEC>
-__global__ void __launch_bounds__(256) quantize_rows_kernel(
-    const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t ss, int H, int S,
-    int64_t total_rows, int words, uint32_t* __restrict__ packed, uint16_t* __restrict__ scales,
-    uint16_t* __restrict__ biases, int64_t dst_bstride, int64_t dst_hstride, int64_t dst_row0) {
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const Jobs jobs) {
   constexpr int PER = 32 / BITS;
   constexpr float NB = (float)((1 << BITS) - 1);
+  const Job& J = jobs.j[blockIdx.y];
+  const int words = jobs.words;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t row = tid / words;
   const int word = (int)(tid - row * words);
-  const bool valid = row < total_rows;
-  const int64_t r = valid ? row : total_rows - 1;
-  const int s = (int)(r % S);
-  const int64_t bh = r / S;
-  const int h = (int)(bh % H);
-  const int64_t b = bh / H;
-  const uint16_t* src = x + b * sb + h * sh + (int64_t)s * ss + (int64_t)word * PER;
+  const bool valid = row < jobs.total_rows;
+  const int64_t r = valid ? row : jobs.total_rows - 1;
+  const int s = (int)(r % jobs.S);
+  const int64_t bh = r / jobs.S;
+  const int h = (int)(bh % jobs.H);
+  const int64_t b = bh / jobs.H;
+  const uint16_t* src = J.x + b * J.sb + h * J.sh + (int64_t)s * J.ss + (int64_t)word * PER;
 
   float w[PER];
   if (VEC) {
@@ -115,80 +131,99 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
     out |= (uint32_t)c << (BITS * i);
   }
   if (!valid) return;
-  const int64_t drow = b * dst_bstride + h * dst_hstride + dst_row0 + s;
-  packed[drow * words + word] = out;
+  const int64_t drow = b * J.dst_bstride + h * J.dst_hstride + J.dst_row0 + s;
+  J.packed[drow * words + word] = out;
   if ((word % TPG) == 0) {
     const int groups = words / TPG;
     const int g = word / TPG;
-    scales[drow * groups + g] = store_bits<BF16>(scale);
-    biases[drow * groups + g] = store_bits<BF16>(bias);
+    J.scales[drow * groups + g] = store_bits<BF16>(scale);
+    J.biases[drow * groups + g] = store_bits<BF16>(bias);
   }
 }
 
 template <int BITS, int TPG, bool BF16>
-int32_t dispatch_vec(bool vec, dim3 grid, cudaStream_t st, const uint16_t* x, int64_t sb,
-                     int64_t sh, int64_t ss, int H, int S, int64_t total, int words, TripleView d,
-                     int64_t row0) {
+int32_t dispatch_vec(bool vec, dim3 grid, cudaStream_t st, const Jobs& jobs) {
   if (vec)
-    quantize_rows_kernel<BITS, TPG, BF16, true><<<grid, 256, 0, st>>>(
-        x, sb, sh, ss, H, S, total, words, d.packed, d.scales, d.biases, d.batch_stride,
-        d.head_stride, row0);
+    quantize_rows_kernel<BITS, TPG, BF16, true><<<grid, 256, 0, st>>>(jobs);
   else
-    quantize_rows_kernel<BITS, TPG, BF16, false><<<grid, 256, 0, st>>>(
-        x, sb, sh, ss, H, S, total, words, d.packed, d.scales, d.biases, d.batch_stride,
-        d.head_stride, row0);
+    quantize_rows_kernel<BITS, TPG, BF16, false><<<grid, 256, 0, st>>>(jobs);
   KVQ_CUDA_TRY(cudaGetLastError());
   return KVQ_OK;
 }
 
 template <int BITS, bool BF16>
-int32_t dispatch_tpg(int tpg, bool vec, dim3 grid, cudaStream_t st, const uint16_t* x,
-                     int64_t sb, int64_t sh, int64_t ss, int H, int S, int64_t total, int words,
-                     TripleView d, int64_t row0) {
+int32_t dispatch_tpg(int tpg, bool vec, dim3 grid, cudaStream_t st, const Jobs& jobs) {
   switch (tpg) {
-    case 2: return dispatch_vec<BITS, 2, BF16>(vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0);
-    case 4: return dispatch_vec<BITS, 4, BF16>(vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0);
-    case 8: return dispatch_vec<BITS, 8, BF16>(vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0);
-    case 16: return dispatch_vec<BITS, 16, BF16>(vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0);
-    case 32: return dispatch_vec<BITS, 32, BF16>(vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0);
+    case 4: return dispatch_vec<BITS, 4, BF16>(vec, grid, st, jobs);
+    case 8: return dispatch_vec<BITS, 8, BF16>(vec, grid, st, jobs);
+    case 16: return dispatch_vec<BITS, 16, BF16>(vec, grid, st, jobs);
+    case 32: return dispatch_vec<BITS, 32, BF16>(vec, grid, st, jobs);
   }
   return fail(KVQ_ERR_ARG, "quantize: unsupported group_size/bits combination");
 }
 
-int32_t launch_generic(const uint16_t* x, int64_t sb, int64_t sh, int64_t ss, int B, int H, int S,
-                       RowGeom g, int dtype, TripleView d, int64_t row0, cudaStream_t st) {
-  const int64_t total = (int64_t)B * H * S;
-  if (total == 0) return KVQ_OK;
-  const int words = g.words();
+bool aligned_for(const Job& j, int per) {
+  return ((uintptr_t)j.x % (per * 2) == 0) && j.sb % per == 0 && j.sh % per == 0 &&
+         j.ss % per == 0;
+}
+
+int32_t launch_jobs(Jobs& jobs, int njobs, int B, RowGeom g, int dtype, cudaStream_t st) {
+  jobs.total_rows = (int64_t)B * jobs.H * jobs.S;
+  if (jobs.total_rows == 0) return KVQ_OK;
+  jobs.words = g.words();
   const int tpg = g.gs * g.bits / 32;
   const int per = 32 / g.bits;
-  const int64_t threads = total * words;
-  const dim3 grid((unsigned)((threads + 255) / 256));
-  const bool vec = ((uintptr_t)x % (per * 2) == 0) && sb % per == 0 && sh % per == 0 &&
-                   ss % per == 0;
+  const int64_t threads = jobs.total_rows * jobs.words;
+  const dim3 grid((unsigned)((threads + 255) / 256), (unsigned)njobs);
+  bool vec = true;
+  for (int i = 0; i < njobs; i++) vec = vec && aligned_for(jobs.j[i], per);
   const bool bf = dtype == KVQ_DTYPE_BFLOAT16;
   if (g.bits == 4)
-    return bf ? dispatch_tpg<4, true>(tpg, vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0)
-              : dispatch_tpg<4, false>(tpg, vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0);
-  return bf ? dispatch_tpg<8, true>(tpg, vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0)
-            : dispatch_tpg<8, false>(tpg, vec, grid, st, x, sb, sh, ss, H, S, total, words, d, row0);
+    return bf ? dispatch_tpg<4, true>(tpg, vec, grid, st, jobs)
+              : dispatch_tpg<4, false>(tpg, vec, grid, st, jobs);
+  return bf ? dispatch_tpg<8, true>(tpg, vec, grid, st, jobs)
+            : dispatch_tpg<8, false>(tpg, vec, grid, st, jobs);
+}
+
+Job job_for(const void* x, const int64_t* strides, const TripleView& d, int64_t row0) {
+  Job j;
+  j.x = static_cast<const uint16_t*>(x);
+  j.sb = strides[0];
+  j.sh = strides[1];
+  j.ss = strides[2];
+  j.packed = d.packed;
+  j.scales = d.scales;
+  j.biases = d.biases;
+  j.dst_bstride = d.batch_stride;
+  j.dst_hstride = d.head_stride;
+  j.dst_row0 = row0;
+  return j;
 }
 
 }  // namespace
 
-int32_t launch_append(const void* x, const int64_t* strides, int B, int H, int S, RowGeom g,
-                      int dtype, TripleView dst, int64_t dst_row0, cudaStream_t st) {
-  return launch_generic(static_cast<const uint16_t*>(x), strides[0], strides[1], strides[2], B, H,
-                        S, g, dtype, dst, dst_row0, st);
+int32_t launch_append_kv(const void* k, const int64_t* k_strides, const void* v,
+                         const int64_t* v_strides, int B, int H, int S, RowGeom g, int dtype,
+                         TripleView dk, TripleView dv, int64_t dst_row0, cudaStream_t st) {
+  Jobs jobs{};
+  jobs.j[0] = job_for(k, k_strides, dk, dst_row0);
+  jobs.j[1] = job_for(v, v_strides, dv, dst_row0);
+  jobs.H = H;
+  jobs.S = S;
+  return launch_jobs(jobs, 2, B, g, dtype, st);
 }
 
 int32_t launch_quantize_rows(const void* x, int64_t rows, RowGeom g, int dtype, uint32_t* packed,
                              uint16_t* scales, uint16_t* biases, cudaStream_t st) {
-  // Treat the rows as [1, 1, rows, D]; rows may exceed int range only via S.
   if (rows > (int64_t)0x7fffffff) return fail(KVQ_ERR_ARG, "quantize: too many rows");
+  // Treat the rows as [1, 1, rows, D].
+  const int64_t strides[3] = {0, 0, g.D};
   TripleView d{packed, scales, biases, 0, 0};
-  return launch_generic(static_cast<const uint16_t*>(x), 0, 0, g.D, 1, 1, (int)rows, g, dtype, d,
-                        0, st);
+  Jobs jobs{};
+  jobs.j[0] = job_for(x, strides, d, 0);
+  jobs.H = 1;
+  jobs.S = (int)rows;
+  return launch_jobs(jobs, 1, 1, g, dtype, st);
 }
 
 }  // namespace kvq
