@@ -208,6 +208,26 @@ int32_t kvq_debug_scores(const kvq_qtensor* keys, const void* q, int32_t q_heads
                          float scale, int32_t mask_mode, int32_t window, float* scores,
                          void* stream);
 
+/* Scratch held by kvq_sdpa_decode_noalloc: the 256 KiB flag-and-ticket
+ * prefix of the decode workspace plus 2 MiB of split partials. */
+#define KVQ_NOALLOC_SCRATCH_BYTES (256u * 1024u + 256u + 2u * 1024u * 1024u)
+
+/* kvq_sdpa_decode for callers that must not allocate device memory: code
+ * running while a CUDA stream capture is open (cudaMalloc is illegal then)
+ * and serving processes that give all device memory to their own pool at
+ * start-up.  No counterpart in the reference (MLX allocates internally).
+ * Same arguments and results as kvq_sdpa_decode without the workspace: the
+ * kernel's scratch is a fixed KVQ_NOALLOC_SCRATCH_BYTES array inside the
+ * library that every GPU loading libkvq keeps until exit.  The first call on
+ * a device looks up that array's device address (make it before any stream
+ * capture).  Each call clears the scratch's flag and tickets with a
+ * stream-ordered memset; all calls share the array, so calls that overlap
+ * on the GPU race — issue them on one stream.  Shapes whose split partials
+ * do not fit return KVQ_ERR_WORKSPACE with the sizes in kvq_last_error(). */
+int32_t kvq_sdpa_decode_noalloc(const kvq_qtensor* keys, const kvq_qtensor* values,
+                                const void* q, int32_t q_heads, float scale,
+                                const int32_t* seq_lens, void* out, void* stream);
+
 /* Synchronize `stream` and report (then clear) the device error flag that a
  * kernel raises when a bounded wait on its own TMA copies times out.
  * workspace: the caller workspace used by the calls, or NULL for the

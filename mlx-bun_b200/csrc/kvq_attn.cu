@@ -148,6 +148,25 @@ size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D) {
   return ws_bytes_for(B, Hkv, s, NT, D);
 }
 
+int32_t decode_workspace_exact(const AttnArgs& a, size_t* bytes, size_t* zero_prefix) {
+  Params p;
+  int NT = 1;
+  int32_t rc = prepare(a, 1, 0, 0, p, NT);
+  if (rc) return rc;
+  int dev = 0;
+  KVQ_CUDA_TRY(cudaGetDevice(&dev));
+  int occ = 1;
+  LaunchShape probe{1, 1, 1};
+  rc = a.bits == 4 ? dispatch_b4(p, probe, a.D, a.gs, NT, a.B, nullptr, &occ)
+                   : dispatch_b8(p, probe, a.D, a.gs, NT, a.B, nullptr, &occ);
+  if (rc) return rc;
+  LaunchShape s = shape_for(a.B, a.Hkv, p.nrep, 1, std::max(a.N, 1), NT, num_sms(dev) * occ);
+  if ((int64_t)a.B * a.Hkv * s.QB > kMaxTickets) s.nsplit = 1;
+  *bytes = ws_bytes_for(a.B, a.Hkv, s, NT, a.D);
+  *zero_prefix = kTicketOff + 4 * (size_t)std::min<int64_t>((int64_t)a.B * a.Hkv * s.QB, kMaxTickets);
+  return KVQ_OK;
+}
+
 int32_t launch_decode(const AttnArgs& a, void* out, float* pm, float* pl, float* po, void* ws,
                       size_t ws_bytes, cudaStream_t st) {
   return run(a, 1, 0, 0, out ? 0 : 1, out, pm, pl, po, ws, ws_bytes, st);

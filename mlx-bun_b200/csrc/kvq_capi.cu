@@ -262,7 +262,24 @@ int32_t check_qt(const kvq_qtensor* t, const char* name) {
   return KVQ_OK;
 }
 
-int32_t make_args(const kvq_qtensor* k, const kvq_qtensor* v, const void* q, int32_t q_heads,
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+namespace kvq {
+
+int32_t make_attn_args(const kvq_qtensor* k, const kvq_qtensor* v, const void* q, int32_t q_heads,
                   float scale, const int32_t* seq_lens, AttnArgs& a) {
   int32_t rc = check_qt(k, "keys");
   if (rc) return rc;
@@ -291,20 +308,7 @@ int32_t make_args(const kvq_qtensor* k, const kvq_qtensor* v, const void* q, int
   return KVQ_OK;
 }
 
-struct DeviceGuard {
-  int prev = -1;
-  bool ok = true;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-  }
-};
-
-}  // namespace
+}  // namespace kvq
 
 extern "C" {
 
@@ -558,7 +562,7 @@ int32_t kvq_sdpa_decode(const kvq_qtensor* keys, const kvq_qtensor* values, cons
                         int32_t q_heads, float scale, const int32_t* seq_lens, void* out,
                         void* workspace, size_t workspace_bytes, void* stream) {
   AttnArgs a{};
-  int32_t rc = make_args(keys, values, q, q_heads, scale, seq_lens, a);
+  int32_t rc = make_attn_args(keys, values, q, q_heads, scale, seq_lens, a);
   if (rc) return rc;
   if (!out) return fail(KVQ_ERR_ARG, "out is NULL");
   return launch_decode(a, out, nullptr, nullptr, nullptr, workspace, workspace_bytes,
@@ -570,7 +574,7 @@ int32_t kvq_sdpa_decode_partial(const kvq_qtensor* keys, const kvq_qtensor* valu
                                 const int32_t* seq_lens, float* m, float* l, float* o,
                                 void* workspace, size_t workspace_bytes, void* stream) {
   AttnArgs a{};
-  int32_t rc = make_args(keys, values, q, q_heads, scale, seq_lens, a);
+  int32_t rc = make_attn_args(keys, values, q, q_heads, scale, seq_lens, a);
   if (rc) return rc;
   if (!m || !l || !o) return fail(KVQ_ERR_ARG, "NULL partial output");
   return launch_decode(a, nullptr, m, l, o, workspace, workspace_bytes,
@@ -593,7 +597,7 @@ int32_t kvq_sdpa_prefill(const kvq_qtensor* keys, const kvq_qtensor* values, con
                          int32_t window, void* out, void* workspace, size_t workspace_bytes,
                          void* stream) {
   AttnArgs a{};
-  int32_t rc = make_args(keys, values, q, q_heads, scale, nullptr, a);
+  int32_t rc = make_attn_args(keys, values, q, q_heads, scale, nullptr, a);
   if (rc) return rc;
   if (!out) return fail(KVQ_ERR_ARG, "out is NULL");
   if (mask_mode != KVQ_MASK_NONE && mask_mode != KVQ_MASK_CAUSAL) return fail(KVQ_ERR_ARG, "bad mask_mode");
@@ -606,7 +610,7 @@ int32_t kvq_debug_scores(const kvq_qtensor* keys, const void* q, int32_t q_heads
                          float scale, int32_t mask_mode, int32_t window, float* scores,
                          void* stream) {
   AttnArgs a{};
-  int32_t rc = make_args(keys, keys, q, q_heads, scale, nullptr, a);
+  int32_t rc = make_attn_args(keys, keys, q, q_heads, scale, nullptr, a);
   if (rc) return rc;
   if (!scores || L <= 0 || L > keys->len) return fail(KVQ_ERR_ARG, "bad scores / L");
   return launch_debug_scores(a, L, mask_mode, mask_mode == KVQ_MASK_CAUSAL ? window : 0, scores,

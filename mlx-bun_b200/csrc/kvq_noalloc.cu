@@ -1,0 +1,72 @@
+// kvq_noalloc.cu — decode attention that allocates no device memory.
+//
+// Some callers must not allocate: code that runs while a CUDA stream
+// capture is open (cudaMalloc is illegal then), and serving processes that
+// hand all device memory to their own pool at start-up.  For them
+// kvq_sdpa_decode_noalloc runs the same decode kernel as kvq_sdpa_decode but
+// keeps the kernel's scratch (device error flag, split tickets, split
+// partials) in the file-scope array below instead of a cudaMalloc'd buffer.
+//
+// The array is KVQ_NOALLOC_SCRATCH_BYTES long; every GPU that loads the
+// library holds it until the process exits.  Host code cannot use the
+// array's name as a device address, so the first call on each device (with
+// that device current) looks the address up once with cudaGetSymbolAddress;
+// make that first call before any stream capture.  Every call shares the
+// array and leaves its contents behind, so each call clears the part that
+// must start at zero (flag and tickets) with a stream-ordered memset, and
+// calls that overlap on the GPU race: issue them on one stream.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+
+#include "kvq_internal.h"
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_decode_scratch[KVQ_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {nullptr};
+
+// Device address of g_decode_scratch on the current device.
+int32_t scratch_address(int dev, void** out) {
+  if (dev < 0 || dev >= 64) return kvq::fail(KVQ_ERR_ARG, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || !p) return kvq::cuda_fail(e, "cudaGetSymbolAddress(decode scratch)");
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return KVQ_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t kvq_sdpa_decode_noalloc(const kvq_qtensor* keys, const kvq_qtensor* values,
+                                           const void* q, int32_t q_heads, float scale,
+                                           const int32_t* seq_lens, void* out, void* stream) {
+  using namespace kvq;
+  AttnArgs a{};
+  int32_t rc = make_attn_args(keys, values, q, q_heads, scale, seq_lens, a);
+  if (rc) return rc;
+  if (!out) return fail(KVQ_ERR_ARG, "out is NULL");
+  size_t need = 0, zero_prefix = 0;
+  if ((rc = decode_workspace_exact(a, &need, &zero_prefix))) return rc;
+  if (need > (size_t)KVQ_NOALLOC_SCRATCH_BYTES)
+    return fail(KVQ_ERR_WORKSPACE,
+                "kvq_sdpa_decode_noalloc: these shapes need " + std::to_string(need) +
+                    " bytes of scratch, more than its fixed " +
+                    std::to_string((size_t)KVQ_NOALLOC_SCRATCH_BYTES) +
+                    "; use kvq_sdpa_decode with a caller workspace");
+  int dev = 0;
+  KVQ_CUDA_TRY(cudaGetDevice(&dev));
+  void* ws = nullptr;
+  if ((rc = scratch_address(dev, &ws))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  KVQ_CUDA_TRY(cudaMemsetAsync(ws, 0, zero_prefix, st));
+  return launch_decode(a, out, nullptr, nullptr, nullptr, ws, (size_t)KVQ_NOALLOC_SCRATCH_BYTES,
+                       st);
+}

@@ -26,6 +26,7 @@ EXPORTS = (
     "kvq_cache_fetch", "kvq_cache_state", "kvq_cache_trim", "kvq_cache_make_mask",
     "kvq_quantize", "kvq_sdpa_decode_workspace", "kvq_sdpa_decode", "kvq_sdpa_decode_partial",
     "kvq_sdpa_merge", "kvq_sdpa_prefill", "kvq_debug_scores", "kvq_check_device",
+    "kvq_sdpa_decode_noalloc",
 )
 
 
@@ -84,6 +85,7 @@ def lib():
                                    ctypes.c_size_t, vp]),
         "kvq_debug_scores": (i32, [P(QTensor), vp, i32, i32, f32, i32, i32, vp, vp]),
         "kvq_check_device": (i32, [vp, vp]),
+        "kvq_sdpa_decode_noalloc": (i32, [P(QTensor), P(QTensor), vp, i32, f32, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
