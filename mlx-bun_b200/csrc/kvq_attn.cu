@@ -1,6 +1,7 @@
 // kvq_attn.cu — host side of the attention entry points: argument checks,
-// launch shapes, workspace, split merge kernel and debug scores.  The kernel
-// itself is kvq_attn_impl.cuh, instantiated in kvq_attn_b4.cu / kvq_attn_b8.cu.
+// kernel choice and launch shapes, workspace, the cross-device merge kernel
+// and debug scores.  The kernels are in kvq_attn_impl.cuh, instantiated in
+// kvq_attn_b4.cu / kvq_attn_b8.cu.
 #include "kvq_attn_impl.cuh"
 
 namespace kvq {
@@ -81,39 +82,73 @@ int32_t prepare(const AttnArgs& a, int L, int mask_mode, int window, Params& p, 
   return KVQ_OK;
 }
 
+// Kernel choice, launch shape and workspace of one attention call.
+struct Plan {
+  LaunchShape s;
+  size_t ws_bytes;  // workspace this call needs
+  int64_t tickets;  // merge tickets it uses (zero before and after the call)
+};
+
+int32_t make_plan(const AttnArgs& a, int L, int mask_mode, int window, bool scores, Params& p,
+                  int& NT, Plan& pl) {
+  int32_t rc = prepare(a, L, mask_mode, window, p, NT);
+  if (rc) return rc;
+  int dev = 0;
+  KVQ_CUDA_TRY(cudaGetDevice(&dev));
+  const int64_t units = (int64_t)a.B * a.Hkv;
+  // Decode over every key of each row: the balanced single-wave kernel.
+  const bool bal = L == 1 && !scores && (mask_mode == 0 || window <= 0) && a.N > 0 &&
+                   units > 0 && units <= kMaxTickets && (!a.seq_lens || a.B <= kBalMaxBatch);
+  LaunchShape probe{1, 1, 1};
+  probe.ctas = bal ? 1 : 0;
+  int occ = 1;
+  rc = a.bits == 4 ? dispatch_b4(p, probe, a.D, a.gs, NT, a.B, nullptr, &occ)
+                   : dispatch_b8(p, probe, a.D, a.gs, NT, a.B, nullptr, &occ);
+  if (rc) return rc;
+  if (bal) {
+    const int Tu = (a.N + kTile - 1) / kTile;
+    int64_t C = (int64_t)num_sms(dev) * occ;
+    C = std::min<int64_t>(C, std::max<int64_t>(1, units * Tu / kBalMinTiles));
+    pl.s = LaunchShape{1, 1, kTile};
+    pl.s.ctas = (int)C;
+    p.B = a.B;
+    p.Tu = Tu;
+    pl.tickets = units;
+  } else {
+    pl.s = shape_for(a.B, a.Hkv, p.nrep, L, std::max(a.N, 1), NT, num_sms(dev) * occ);
+    if (units * pl.s.QB > kMaxTickets) {  // too many merge groups: no key split
+      pl.s.nsplit = 1;
+      pl.s.rps = std::max(a.N, 1);
+    }
+    pl.tickets = pl.s.nsplit > 1 ? units * pl.s.QB : 0;
+  }
+  pl.ws_bytes = ws_bytes_for(a.B, a.Hkv, pl.s, NT, a.D);
+  return KVQ_OK;
+}
+
 int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void* out, float* pm,
-            float* pl, float* po, void* ws, size_t ws_bytes, cudaStream_t st,
+            float* pl_, float* po, void* ws, size_t ws_bytes, cudaStream_t st,
             float* scores = nullptr) {
   Params p;
   int NT = 1;
-  int32_t rc = prepare(a, L, mask_mode, window, p, NT);
+  Plan pl;
+  int32_t rc = make_plan(a, L, mask_mode, window, scores != nullptr, p, NT, pl);
   if (rc) return rc;
   if (a.B == 0 || a.Hq == 0) return KVQ_OK;
   int dev = 0;
   KVQ_CUDA_TRY(cudaGetDevice(&dev));
-  int occ = 1;
-  {
-    LaunchShape probe{1, 1, 1};
-    rc = a.bits == 4 ? dispatch_b4(p, probe, a.D, a.gs, NT, a.B, st, &occ)
-                     : dispatch_b8(p, probe, a.D, a.gs, NT, a.B, st, &occ);
-    if (rc) return rc;
-  }
-  LaunchShape s = shape_for(a.B, a.Hkv, p.nrep, L, std::max(a.N, 1), NT, num_sms(dev) * occ);
-  if ((int64_t)a.B * a.Hkv * s.QB > kMaxTickets) {  // too many merge groups: no key split
-    s.nsplit = 1;
-    s.rps = std::max(a.N, 1);
-  }
-  const size_t need = ws_bytes_for(a.B, a.Hkv, s, NT, a.D);
+  const LaunchShape& s = pl.s;
   if (!ws) {
-    ws = managed_workspace(dev, need, st, &rc);
+    ws = managed_workspace(dev, pl.ws_bytes, st, &rc);
     if (rc) return rc;
-  } else if (ws_bytes < need) {
+  } else if (ws_bytes < pl.ws_bytes) {
     return fail(KVQ_ERR_WORKSPACE, "workspace smaller than kvq_sdpa_decode_workspace()");
   }
   uint8_t* w = static_cast<uint8_t*>(ws);
   p.err = reinterpret_cast<int*>(w);
-  if (s.nsplit > 1) {
-    const size_t slots = (size_t)a.B * a.Hkv * s.QB * s.nsplit * 8 * NT;
+  if (pl.tickets > 0) {
+    const size_t slots = s.ctas > 0 ? ((size_t)s.ctas + (size_t)a.B * a.Hkv) * 8 * NT
+                                    : (size_t)a.B * a.Hkv * s.QB * s.nsplit * 8 * NT;
     p.counters = reinterpret_cast<unsigned*>(w + kTicketOff);
     p.ws_ml = reinterpret_cast<float*>(w + kPartialOff);
     p.ws_o = reinterpret_cast<float*>(w + kPartialOff + (slots * 2 * 4 + 255) / 256 * 256);
@@ -124,7 +159,7 @@ int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void*
   p.mode = mode;
   p.out = static_cast<uint16_t*>(out);
   p.pm = pm;
-  p.pl = pl;
+  p.pl = pl_;
   p.po = po;
   p.scores = scores;
   if (a.bits == 4) return dispatch_b4(p, s, a.D, a.gs, NT, a.B, st, nullptr);
@@ -141,29 +176,27 @@ size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D) {
   const int NT = nrep <= 8 ? 1 : 2;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  // Upper bound over every kernel instance: the split count shape_for can
-  // reach with the largest possible residency (its cap is 256 rows a split).
+  // Upper bound over every kernel instance and both decode kernels, with
+  // the largest possible residency (64 blocks per SM).
   LaunchShape s = shape_for(B, Hkv, nrep, 1, std::max(N, 1), NT, num_sms(dev) * 64);
   if ((int64_t)B * Hkv * s.QB > kMaxTickets) s.nsplit = 1;
-  return ws_bytes_for(B, Hkv, s, NT, D);
+  LaunchShape sb{1, 1, kTile};
+  const int64_t units = (int64_t)B * Hkv;
+  const int64_t Tu = (std::max(N, 0) + kTile - 1) / kTile;
+  sb.ctas = (int)std::min<int64_t>((int64_t)num_sms(dev) * 64,
+                                   std::max<int64_t>(1, units * Tu / kBalMinTiles));
+  return std::max(ws_bytes_for(B, Hkv, s, NT, D), ws_bytes_for(B, Hkv, sb, NT, D));
 }
 
 int32_t decode_workspace_exact(const AttnArgs& a, size_t* bytes, size_t* zero_prefix) {
   Params p;
   int NT = 1;
-  int32_t rc = prepare(a, 1, 0, 0, p, NT);
+  Plan pl;
+  int32_t rc = make_plan(a, 1, 0, 0, false, p, NT, pl);
   if (rc) return rc;
-  int dev = 0;
-  KVQ_CUDA_TRY(cudaGetDevice(&dev));
-  int occ = 1;
-  LaunchShape probe{1, 1, 1};
-  rc = a.bits == 4 ? dispatch_b4(p, probe, a.D, a.gs, NT, a.B, nullptr, &occ)
-                   : dispatch_b8(p, probe, a.D, a.gs, NT, a.B, nullptr, &occ);
-  if (rc) return rc;
-  LaunchShape s = shape_for(a.B, a.Hkv, p.nrep, 1, std::max(a.N, 1), NT, num_sms(dev) * occ);
-  if ((int64_t)a.B * a.Hkv * s.QB > kMaxTickets) s.nsplit = 1;
-  *bytes = ws_bytes_for(a.B, a.Hkv, s, NT, a.D);
-  *zero_prefix = kTicketOff + 4 * (size_t)std::min<int64_t>((int64_t)a.B * a.Hkv * s.QB, kMaxTickets);
+  *bytes = pl.ws_bytes;
+  *zero_prefix =
+      kTicketOff + 4 * (size_t)std::min<int64_t>(std::max<int64_t>(pl.tickets, 0), kMaxTickets);
   return KVQ_OK;
 }
 

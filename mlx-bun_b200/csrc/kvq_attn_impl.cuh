@@ -1,11 +1,15 @@
 #pragma once
 // kvq_attn_impl.cuh — attention over MLX affine-quantized K/V for sm_100a.
 //
-// One kernel serves decode (L = 1), the context-split partial form and an
-// interim chunked prefill.  Work unit: a CTA owns one (batch, kv head, block
-// of 8*NT query rows, key split).  Query rows are (position, head) pairs of
-// the GQA group (row qr -> position qr / nrep, head qr % nrep), so every K/V
-// byte a CTA streams serves all query heads that share it.
+// Two kernels share the per-slice math:
+//   * attn_kernel — a CTA owns one (batch, kv head, block of 8*NT query
+//     rows, key split): chunked prefill, windowed decode and debug scores;
+//   * attn_bal_kernel — decode over one resident wave of CTAs that split the
+//     concatenated key tiles of all (batch, kv head) units evenly, so every
+//     SM streams the same bytes whatever the lengths in the batch.
+// Query rows are (position, head) pairs of the GQA group (row qr ->
+// position qr / nrep, head qr % nrep), so every K/V byte a CTA streams
+// serves all query heads that share it.
 //
 // CTA = W consumer warps + 1 producer warp (warp specialised):
 //   * the producer streams the split's key rows in chunks of CH = W*RW rows:
@@ -59,6 +63,7 @@ constexpr int kTile = 16;                     // rows per MMA tile; row-alignmen
 constexpr long long kWaitLimit = 1ll << 30;   // mbarrier polls before declaring a hang
 constexpr uint64_t kWaitNs = 2000000000ull;   // ... or 2 s of %globaltimer, whichever first
 constexpr int kMergeMax = 64;                 // splits the last CTA merges through shared memory
+constexpr int kBalMinTiles = 8;                // balanced decode: key tiles per CTA at least (one chunk)
 
 struct Params {
   const uint8_t* kp;
@@ -82,6 +87,8 @@ struct Params {
   int Hq, Hkv, nrep, N, L, QB, rps, nsplit, mode, mask_mode, window;
   float scale;
   int bf16;
+  int B;                 // batch entries (balanced kernel)
+  int Tu;                // key tiles of a unit of N rows (balanced kernel)
 };
 
 // ---------------------------------------------------------------- PTX ----
@@ -280,18 +287,28 @@ struct Geo {
   static_assert(KB >= 4, "unsupported group size / bits");
 };
 
-template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
-struct Smem {
+// Offsets of one ring stage holding CH key rows of the six K/V arrays.
+template <int BITS, int D, int GS, int CH>
+struct StageLayout {
   using G = Geo<BITS, D, GS>;
-  static constexpr int HQ = 8 * NT;
-  static constexpr int CH = W * RW;                            // key rows per chunk
-  static constexpr int O_KP = 0;                               // offsets inside a stage
+  static constexpr int O_KP = 0;
   static constexpr int O_KS = O_KP + CH * G::KRB;
   static constexpr int O_KB = O_KS + CH * G::SRB;
   static constexpr int O_VP = O_KB + CH * G::SRB;
   static constexpr int O_VS = O_VP + CH * G::KRB;
   static constexpr int O_VB = O_VS + CH * G::SRB;
   static constexpr int STAGE = O_VB + CH * G::SRB;
+  static_assert((CH * G::SRB) % 16 == 0, "scale rows must tile in 16-byte units");
+};
+
+// Shared memory of the split kernel: barriers, merge scratch, then the ring
+// (reused as the warp-merge buffer once every stage is consumed).
+template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
+struct Smem {
+  using G = Geo<BITS, D, GS>;
+  static constexpr int HQ = 8 * NT;
+  static constexpr int CH = W * RW;                            // key rows per chunk
+  static constexpr int STAGE = StageLayout<BITS, D, GS, CH>::STAGE;
   static constexpr int BARS = 0;                               // full[ST], empty[ST]
   static constexpr int CTRL = BARS + 2 * STAGES * 8;           // ints
   static constexpr int WM = CTRL + 16;                         // f32 [W][HQ] warp maxima
@@ -304,16 +321,535 @@ struct Smem {
   static constexpr int MERGE_BYTES = W * HQ * D * 4;
   static constexpr int TOTAL =
       STAGES_OFF + (STAGE_BYTES > MERGE_BYTES ? STAGE_BYTES : MERGE_BYTES);
-  static_assert((CH * G::SRB) % 16 == 0, "scale rows must tile in 16-byte units");
 };
 
-template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES, bool BF>
-__global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
+// Shared memory of the balanced kernel: the ring keeps streaming while the
+// consumer warps close a segment, so the warp-merge buffer is separate.
+constexpr int kBalMaxBatch = 256;  // ragged batches up to this size use the balanced kernel
+template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
+struct BalSmem {
   using G = Geo<BITS, D, GS>;
+  static constexpr int HQ = 8 * NT;
+  static constexpr int CH = W * RW;
+  static constexpr int STAGE = StageLayout<BITS, D, GS, CH>::STAGE;
+  static constexpr int BARS = 0;
+  static constexpr int CTRL = BARS + 2 * STAGES * 8;
+  static constexpr int WM = CTRL + 16;
+  static constexpr int WL = WM + W * HQ * 4;
+  static constexpr int RM = WL + W * HQ * 4;
+  static constexpr int RL = RM + HQ * 4;
+  static constexpr int SW = RL + HQ * 4;
+  static constexpr int BS = (SW + HQ * kMergeMax * 4 + 7) / 8 * 8;   // i64 [B+1] first tile of each entry
+  static constexpr int BL = BS + (kBalMaxBatch + 1) * 8;             // int [B] key rows of each entry
+  static constexpr int MRG = (BL + kBalMaxBatch * 4 + 127) / 128 * 128;  // f32 [2][HQ][D]
+  static constexpr int STAGES_OFF = MRG + 2 * HQ * D * 4;
+  static constexpr int TOTAL = STAGES_OFF + STAGES * STAGE;
+};
+
+// Running state of one consumer warp.
+template <int BITS, int D, int GS, int NT>
+struct WarpAcc {
+  using G = Geo<BITS, D, GS>;
+  float m_run[NT][2], l_run[NT][2], mls_run[NT][2], pb[NT][G::NG][2];
+  float o_acc[G::MT][NT][4];
+  __device__ __forceinline__ void reset() {
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        m_run[nt][hh] = kNeg;
+        mls_run[nt][hh] = kNeg * kLog2e;
+        l_run[nt][hh] = 0.0f;
+#pragma unroll
+        for (int grp = 0; grp < G::NG; grp++) pb[nt][grp][hh] = 0.0f;
+      }
+#pragma unroll
+    for (int mt = 0; mt < G::MT; mt++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) o_acc[mt][nt][c] = 0.0f;
+  }
+};
+
+// Query operand of one consumer lane (the B operand of QK).
+template <int BITS, int D, int GS, int NT>
+struct QFrag {
+  using G = Geo<BITS, D, GS>;
+  uint32_t qbf[G::KSTEPS][NT][2];
+  float qs_r[NT][G::NG][2];
+};
+
+// Lane (g, t) holds q * dtype(scale) (rounded to dtype, like mulScalar) of
+// query row qr0 + nt*8 + g at the d positions its K fragments pair with,
+// read straight from global memory; sum(q) per group comes from the 4 lanes
+// t of the row, then moves to the lanes that own each column of the score tile.
+template <int BITS, int D, int GS, int NT, bool BF>
+__device__ __forceinline__ void load_qfrag(QFrag<BITS, D, GS, NT>& f, const Params& p, int b,
+                                           int kvh, int qr0, int qrows, int g, int t) {
+  using G = Geo<BITS, D, GS>;
+  const int nrep = p.nrep, L = p.L;
+  const float scale_dt = round_dt<BF>(p.scale);
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    const int qr = qr0 + nt * 8 + g;
+    const bool qvalid = qr < qrows;
+    const int l = qvalid ? qr / nrep : 0, hh = qvalid ? qr - l * nrep : 0;
+    const uint16_t* qrow = p.q + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * D;
+    float gsum[G::NG];
+#pragma unroll
+    for (int grp = 0; grp < G::NG; grp++) gsum[grp] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < G::KSTEPS; kk++) {
+      const int grp = kk / G::MTG, kin = kk % G::MTG;
+#pragma unroll
+      for (int w2 = 0; w2 < 2; w2++) {
+        const int v = 2 * kin + w2;
+        int d_lo, d_hi;
+        float fac = 1.0f;
+        if (BITS == 4) {
+          const int wi = v / 4, x = v % 4;
+          const int base = grp * GS + t * (GS / 4) + 8 * wi;
+          d_lo = base + x;
+          d_hi = base + x + 4;
+          if (x & 1) fac = 0.0625f;
+        } else {
+          const int wi = v / 2, x = v % 2;
+          const int base = grp * GS + t * (GS / 4) + 4 * wi;
+          d_lo = base + 2 * x;
+          d_hi = base + 2 * x + 1;
+        }
+        const float a0 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d_lo)) * scale_dt) : 0.0f;
+        const float a1 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d_hi)) * scale_dt) : 0.0f;
+        gsum[grp] += a0 + a1;
+        f.qbf[kk][nt][w2] = pack_h2(a0 * fac, a1 * fac);
+      }
+    }
+#pragma unroll
+    for (int grp = 0; grp < G::NG; grp++) {
+      float v = gsum[grp];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      // column 2t + hh of this n-tile is query row nt*8 + 2t + hh, held by lanes g = 2t + hh
+      f.qs_r[nt][grp][0] = __shfl_sync(0xffffffffu, v, (2 * t) << 2);
+      f.qs_r[nt][grp][1] = __shfl_sync(0xffffffffu, v, (2 * t + 1) << 2);
+    }
+  }
+}
+
+// Key-index limits (inclusive) of this lane's query columns.
+template <int NT>
+__device__ __forceinline__ void column_bounds(int (&klo)[NT][2], int (&khi)[NT][2],
+                                              const Params& p, int qr0, int qrows, int Nb, int t) {
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      const int qr = qr0 + nt * 8 + 2 * t + hh;
+      int a = 0, z = Nb - 1;
+      if (p.mask_mode == 1 && qr < qrows) {
+        const int pos = Nb - p.L + qr / p.nrep;
+        z = min(z, pos);
+        if (p.window > 0) a = max(0, pos - p.window + 1);
+      }
+      klo[nt][hh] = a;
+      khi[nt][hh] = z;
+    }
+}
+
+// One consumer slice: RW key rows of the stage at `st` (chunk rows r_base..,
+// global key rows srow0..), valid below n1; `fast` = every row valid for
+// every column (no masking work).
+template <int BITS, int D, int GS, int NT, int RW, int CH, bool BF>
+__device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
+                                              const QFrag<BITS, D, GS, NT>& Q, const Params& p,
+                                              const uint8_t* st, int r_base, int srow0, int n1,
+                                              bool fast, const int (&klo)[NT][2],
+                                              const int (&khi)[NT][2], int qr0, int qrows,
+                                              int kvh, int b, int g, int t) {
+  using G = Geo<BITS, D, GS>;
+  using Lay = StageLayout<BITS, D, GS, CH>;
+  constexpr int MTS = RW / 16;  // 16-row m-tiles per consumer slice
+  const int nrep = p.nrep, L = p.L;
+  auto& m_run = A.m_run;
+  auto& l_run = A.l_run;
+  auto& mls_run = A.mls_run;
+  auto& pb = A.pb;
+  auto& o_acc = A.o_acc;
+  const auto& qbf = Q.qbf;
+  const auto& qs_r = Q.qs_r;
+  // ---------------- scores ----------------
+  float sc[MTS][NT][4];
+#pragma unroll
+  for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int cc = 0; cc < 4; cc++) sc[mt][nt][cc] = 0.0f;
+#pragma unroll
+  for (int mt = 0; mt < MTS; mt++) {
+    const int R0 = r_base + mt * 16 + g, R1 = R0 + 8;
+    float ks0[G::NG], kb0[G::NG], ks1[G::NG], kb1[G::NG];
+    lds_scales<G::NG, BF>(ks0, reinterpret_cast<const uint16_t*>(st + Lay::O_KS) + R0 * G::NG);
+    lds_scales<G::NG, BF>(kb0, reinterpret_cast<const uint16_t*>(st + Lay::O_KB) + R0 * G::NG);
+    lds_scales<G::NG, BF>(ks1, reinterpret_cast<const uint16_t*>(st + Lay::O_KS) + R1 * G::NG);
+    lds_scales<G::NG, BF>(kb1, reinterpret_cast<const uint16_t*>(st + Lay::O_KB) + R1 * G::NG);
+#pragma unroll
+    for (int grp = 0; grp < G::NG; grp++) {
+      uint32_t kw0[G::KW], kw1[G::KW];
+      lds_words<G::KB>(kw0, st + Lay::O_KP + R0 * G::KRB + grp * G::GB + t * G::KB);
+      lds_words<G::KB>(kw1, st + Lay::O_KP + R1 * G::KRB + grp * G::GB + t * G::KB);
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+      }
+#pragma unroll
+      for (int kin = 0; kin < G::MTG; kin++) {
+        uint32_t a[4];
+#pragma unroll
+        for (int w2 = 0; w2 < 2; w2++) {
+          const int v = 2 * kin + w2;
+          const int wi = BITS == 4 ? v / 4 : v / 2;
+          const int x = BITS == 4 ? v % 4 : v % 2;
+          a[2 * w2] = k_extract<BITS>(kw0[wi], x);
+          a[2 * w2 + 1] = k_extract<BITS>(kw1[wi], x);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+          mma16816(acc[nt], a, qbf[grp * G::MTG + kin][nt][0],
+                   qbf[grp * G::MTG + kin][nt][1]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        sc[mt][nt][0] = fmaf(ks0[grp], acc[nt][0], fmaf(kb0[grp], qs_r[nt][grp][0], sc[mt][nt][0]));
+        sc[mt][nt][1] = fmaf(ks0[grp], acc[nt][1], fmaf(kb0[grp], qs_r[nt][grp][1], sc[mt][nt][1]));
+        sc[mt][nt][2] = fmaf(ks1[grp], acc[nt][2], fmaf(kb1[grp], qs_r[nt][grp][0], sc[mt][nt][2]));
+        sc[mt][nt][3] = fmaf(ks1[grp], acc[nt][3], fmaf(kb1[grp], qs_r[nt][grp][1], sc[mt][nt][3]));
+      }
+    }
+  }
+
+  // ---------------- online softmax ----------------
+  // Logits rounded to the dtype, masked to kNeg.  When no lane sees a
+  // logit above its column's running max (most slices once a few have
+  // passed) the max, and so every scale factor, is unchanged: skip the
+  // cross-lane reduction and the rescale.  Otherwise do the full update.
+  float pr[MTS][NT][4];
+  float alpha[NT][2];
+  bool rescale = false;
+  float x[NT][2][MTS][2];
+  bool vv[NT][2][MTS][2];
+  bool above = false;
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+      for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int r = srow0 + mt * 16 + g + 8 * e;
+          const float rs = round_dt<BF>(sc[mt][nt][2 * e + hh]);
+          if (fast) {
+            vv[nt][hh][mt][e] = true;
+            x[nt][hh][mt][e] = rs;
+          } else {
+            vv[nt][hh][mt][e] = r < n1 && r >= klo[nt][hh] && r <= khi[nt][hh];
+            x[nt][hh][mt][e] = vv[nt][hh][mt][e] ? rs : kNeg;
+            if (p.scores && vv[nt][hh][mt][e]) {
+              const int qr = qr0 + nt * 8 + 2 * t + hh;
+              if (qr < qrows) {
+                const int l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
+                p.scores[(((int64_t)b * p.Hq + hq) * L + l) * p.N + r] = rs;
+              }
+            }
+          }
+          above |= x[nt][hh][mt][e] > m_run[nt][hh];
+        }
+  if (__any_sync(0xffffffffu, above)) {
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        float tm = x[nt][hh][0][0];
+#pragma unroll
+        for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+          for (int e = 0; e < 2; e++) tm = fmaxf(tm, x[nt][hh][mt][e]);
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
+        const float mn = fmaxf(m_run[nt][hh], tm);
+        // (m_old - m_new) first: exactly 0 when the max is unchanged, even at
+        // the -1e30 sentinel (an fma against the rounded product would leave
+        // its rounding residual, ~1e23 there, and 2^that is inf).
+        const float al = ex2((m_run[nt][hh] - mn) * kLog2e);
+        rescale |= (mn != m_run[nt][hh]);
+        alpha[nt][hh] = al;
+        m_run[nt][hh] = mn;
+        mls_run[nt][hh] = mn * kLog2e;
+        float lsum = 0.0f;
+#pragma unroll
+        for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+          for (int e = 0; e < 2; e++) {
+            const float pe = ex2(fmaf(x[nt][hh][mt][e], kLog2e, -mls_run[nt][hh]));
+            const float pv = (fast || vv[nt][hh][mt][e]) ? pe : 0.0f;
+            pr[mt][nt][2 * e + hh] = pv;
+            lsum += pv;
+          }
+        l_run[nt][hh] = fmaf(l_run[nt][hh], al, lsum);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        float lsum = 0.0f;
+#pragma unroll
+        for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+          for (int e = 0; e < 2; e++) {
+            const float pe = ex2(fmaf(x[nt][hh][mt][e], kLog2e, -mls_run[nt][hh]));
+            const float pv = (fast || vv[nt][hh][mt][e]) ? pe : 0.0f;
+            pr[mt][nt][2 * e + hh] = pv;
+            lsum += pv;
+          }
+        l_run[nt][hh] += lsum;
+      }
+  }
+  if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+      for (int mt = 0; mt < G::MT; mt++) {
+        o_acc[mt][nt][0] *= alpha[nt][0];
+        o_acc[mt][nt][1] *= alpha[nt][1];
+        o_acc[mt][nt][2] *= alpha[nt][0];
+        o_acc[mt][nt][3] *= alpha[nt][1];
+      }
+#pragma unroll
+      for (int grp = 0; grp < G::NG; grp++) {
+        pb[nt][grp][0] *= alpha[nt][0];
+        pb[nt][grp][1] *= alpha[nt][1];
+      }
+    }
+  }
+
+  // ---------------- P V ----------------
+#pragma unroll
+  for (int kk = 0; kk < MTS; kk++) {  // 16-row k-steps of the slice
+    const int R0 = r_base + kk * 16 + g, R1 = R0 + 8;
+    float vs0[G::NG], vb0[G::NG], vs1[G::NG], vb1[G::NG];
+    lds_scales<G::NG, BF>(vs0, reinterpret_cast<const uint16_t*>(st + Lay::O_VS) + R0 * G::NG);
+    lds_scales<G::NG, BF>(vb0, reinterpret_cast<const uint16_t*>(st + Lay::O_VB) + R0 * G::NG);
+    lds_scales<G::NG, BF>(vs1, reinterpret_cast<const uint16_t*>(st + Lay::O_VS) + R1 * G::NG);
+    lds_scales<G::NG, BF>(vb1, reinterpret_cast<const uint16_t*>(st + Lay::O_VB) + R1 * G::NG);
+    const int vr = r_base + kk * 16 + 2 * t;
+#pragma unroll
+    for (int grp = 0; grp < G::NG; grp++) {
+      uint32_t bfr[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        // p == 0 for masked rows: select, never multiply stale scales.
+        const float p0 = pr[kk][nt][0], p1 = pr[kk][nt][1], p2 = pr[kk][nt][2],
+                    p3 = pr[kk][nt][3];
+        float q0, q1, q2, q3;
+        if (fast) {
+          pb[nt][grp][0] = fmaf(p0, vb0[grp], fmaf(p2, vb1[grp], pb[nt][grp][0]));
+          pb[nt][grp][1] = fmaf(p1, vb0[grp], fmaf(p3, vb1[grp], pb[nt][grp][1]));
+          q0 = p0 * vs0[grp];
+          q1 = p1 * vs0[grp];
+          q2 = p2 * vs1[grp];
+          q3 = p3 * vs1[grp];
+        } else {
+          pb[nt][grp][0] += (p0 != 0.0f ? p0 * vb0[grp] : 0.0f) + (p2 != 0.0f ? p2 * vb1[grp] : 0.0f);
+          pb[nt][grp][1] += (p1 != 0.0f ? p1 * vb0[grp] : 0.0f) + (p3 != 0.0f ? p3 * vb1[grp] : 0.0f);
+          q0 = p0 != 0.0f ? p0 * vs0[grp] : 0.0f;
+          q1 = p1 != 0.0f ? p1 * vs0[grp] : 0.0f;
+          q2 = p2 != 0.0f ? p2 * vs1[grp] : 0.0f;
+          q3 = p3 != 0.0f ? p3 * vs1[grp] : 0.0f;
+        }
+        bfr[nt][0] = movmatrix_t(pack_h2(q0, q1));
+        bfr[nt][1] = movmatrix_t(pack_h2(q2, q3));
+      }
+      uint32_t vw[4][G::VW];
+      const uint8_t* vrow = st + Lay::O_VP + grp * G::GB + g * G::VB;
+      lds_words<G::VB>(vw[0], vrow + (vr)*G::KRB);
+      lds_words<G::VB>(vw[1], vrow + (vr + 1) * G::KRB);
+      lds_words<G::VB>(vw[2], vrow + (vr + 8) * G::KRB);
+      lds_words<G::VB>(vw[3], vrow + (vr + 9) * G::KRB);
+      uint32_t af[G::MTG][4];
+#pragma unroll
+      for (int cc = 0; cc < G::C; cc++) {
+        const uint32_t sel = (cc & 1) ? 0x7632u : 0x5410u;
+        const uint32_t Tlo = prmt(vw[0][cc / 2], vw[1][cc / 2], sel);
+        const uint32_t Thi = prmt(vw[2][cc / 2], vw[3][cc / 2], sel);
+#pragma unroll
+        for (int j = 0; j < G::E; j++) {
+          const int sl = cc * G::E + j;
+          const int mt = sl % G::MTG, half = sl / G::MTG;
+          af[mt][half] = v_extract<BITS>(Tlo, j);      // a0 (m-row g) / a1 (m-row g+8)
+          af[mt][2 + half] = v_extract<BITS>(Thi, j);  // a2 / a3
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < G::MTG; mt++)
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+          mma16816(o_acc[grp * G::MTG + mt][nt], af[mt], bfr[nt][0], bfr[nt][1]);
+    }
+  }
+}
+
+// Row-lane reductions of l and the bias sums at the end of a warp's work.
+template <int BITS, int D, int GS, int NT>
+__device__ __forceinline__ void warp_reduce(WarpAcc<BITS, D, GS, NT>& A) {
+  using G = Geo<BITS, D, GS>;
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      float l = A.l_run[nt][hh];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      A.l_run[nt][hh] = l;
+#pragma unroll
+      for (int grp = 0; grp < G::NG; grp++) {
+        float v = A.pb[nt][grp][hh];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        A.pb[nt][grp][hh] = v;
+      }
+    }
+}
+
+// Rescale a warp's partial to the block maxima (from wm) so the cross-warp
+// combine is a plain sum; lanes g == 0 publish l (wl) and warp 0 the maxima (rm).
+template <int BITS, int D, int GS, int NT, int W>
+__device__ __forceinline__ void rescale_warp(WarpAcc<BITS, D, GS, NT>& A, const float* wm,
+                                             float* wl, float* rm, int warp, int g, int t) {
+  using G = Geo<BITS, D, GS>;
+  constexpr int HQ = 8 * NT;
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      const int col = nt * 8 + 2 * t + hh;
+      float M = wm[col];
+#pragma unroll
+      for (int w = 1; w < W; w++) M = fmaxf(M, wm[w * HQ + col]);
+      const float f = ex2((A.m_run[nt][hh] - M) * kLog2e);
+      A.l_run[nt][hh] *= f;
+#pragma unroll
+      for (int grp = 0; grp < G::NG; grp++) A.pb[nt][grp][hh] *= f;
+#pragma unroll
+      for (int mtg = 0; mtg < G::MT; mtg++) {
+        A.o_acc[mtg][nt][hh] *= f;
+        A.o_acc[mtg][nt][2 + hh] *= f;
+      }
+      if (g == 0) {
+        wl[warp * HQ + col] = A.l_run[nt][hh];
+        if (warp == 0) rm[col] = M;
+      }
+    }
+}
+
+// Write (or add) a warp's output partial o * fac + sum(p * bias) into wo [HQ][D].
+template <int BITS, int D, int GS, int NT, bool ADD>
+__device__ __forceinline__ void store_warp(const WarpAcc<BITS, D, GS, NT>& A, float* wo, int g,
+                                           int t) {
+  using G = Geo<BITS, D, GS>;
+#pragma unroll
+  for (int mtg = 0; mtg < G::MT; mtg++) {
+    const int grp = mtg / G::MTG, mt = mtg % G::MTG;
+    const float fac = (BITS == 4 && (mt & 1)) ? 0.0625f : 1.0f;
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+      const int sl = half * G::MTG + mt;
+      const int cc = sl / G::E, j = sl % G::E;
+      const int d = grp * GS + (g * G::C + cc) * G::E + j;
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+          const float v = fmaf(A.o_acc[mtg][nt][half * 2 + hh], fac, A.pb[nt][grp][hh]);
+          float* dst = wo + (nt * 8 + 2 * t + hh) * D + d;
+          if (ADD) *dst += v;
+          else *dst = v;
+        }
+    }
+  }
+}
+
+// One output element of query row `orow`: the normalised result (mode 0) or
+// the unnormalised partial with its (m, l) (mode 1).
+template <int D, bool BF>
+__device__ __forceinline__ void write_row(const Params& p, int64_t orow, int d, float O, float M,
+                                          float Lsum) {
+  if (p.mode == 0) {
+    p.out[orow * D + d] = f_to_dt<BF>(Lsum > 0.0f ? O / Lsum : 0.0f);
+  } else {
+    p.po[orow * D + d] = O;
+    if (d == 0) {
+      p.pm[orow] = M;
+      p.pl[orow] = Lsum;
+    }
+  }
+}
+
+// acc + sum_j o0[j * stride] * w[j], in j order (deterministic).
+__device__ __forceinline__ float merge_sum(const float* o0, int64_t stride, const float* w, int n,
+                                           float acc) {
+  int j = 0;
+  for (; j + 4 <= n; j += 4) {
+    const float v0 = __ldcg(o0 + (int64_t)(j + 0) * stride);
+    const float v1 = __ldcg(o0 + (int64_t)(j + 1) * stride);
+    const float v2 = __ldcg(o0 + (int64_t)(j + 2) * stride);
+    const float v3 = __ldcg(o0 + (int64_t)(j + 3) * stride);
+    acc = fmaf(v0, w[j], acc);
+    acc = fmaf(v1, w[j + 1], acc);
+    acc = fmaf(v2, w[j + 2], acc);
+    acc = fmaf(v3, w[j + 3], acc);
+  }
+  for (; j < n; j++) acc = fmaf(__ldcg(o0 + (int64_t)j * stride), w[j], acc);
+  return acc;
+}
+
+// Issue the six bulk copies of `rows` (a multiple of 16) key rows starting
+// at row `row` of the (b, h) pair whose first rows are kbase / vbase.
+template <int BITS, int D, int GS, int CH>
+__device__ __forceinline__ void issue_chunk(const Params& p, uint8_t* st, uint64_t* bar,
+                                            int64_t kbase, int64_t vbase, int64_t row,
+                                            uint32_t rows) {
+  using G = Geo<BITS, D, GS>;
+  using Lay = StageLayout<BITS, D, GS, CH>;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  mbar_expect_tx(bar, rows * G::ROWB);
+  bulk_g2s(st + Lay::O_KP, p.kp + (kbase + row) * G::KRB, rows * G::KRB, bar);
+  bulk_g2s(st + Lay::O_KS, p.ks + (kbase + row) * G::NG, rows * G::SRB, bar);
+  bulk_g2s(st + Lay::O_KB, p.kb + (kbase + row) * G::NG, rows * G::SRB, bar);
+  bulk_g2s(st + Lay::O_VP, p.vp + (vbase + row) * G::KRB, rows * G::KRB, bar);
+  bulk_g2s(st + Lay::O_VS, p.vs + (vbase + row) * G::NG, rows * G::SRB, bar);
+  bulk_g2s(st + Lay::O_VB, p.vb + (vbase + row) * G::NG, rows * G::SRB, bar);
+}
+
+// Barrier among the consumer warps only (the producer warp streams on).
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// ------------------------------------------------------------ split kernel --
+
+template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES, bool BF>
+__global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_kernel(const Params p) {
   using S = Smem<BITS, D, GS, NT, W, RW, STAGES>;
   constexpr int HQ = S::HQ;
   constexpr int CH = S::CH;
-  constexpr int MTS = RW / 16;  // 16-row m-tiles per consumer slice
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BARS);
   uint64_t* empty = full + STAGES;
@@ -378,45 +914,20 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
   auto produce = [&](int c) -> bool {
     const int s = c % STAGES;
     if (c >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1))) return false;
-    const int64_t row = n0 + (int64_t)c * CH;
-    const int rows = min(CH, n1 - (int)(row));
+    const int row = n0 + c * CH;
+    const int rows = min(CH, n1 - row);
     const uint32_t cr = (uint32_t)((rows + kTile - 1) / kTile * kTile);
-    uint8_t* st = stages + s * S::STAGE;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(&full[s], cr * G::ROWB);
-    bulk_g2s(st + S::O_KP, p.kp + (kbase + row) * G::KRB, cr * G::KRB, &full[s]);
-    bulk_g2s(st + S::O_KS, p.ks + (kbase + row) * G::NG, cr * G::SRB, &full[s]);
-    bulk_g2s(st + S::O_KB, p.kb + (kbase + row) * G::NG, cr * G::SRB, &full[s]);
-    bulk_g2s(st + S::O_VP, p.vp + (vbase + row) * G::KRB, cr * G::KRB, &full[s]);
-    bulk_g2s(st + S::O_VS, p.vs + (vbase + row) * G::NG, cr * G::SRB, &full[s]);
-    bulk_g2s(st + S::O_VB, p.vb + (vbase + row) * G::NG, cr * G::SRB, &full[s]);
+    issue_chunk<BITS, D, GS, CH>(p, stages + s * S::STAGE, &full[s], kbase, vbase, row, cr);
     return true;
   };
   // Prologue before any block-wide barrier: fill the ring (no waits needed).
   if (producer && lane == 0)
     for (int c = 0; c < STAGES && c < nchunks; c++) produce(c);
 
-  float m_run[NT][2], l_run[NT][2], mls_run[NT][2], pb[NT][G::NG][2];
-  float o_acc[G::MT][NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-      m_run[nt][hh] = kNeg;
-      mls_run[nt][hh] = kNeg * kLog2e;
-      l_run[nt][hh] = 0.0f;
-#pragma unroll
-      for (int grp = 0; grp < G::NG; grp++) pb[nt][grp][hh] = 0.0f;
-    }
-#pragma unroll
-  for (int mt = 0; mt < G::MT; mt++)
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int c = 0; c < 4; c++) o_acc[mt][nt][c] = 0.0f;
+  WarpAcc<BITS, D, GS, NT> A;
+  A.reset();
 
   if (producer) {
-    // ---------------- producer: keep the ring full ----------------
     if (lane == 0)
       for (int c = STAGES; c < nchunks; c++)
         if (!produce(c)) {
@@ -424,77 +935,10 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
           break;
         }
   } else {
-    // ---- query fragments (B operand of QK), straight from global memory ----
-    // Lane (g, t) holds q * dtype(scale) (rounded to dtype, like mulScalar)
-    // of query row nt*8 + g at the d positions its K fragments pair with;
-    // sum(q) per group comes from the 4 lanes t of the row, then moves to the
-    // lanes that own each column of the score tile.
-    const float scale_dt = round_dt<BF>(p.scale);
-    uint32_t qbf[G::KSTEPS][NT][2];
-    float qs_r[NT][G::NG][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      const int qr = qr0 + nt * 8 + g;
-      const bool qvalid = qr < qrows;
-      const int l = qvalid ? qr / nrep : 0, hh = qvalid ? qr - l * nrep : 0;
-      const uint16_t* qrow = p.q + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * D;
-      float gsum[G::NG];
-#pragma unroll
-      for (int grp = 0; grp < G::NG; grp++) gsum[grp] = 0.0f;
-#pragma unroll
-      for (int kk = 0; kk < G::KSTEPS; kk++) {
-        const int grp = kk / G::MTG, kin = kk % G::MTG;
-#pragma unroll
-        for (int w2 = 0; w2 < 2; w2++) {
-          const int v = 2 * kin + w2;
-          int d_lo, d_hi;
-          float f = 1.0f;
-          if (BITS == 4) {
-            const int wi = v / 4, x = v % 4;
-            const int base = grp * GS + t * (GS / 4) + 8 * wi;
-            d_lo = base + x;
-            d_hi = base + x + 4;
-            if (x & 1) f = 0.0625f;
-          } else {
-            const int wi = v / 2, x = v % 2;
-            const int base = grp * GS + t * (GS / 4) + 4 * wi;
-            d_lo = base + 2 * x;
-            d_hi = base + 2 * x + 1;
-          }
-          const float a0 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d_lo)) * scale_dt) : 0.0f;
-          const float a1 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d_hi)) * scale_dt) : 0.0f;
-          gsum[grp] += a0 + a1;
-          qbf[kk][nt][w2] = pack_h2(a0 * f, a1 * f);
-        }
-      }
-#pragma unroll
-      for (int grp = 0; grp < G::NG; grp++) {
-        float v = gsum[grp];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        // column 2t + hh of this n-tile is query row nt*8 + 2t + hh, held by lanes g = 2t + hh
-        qs_r[nt][grp][0] = __shfl_sync(0xffffffffu, v, (2 * t) << 2);
-        qs_r[nt][grp][1] = __shfl_sync(0xffffffffu, v, (2 * t + 1) << 2);
-      }
-    }
-
-    // Key-index limits of this lane's query columns (inclusive bounds).
+    QFrag<BITS, D, GS, NT> Q;
+    load_qfrag<BITS, D, GS, NT, BF>(Q, p, b, kvh, qr0, qrows, g, t);
     int klo[NT][2], khi[NT][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int hh = 0; hh < 2; hh++) {
-        const int qr = qr0 + nt * 8 + 2 * t + hh;
-        int a = 0, z = Nb - 1;
-        if (p.mask_mode == 1 && qr < qrows) {
-          const int pos = Nb - L + qr / nrep;
-          z = min(z, pos);
-          if (p.window > 0) a = max(0, pos - p.window + 1);
-        }
-        klo[nt][hh] = a;
-        khi[nt][hh] = z;
-      }
-
+    column_bounds<NT>(klo, khi, p, qr0, qrows, Nb, t);
     for (int c = 0; c < nchunks; c++) {
       const int s = c % STAGES;
       // The decision must be warp-uniform: the slice is full of warp-collective ops.
@@ -502,237 +946,13 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
         hung = true;
         break;
       }
-      const uint8_t* st = stages + s * S::STAGE;
       const int srow0 = n0 + c * CH + warp * RW;  // first key row of this slice
       if (srow0 < n1) {
         const bool fast = !p.scores && srow0 + RW <= n1 && srow0 + RW - 1 <= kz_min &&
                           srow0 >= ka_max;
-        const int r_base = warp * RW;  // slice rows inside the chunk
-
-        // ---------------- scores ----------------
-        float sc[MTS][NT][4];
-#pragma unroll
-        for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-          for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int cc = 0; cc < 4; cc++) sc[mt][nt][cc] = 0.0f;
-#pragma unroll
-        for (int mt = 0; mt < MTS; mt++) {
-          const int R0 = r_base + mt * 16 + g, R1 = R0 + 8;
-          float ks0[G::NG], kb0[G::NG], ks1[G::NG], kb1[G::NG];
-          lds_scales<G::NG, BF>(ks0, reinterpret_cast<const uint16_t*>(st + S::O_KS) + R0 * G::NG);
-          lds_scales<G::NG, BF>(kb0, reinterpret_cast<const uint16_t*>(st + S::O_KB) + R0 * G::NG);
-          lds_scales<G::NG, BF>(ks1, reinterpret_cast<const uint16_t*>(st + S::O_KS) + R1 * G::NG);
-          lds_scales<G::NG, BF>(kb1, reinterpret_cast<const uint16_t*>(st + S::O_KB) + R1 * G::NG);
-#pragma unroll
-          for (int grp = 0; grp < G::NG; grp++) {
-            uint32_t kw0[G::KW], kw1[G::KW];
-            lds_words<G::KB>(kw0, st + S::O_KP + R0 * G::KRB + grp * G::GB + t * G::KB);
-            lds_words<G::KB>(kw1, st + S::O_KP + R1 * G::KRB + grp * G::GB + t * G::KB);
-            float acc[NT][4];
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-              acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
-            }
-#pragma unroll
-            for (int kin = 0; kin < G::MTG; kin++) {
-              uint32_t a[4];
-#pragma unroll
-              for (int w2 = 0; w2 < 2; w2++) {
-                const int v = 2 * kin + w2;
-                const int wi = BITS == 4 ? v / 4 : v / 2;
-                const int x = BITS == 4 ? v % 4 : v % 2;
-                a[2 * w2] = k_extract<BITS>(kw0[wi], x);
-                a[2 * w2 + 1] = k_extract<BITS>(kw1[wi], x);
-              }
-#pragma unroll
-              for (int nt = 0; nt < NT; nt++)
-                mma16816(acc[nt], a, qbf[grp * G::MTG + kin][nt][0],
-                         qbf[grp * G::MTG + kin][nt][1]);
-            }
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-              sc[mt][nt][0] = fmaf(ks0[grp], acc[nt][0], fmaf(kb0[grp], qs_r[nt][grp][0], sc[mt][nt][0]));
-              sc[mt][nt][1] = fmaf(ks0[grp], acc[nt][1], fmaf(kb0[grp], qs_r[nt][grp][1], sc[mt][nt][1]));
-              sc[mt][nt][2] = fmaf(ks1[grp], acc[nt][2], fmaf(kb1[grp], qs_r[nt][grp][0], sc[mt][nt][2]));
-              sc[mt][nt][3] = fmaf(ks1[grp], acc[nt][3], fmaf(kb1[grp], qs_r[nt][grp][1], sc[mt][nt][3]));
-            }
-          }
-        }
-
-        // ---------------- online softmax ----------------
-        // Logits rounded to the dtype, masked to kNeg.  When no lane sees a
-        // logit above its column's running max (most slices once a few have
-        // passed) the max, and so every scale factor, is unchanged: skip the
-        // cross-lane reduction and the rescale.  Otherwise do the full update.
-        float pr[MTS][NT][4];
-        float alpha[NT][2];
-        bool rescale = false;
-        float x[NT][2][MTS][2];
-        bool vv[NT][2][MTS][2];
-        bool above = false;
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-          for (int hh = 0; hh < 2; hh++)
-#pragma unroll
-            for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-              for (int e = 0; e < 2; e++) {
-                const int r = srow0 + mt * 16 + g + 8 * e;
-                const float rs = round_dt<BF>(sc[mt][nt][2 * e + hh]);
-                if (fast) {
-                  vv[nt][hh][mt][e] = true;
-                  x[nt][hh][mt][e] = rs;
-                } else {
-                  vv[nt][hh][mt][e] = r < n1 && r >= klo[nt][hh] && r <= khi[nt][hh];
-                  x[nt][hh][mt][e] = vv[nt][hh][mt][e] ? rs : kNeg;
-                  if (p.scores && vv[nt][hh][mt][e]) {
-                    const int qr = qr0 + nt * 8 + 2 * t + hh;
-                    if (qr < qrows) {
-                      const int l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
-                      p.scores[(((int64_t)b * p.Hq + hq) * L + l) * p.N + r] = rs;
-                    }
-                  }
-                }
-                above |= x[nt][hh][mt][e] > m_run[nt][hh];
-              }
-        if (__any_sync(0xffffffffu, above)) {
-#pragma unroll
-          for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-              float tm = x[nt][hh][0][0];
-#pragma unroll
-              for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-                for (int e = 0; e < 2; e++) tm = fmaxf(tm, x[nt][hh][mt][e]);
-              tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
-              tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
-              tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
-              const float mn = fmaxf(m_run[nt][hh], tm);
-              // (m_old - m_new) first: exactly 0 when the max is unchanged, even at
-              // the -1e30 sentinel (an fma against the rounded product would leave
-              // its rounding residual, ~1e23 there, and 2^that is inf).
-              const float al = ex2((m_run[nt][hh] - mn) * kLog2e);
-              rescale |= (mn != m_run[nt][hh]);
-              alpha[nt][hh] = al;
-              m_run[nt][hh] = mn;
-              mls_run[nt][hh] = mn * kLog2e;
-              float lsum = 0.0f;
-#pragma unroll
-              for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                  const float pe = ex2(fmaf(x[nt][hh][mt][e], kLog2e, -mls_run[nt][hh]));
-                  const float pv = (fast || vv[nt][hh][mt][e]) ? pe : 0.0f;
-                  pr[mt][nt][2 * e + hh] = pv;
-                  lsum += pv;
-                }
-              l_run[nt][hh] = fmaf(l_run[nt][hh], al, lsum);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-              float lsum = 0.0f;
-#pragma unroll
-              for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                  const float pe = ex2(fmaf(x[nt][hh][mt][e], kLog2e, -mls_run[nt][hh]));
-                  const float pv = (fast || vv[nt][hh][mt][e]) ? pe : 0.0f;
-                  pr[mt][nt][2 * e + hh] = pv;
-                  lsum += pv;
-                }
-              l_run[nt][hh] += lsum;
-            }
-        }
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-          for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-            for (int mt = 0; mt < G::MT; mt++) {
-              o_acc[mt][nt][0] *= alpha[nt][0];
-              o_acc[mt][nt][1] *= alpha[nt][1];
-              o_acc[mt][nt][2] *= alpha[nt][0];
-              o_acc[mt][nt][3] *= alpha[nt][1];
-            }
-#pragma unroll
-            for (int grp = 0; grp < G::NG; grp++) {
-              pb[nt][grp][0] *= alpha[nt][0];
-              pb[nt][grp][1] *= alpha[nt][1];
-            }
-          }
-        }
-
-        // ---------------- P V ----------------
-#pragma unroll
-        for (int kk = 0; kk < MTS; kk++) {  // 16-row k-steps of the slice
-          const int R0 = r_base + kk * 16 + g, R1 = R0 + 8;
-          float vs0[G::NG], vb0[G::NG], vs1[G::NG], vb1[G::NG];
-          lds_scales<G::NG, BF>(vs0, reinterpret_cast<const uint16_t*>(st + S::O_VS) + R0 * G::NG);
-          lds_scales<G::NG, BF>(vb0, reinterpret_cast<const uint16_t*>(st + S::O_VB) + R0 * G::NG);
-          lds_scales<G::NG, BF>(vs1, reinterpret_cast<const uint16_t*>(st + S::O_VS) + R1 * G::NG);
-          lds_scales<G::NG, BF>(vb1, reinterpret_cast<const uint16_t*>(st + S::O_VB) + R1 * G::NG);
-          const int vr = r_base + kk * 16 + 2 * t;
-#pragma unroll
-          for (int grp = 0; grp < G::NG; grp++) {
-            uint32_t bfr[NT][2];
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-              // p == 0 for masked rows: select, never multiply stale scales.
-              const float p0 = pr[kk][nt][0], p1 = pr[kk][nt][1], p2 = pr[kk][nt][2],
-                          p3 = pr[kk][nt][3];
-              float q0, q1, q2, q3;
-              if (fast) {
-                pb[nt][grp][0] = fmaf(p0, vb0[grp], fmaf(p2, vb1[grp], pb[nt][grp][0]));
-                pb[nt][grp][1] = fmaf(p1, vb0[grp], fmaf(p3, vb1[grp], pb[nt][grp][1]));
-                q0 = p0 * vs0[grp];
-                q1 = p1 * vs0[grp];
-                q2 = p2 * vs1[grp];
-                q3 = p3 * vs1[grp];
-              } else {
-                pb[nt][grp][0] += (p0 != 0.0f ? p0 * vb0[grp] : 0.0f) + (p2 != 0.0f ? p2 * vb1[grp] : 0.0f);
-                pb[nt][grp][1] += (p1 != 0.0f ? p1 * vb0[grp] : 0.0f) + (p3 != 0.0f ? p3 * vb1[grp] : 0.0f);
-                q0 = p0 != 0.0f ? p0 * vs0[grp] : 0.0f;
-                q1 = p1 != 0.0f ? p1 * vs0[grp] : 0.0f;
-                q2 = p2 != 0.0f ? p2 * vs1[grp] : 0.0f;
-                q3 = p3 != 0.0f ? p3 * vs1[grp] : 0.0f;
-              }
-              bfr[nt][0] = movmatrix_t(pack_h2(q0, q1));
-              bfr[nt][1] = movmatrix_t(pack_h2(q2, q3));
-            }
-            uint32_t vw[4][G::VW];
-            const uint8_t* vrow = st + S::O_VP + grp * G::GB + g * G::VB;
-            lds_words<G::VB>(vw[0], vrow + (vr)*G::KRB);
-            lds_words<G::VB>(vw[1], vrow + (vr + 1) * G::KRB);
-            lds_words<G::VB>(vw[2], vrow + (vr + 8) * G::KRB);
-            lds_words<G::VB>(vw[3], vrow + (vr + 9) * G::KRB);
-            uint32_t af[G::MTG][4];
-#pragma unroll
-            for (int cc = 0; cc < G::C; cc++) {
-              const uint32_t sel = (cc & 1) ? 0x7632u : 0x5410u;
-              const uint32_t Tlo = prmt(vw[0][cc / 2], vw[1][cc / 2], sel);
-              const uint32_t Thi = prmt(vw[2][cc / 2], vw[3][cc / 2], sel);
-#pragma unroll
-              for (int j = 0; j < G::E; j++) {
-                const int sl = cc * G::E + j;
-                const int mt = sl % G::MTG, half = sl / G::MTG;
-                af[mt][half] = v_extract<BITS>(Tlo, j);      // a0 (m-row g) / a1 (m-row g+8)
-                af[mt][2 + half] = v_extract<BITS>(Thi, j);  // a2 / a3
-              }
-            }
-#pragma unroll
-            for (int mt = 0; mt < G::MTG; mt++)
-#pragma unroll
-              for (int nt = 0; nt < NT; nt++)
-                mma16816(o_acc[grp * G::MTG + mt][nt], af[mt], bfr[nt][0], bfr[nt][1]);
-          }
-        }
+        process_slice<BITS, D, GS, NT, RW, CH, BF>(A, Q, p, stages + s * S::STAGE, warp * RW,
+                                                   srow0, n1, fast, klo, khi, qr0, qrows, kvh, b,
+                                                   g, t);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -740,75 +960,18 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
   }
   if (hung && lane == 0) atomicExch(p.err, 1);
 
-  // ---- finish each consumer warp: reduce row-lane partials, fold bias sums ----
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-      float l = l_run[nt][hh];
-      l += __shfl_xor_sync(0xffffffffu, l, 4);
-      l += __shfl_xor_sync(0xffffffffu, l, 8);
-      l += __shfl_xor_sync(0xffffffffu, l, 16);
-      l_run[nt][hh] = l;
-#pragma unroll
-      for (int grp = 0; grp < G::NG; grp++) {
-        float v = pb[nt][grp][hh];
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        v += __shfl_xor_sync(0xffffffffu, v, 8);
-        v += __shfl_xor_sync(0xffffffffu, v, 16);
-        pb[nt][grp][hh] = v;
-      }
-    }
+  // ---- finish each consumer warp; combine the warps in shared memory ----
+  warp_reduce<BITS, D, GS, NT>(A);
   if (!producer && g == 0) {
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-      for (int hh = 0; hh < 2; hh++) wm[warp * HQ + nt * 8 + 2 * t + hh] = m_run[nt][hh];
+      for (int hh = 0; hh < 2; hh++) wm[warp * HQ + nt * 8 + 2 * t + hh] = A.m_run[nt][hh];
   }
   __syncthreads();  // every stage consumed (ring reusable) and warp maxima visible
   if (!producer) {
-    // Rescale this warp's partial to the block maximum of each column, then
-    // publish it; the cross-warp combine becomes a plain sum.
-    float* wo = mrg + warp * HQ * D;
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int hh = 0; hh < 2; hh++) {
-        const int col = nt * 8 + 2 * t + hh;
-        float M = wm[col];
-#pragma unroll
-        for (int w = 1; w < W; w++) M = fmaxf(M, wm[w * HQ + col]);
-        const float f = ex2((m_run[nt][hh] - M) * kLog2e);
-        l_run[nt][hh] *= f;
-#pragma unroll
-        for (int grp = 0; grp < G::NG; grp++) pb[nt][grp][hh] *= f;
-#pragma unroll
-        for (int mtg = 0; mtg < G::MT; mtg++) {
-          o_acc[mtg][nt][hh] *= f;
-          o_acc[mtg][nt][2 + hh] *= f;
-        }
-        if (g == 0) {
-          wl[warp * HQ + col] = l_run[nt][hh];
-          if (warp == 0) rm[col] = M;
-        }
-      }
-#pragma unroll
-    for (int mtg = 0; mtg < G::MT; mtg++) {
-      const int grp = mtg / G::MTG, mt = mtg % G::MTG;
-      const float fac = (BITS == 4 && (mt & 1)) ? 0.0625f : 1.0f;
-#pragma unroll
-      for (int half = 0; half < 2; half++) {
-        const int sl = half * G::MTG + mt;
-        const int cc = sl / G::E, j = sl % G::E;
-        const int d = grp * GS + (g * G::C + cc) * G::E + j;
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-          for (int hh = 0; hh < 2; hh++)
-            wo[(nt * 8 + 2 * t + hh) * D + d] =
-                fmaf(o_acc[mtg][nt][half * 2 + hh], fac, pb[nt][grp][hh]);
-      }
-    }
+    rescale_warp<BITS, D, GS, NT, W>(A, wm, wl, rm, warp, g, t);
+    store_warp<BITS, D, GS, NT, false>(A, mrg + warp * HQ * D, g, t);
   }
   __syncthreads();
   if (tid < HQ) {
@@ -832,15 +995,7 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
     const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
     const int64_t orow = ((int64_t)b * p.Hq + hq) * L + l;
     if (single) {
-      if (p.mode == 0) {
-        p.out[orow * D + d] = f_to_dt<BF>(Lsum > 0.0f ? O / Lsum : 0.0f);
-      } else {
-        p.po[orow * D + d] = O;
-        if (d == 0) {
-          p.pm[orow] = M;
-          p.pl[orow] = Lsum;
-        }
-      }
+      write_row<D, BF>(p, orow, d, O, M, Lsum);
     } else {
       const int64_t slot = (cta * p.nsplit + split) * HQ + r;
       p.ws_o[slot * D + d] = O;
@@ -862,7 +1017,7 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
   __syncthreads();
   if (!ctrl[0]) return;
   __threadfence();
-  // Per-row split weights exp(M_s - M) / L in shared memory (nact <= kMergeMax
+  // Per-row split weights exp(M_s - M) in shared memory (nact <= kMergeMax
   // is guaranteed by the launch shape), then independent loads of the O rows.
   if (tid < rows_here) {
     const int r = tid;
@@ -882,34 +1037,278 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_kernel(const Params p) {
   __syncthreads();
   for (int i = tid; i < rows_here * D; i += (W + 1) * 32) {
     const int r = i / D, d = i - r * D;
-    const float* o0 = p.ws_o + ((cta * p.nsplit) * HQ + r) * D + d;
-    float O = 0.0f;
-    int sp = 0;
-    for (; sp + 4 <= nact; sp += 4) {
-      const float v0 = __ldcg(o0 + (int64_t)(sp + 0) * HQ * D);
-      const float v1 = __ldcg(o0 + (int64_t)(sp + 1) * HQ * D);
-      const float v2 = __ldcg(o0 + (int64_t)(sp + 2) * HQ * D);
-      const float v3 = __ldcg(o0 + (int64_t)(sp + 3) * HQ * D);
-      O = fmaf(v0, sw[r * kMergeMax + sp], O);
-      O = fmaf(v1, sw[r * kMergeMax + sp + 1], O);
-      O = fmaf(v2, sw[r * kMergeMax + sp + 2], O);
-      O = fmaf(v3, sw[r * kMergeMax + sp + 3], O);
-    }
-    for (; sp < nact; sp++) O = fmaf(__ldcg(o0 + (int64_t)sp * HQ * D), sw[r * kMergeMax + sp], O);
-    const float Lsum = rl[r];
+    const float O = merge_sum(p.ws_o + ((cta * p.nsplit) * HQ + r) * D + d, (int64_t)HQ * D,
+                              sw + r * kMergeMax, nact, 0.0f);
     const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
-    const int64_t orow = ((int64_t)b * p.Hq + hq) * L + l;
-    if (p.mode == 0) {
-      p.out[orow * D + d] = f_to_dt<BF>(Lsum > 0.0f ? O / Lsum : 0.0f);
-    } else {
-      p.po[orow * D + d] = O;
-      if (d == 0) {
-        p.pm[orow] = rm[r];
-        p.pl[orow] = Lsum;
-      }
-    }
+    write_row<D, BF>(p, ((int64_t)b * p.Hq + hq) * L + l, d, O, rm[r], rl[r]);
   }
   if (tid == 0) p.counters[cta] = 0u;  // leave the ticket ready for the next call
+}
+
+// --------------------------------------------------------- balanced kernel --
+//
+// Decode (L = 1, no window) over one resident wave of C CTAs.  The
+// key tiles (16 rows) of all units u = b*Hkv + kvh are laid end to end,
+// unit u owning tiles [U_u, U_u + T_u); CTA i streams tiles
+// [i*RT/C, (i+1)*RT/C) of the RT in total, so every CTA moves the same bytes
+// whatever the lengths in the batch.  Where its range crosses a unit
+// boundary it closes one segment (the part of a unit it holds) and opens
+// the next; the producer warp streams on across segments while the consumer
+// warps close the previous one.  A unit held by one CTA is written directly;
+// otherwise each holder writes its partial (m, l, o) to slot i + u —
+// consecutive slots for the consecutive holders of u — and the last holder
+// to finish (atomic ticket per unit) merges them in holder order.
+template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES, bool BF>
+__global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) {
+  using S = BalSmem<BITS, D, GS, NT, W, RW, STAGES>;
+  constexpr int HQ = S::HQ;
+  constexpr int CH = S::CH;
+  constexpr int NC = W * 32;  // consumer threads
+  static_assert(W % 2 == 0, "warps pair up in the combine");
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BARS);
+  uint64_t* empty = full + STAGES;
+  volatile int* ctrl = reinterpret_cast<volatile int*>(smem + S::CTRL);  // [0] merge, [1] abort
+  uint8_t* stages = smem + S::STAGES_OFF;
+  float* buf = reinterpret_cast<float*>(smem + S::MRG);  // [2][HQ][D]
+  float* wm = reinterpret_cast<float*>(smem + S::WM);
+  float* wl = reinterpret_cast<float*>(smem + S::WL);
+  float* rm = reinterpret_cast<float*>(smem + S::RM);
+  float* rl = reinterpret_cast<float*>(smem + S::RL);
+  float* sw = reinterpret_cast<float*>(smem + S::SW);
+  int* blen = reinterpret_cast<int*>(smem + S::BL);             // [B] key rows of each entry
+  int64_t* bfirst = reinterpret_cast<int64_t*>(smem + S::BS);   // [B+1] first tile of each entry
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const bool producer = warp == W;
+  const int i = blockIdx.x;
+  const int Hkv = p.Hkv, nrep = p.nrep, qrows = nrep, B = p.B;
+  const bool ragged = p.seq_lens != nullptr;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], W);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    ctrl[1] = 0;
+  }
+  int64_t RT = (int64_t)B * Hkv * p.Tu;
+  if (ragged) {
+    for (int bb = tid; bb < B; bb += blockDim.x) blen[bb] = min(max(p.seq_lens[bb], 0), p.N);
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of Hkv * ceil(len / 16)
+      int64_t run = 0;
+      for (int base = 0; base < B; base += 32) {
+        const int bb = base + lane;
+        const int64_t v = bb < B ? (int64_t)Hkv * ((blen[bb] + kTile - 1) / kTile) : 0;
+        int64_t incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        if (bb < B) bfirst[bb] = run + incl - v;
+        run += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) bfirst[B] = run;
+    }
+    __syncthreads();
+    RT = bfirst[B];
+  } else {
+    __syncthreads();
+  }
+  // Working CTAs: at most one per kBalMinTiles tiles (the host sized the grid
+  // that way from N; with per-entry lengths RT is only known here), so every
+  // working CTA's range is non-empty and holders of a unit are consecutive.
+  int64_t c_work = RT / kBalMinTiles;
+  if (c_work > (int64_t)gridDim.x) c_work = gridDim.x;
+  if (c_work < 1) c_work = 1;
+  const int C = (int)c_work;
+  const int64_t x0 = i < C ? (int64_t)i * RT / C : RT;
+  const int64_t x1 = i < C ? (int64_t)(i + 1) * RT / C : RT;
+
+  // Unit holding tile x: batch entry b, kv head kvh, first tile U, tiles T, rows n.
+  auto unit_at = [&](int64_t x, int& b, int& kvh, int64_t& U, int& T, int& n) {
+    if (!ragged) {
+      const int64_t u = x / p.Tu;
+      b = (int)(u / Hkv);
+      kvh = (int)(u - (int64_t)b * Hkv);
+      U = u * p.Tu;
+      T = p.Tu;
+      n = p.N;
+    } else {
+      int lo = 0, hi = B - 1;  // last entry whose first tile is <= x
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (bfirst[mid] <= x) lo = mid;
+        else hi = mid - 1;
+      }
+      b = lo;
+      n = blen[b];
+      T = (n + kTile - 1) / kTile;
+      kvh = (int)((x - bfirst[b]) / T);
+      U = bfirst[b] + (int64_t)kvh * T;
+    }
+  };
+  // Holder of tile x: the last CTA whose range starts at or before x.
+  auto cta_of = [&](int64_t x) -> int { return (int)(((x + 1) * C - 1) / RT); };
+
+  // Batch entries with no keys: their rows are written here (zeros, or an
+  // empty partial), spread over the CTAs.
+  if (ragged)
+    for (int bb = i; bb < B; bb += gridDim.x)
+      if (blen[bb] == 0)
+        for (int e = tid; e < p.Hq * D; e += blockDim.x)
+          write_row<D, BF>(p, (int64_t)bb * p.Hq + e / D, e % D, 0.0f, kNeg, 0.0f);
+
+  bool hung = false;
+  if (producer) {
+    if (lane == 0) {
+      int c = 0;
+      for (int64_t x = x0; x < x1 && !hung;) {
+        int b, kvh, T, n;
+        int64_t U;
+        unit_at(x, b, kvh, U, T, n);
+        const int64_t xe = x1 < U + T ? x1 : U + T;
+        const int r0 = (int)(x - U) * kTile, r1 = (int)(xe - U) * kTile;
+        const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
+        const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
+        for (int row = r0; row < r1; row += CH, c++) {
+          const int s = c % STAGES;
+          if (c >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1))) {
+            hung = true;
+            ctrl[1] = 1;
+            break;
+          }
+          issue_chunk<BITS, D, GS, CH>(p, stages + s * S::STAGE, &full[s], kbase, vbase, row,
+                                       (uint32_t)min(CH, r1 - row));
+        }
+        x = xe;
+      }
+    }
+  } else {
+    WarpAcc<BITS, D, GS, NT> A;
+    QFrag<BITS, D, GS, NT> Q;
+    int c = 0;
+    for (int64_t x = x0; x < x1;) {
+      int b, kvh, T, n;
+      int64_t U;
+      unit_at(x, b, kvh, U, T, n);
+      const int64_t xe = x1 < U + T ? x1 : U + T;
+      const int r0 = (int)(x - U) * kTile, r1 = (int)(xe - U) * kTile;
+      const int n1 = min(r1, n);
+      load_qfrag<BITS, D, GS, NT, BF>(Q, p, b, kvh, 0, qrows, g, t);
+      int klo[NT][2], khi[NT][2];
+      column_bounds<NT>(klo, khi, p, 0, qrows, n, t);
+      A.reset();
+      for (int row = r0; row < r1; row += CH, c++) {
+        const int s = c % STAGES;
+        // Warp-uniform decision: the slice is full of warp-collective ops.
+        // After a timeout anywhere, skip the waits but keep the structure, so
+        // every consumer still meets every named barrier below.
+        const bool ok = !hung && !ctrl[1] && mbar_wait(&full[s], (uint32_t)((c / STAGES) & 1));
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (!hung && lane == 0) ctrl[1] = 1;
+          hung = true;
+          continue;
+        }
+        const int srow0 = row + warp * RW;
+        if (srow0 < n1)
+          process_slice<BITS, D, GS, NT, RW, CH, BF>(A, Q, p, stages + s * S::STAGE, warp * RW,
+                                                     srow0, n1, srow0 + RW <= n1, klo, khi, 0,
+                                                     qrows, kvh, b, g, t);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+
+      // ---- close the segment: combine the warps in a fixed order ----
+      warp_reduce<BITS, D, GS, NT>(A);
+      if (g == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++) wm[warp * HQ + nt * 8 + 2 * t + hh] = A.m_run[nt][hh];
+      }
+      consumer_sync(NC);
+      rescale_warp<BITS, D, GS, NT, W>(A, wm, wl, rm, warp, g, t);
+      if (warp >= W / 2) store_warp<BITS, D, GS, NT, false>(A, buf + (warp - W / 2) * HQ * D, g, t);
+      consumer_sync(NC);
+      if (warp < W / 2) store_warp<BITS, D, GS, NT, true>(A, buf + warp * HQ * D, g, t);
+      if (tid < HQ) {
+        float Ls = 0.0f;
+#pragma unroll
+        for (int w = 0; w < W; w++) Ls += wl[w * HQ + tid];
+        rl[tid] = Ls;
+      }
+      consumer_sync(NC);
+
+      const int u = b * Hkv + kvh;
+      const int i_first = cta_of(U), nseg = cta_of(U + T - 1) - i_first + 1;
+      const int64_t slot0 = (int64_t)i_first + u;  // partial slots of this unit's holders
+      const int64_t slot = (int64_t)i + u;
+      for (int e = tid; e < qrows * D; e += NC) {
+        const int r = e / D, d = e - r * D;
+        float O = buf[e];
+#pragma unroll
+        for (int w = 1; w < W / 2; w++) O += buf[w * HQ * D + e];
+        const float M = rm[r], Lsum = rl[r];
+        if (nseg == 1) {
+          write_row<D, BF>(p, (int64_t)b * p.Hq + kvh * nrep + r, d, O, M, Lsum);
+        } else {
+          p.ws_o[(slot * HQ + r) * D + d] = O;
+          if (d == 0) {
+            p.ws_ml[(slot * HQ + r) * 2] = M;
+            p.ws_ml[(slot * HQ + r) * 2 + 1] = Lsum;
+          }
+        }
+      }
+      if (nseg > 1) {
+        __threadfence();
+        consumer_sync(NC);
+        if (tid == 0) {
+          const unsigned prev = atomicAdd(&p.counters[u], 1u);
+          ctrl[0] = (prev == (unsigned)(nseg - 1)) ? 1 : 0;
+        }
+        consumer_sync(NC);
+        if (ctrl[0]) {
+          __threadfence();
+          if (tid < qrows) {
+            float M = kNeg;
+            for (int j = 0; j < nseg; j++)
+              M = fmaxf(M, __ldcg(&p.ws_ml[((slot0 + j) * HQ + tid) * 2]));
+            float Ls = 0.0f;
+            for (int j = 0; j < nseg; j++) {
+              const int64_t sj = (slot0 + j) * HQ + tid;
+              Ls += __ldcg(&p.ws_ml[sj * 2 + 1]) * ex2((__ldcg(&p.ws_ml[sj * 2]) - M) * kLog2e);
+            }
+            rm[tid] = M;
+            rl[tid] = Ls;
+          }
+          // holders in order, kMergeMax at a time; the running sum waits in buf
+          for (int j0 = 0; j0 < nseg; j0 += kMergeMax) {
+            const int nj = min(kMergeMax, nseg - j0);
+            consumer_sync(NC);
+            if (tid < qrows)
+              for (int j = 0; j < nj; j++)
+                sw[tid * kMergeMax + j] =
+                    ex2((__ldcg(&p.ws_ml[((slot0 + j0 + j) * HQ + tid) * 2]) - rm[tid]) * kLog2e);
+            consumer_sync(NC);
+            for (int e = tid; e < qrows * D; e += NC) {
+              const int r = e / D, d = e - r * D;
+              const float O = merge_sum(p.ws_o + ((slot0 + j0) * HQ + r) * D + d, (int64_t)HQ * D,
+                                        sw + r * kMergeMax, nj, j0 ? buf[e] : 0.0f);
+              if (j0 + nj < nseg) buf[e] = O;
+              else write_row<D, BF>(p, (int64_t)b * p.Hq + kvh * nrep + r, d, O, rm[r], rl[r]);
+            }
+          }
+          if (tid == 0) p.counters[u] = 0u;  // leave the ticket ready for the next call
+        }
+      }
+      x = xe;
+    }
+  }
+  if (hung && lane == 0) atomicExch(p.err, 1);
 }
 
 // ------------------------------------------------------------ host side --
@@ -930,6 +1329,7 @@ constexpr int stages_for() {
 
 struct LaunchShape {
   int QB, nsplit, rps;
+  int ctas = 0;  // > 0: balanced kernel with this many CTAs (one wave)
 };
 
 inline int num_sms(int dev) {
@@ -975,13 +1375,85 @@ constexpr size_t kTicketOff = 256;
 constexpr size_t kPartialOff = kTicketOff + 4 * kMaxTickets;
 
 inline size_t ws_bytes_for(int B, int Hkv, const LaunchShape& s, int NT, int D) {
+  if (s.ctas > 0) {  // balanced: partial slots i + u, i < ctas, u < B * Hkv
+    const size_t slots = ((size_t)s.ctas + (size_t)B * Hkv) * 8 * NT;
+    return kPartialOff + (slots * 2 * 4 + 255) / 256 * 256 + slots * D * 4;
+  }
   if (s.nsplit <= 1) return kPartialOff;
   const size_t slots = (size_t)B * Hkv * s.QB * s.nsplit * 8 * NT;
   return kPartialOff + (slots * 2 * 4 + 255) / 256 * 256 + slots * D * 4;
 }
 
-// Per-width launchers (one translation unit each, compiled in parallel).
-// With occ != nullptr they only report the kernel's resident blocks per SM.
+// Launch one kernel instance: the balanced decode kernel when s.ctas > 0,
+// else the split kernel.  Blocks per SM are queried once per (kernel,
+// dtype, device) and cached.
+template <int BITS, int D, int GS, int NT>
+int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* occ) {
+  constexpr int RW = rows_per_warp<D, NT>();
+  constexpr int ST = stages_for<BITS, D, GS, RW>();
+  const bool bal = s.ctas > 0;
+  const int smem = bal ? BalSmem<BITS, D, GS, NT, kWarps, RW, ST>::TOTAL
+                       : Smem<BITS, D, GS, NT, kWarps, RW, ST>::TOTAL;
+  void (*kern)(Params);
+  if (bal)
+    kern = p.bf16 ? attn_bal_kernel<BITS, D, GS, NT, kWarps, RW, ST, true>
+                  : attn_bal_kernel<BITS, D, GS, NT, kWarps, RW, ST, false>;
+  else
+    kern = p.bf16 ? attn_kernel<BITS, D, GS, NT, kWarps, RW, ST, true>
+                  : attn_kernel<BITS, D, GS, NT, kWarps, RW, ST, false>;
+  static int blocks[2][2][64] = {};
+  int dev = 0;
+  KVQ_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(KVQ_ERR_ARG, "device ordinal out of range");
+  int& nb = blocks[bal][p.bf16][dev];
+  if (!nb) {
+    KVQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    int n = 0;
+    KVQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kWarps + 1) * 32, smem));
+    nb = n > 0 ? n : 1;
+  }
+  if (occ) {
+    *occ = nb;
+    return KVQ_OK;
+  }
+  const dim3 grid = bal ? dim3(s.ctas) : dim3(s.nsplit, p.Hkv * s.QB, B);
+  kern<<<grid, (kWarps + 1) * 32, smem, st>>>(p);
+  KVQ_CUDA_TRY(cudaGetLastError());
+  return KVQ_OK;
+}
+
+template <int BITS, int D, int GS>
+int32_t pick_nt(Params& p, const LaunchShape& s, int NT, int B, cudaStream_t st, int* occ) {
+  if (NT == 1) return launch_t<BITS, D, GS, 1>(p, s, B, st, occ);
+  return launch_t<BITS, D, GS, 2>(p, s, B, st, occ);
+}
+
+template <int BITS, int D>
+int32_t pick_gs(Params& p, const LaunchShape& s, int GSv, int NT, int B, cudaStream_t st, int* occ) {
+  switch (GSv) {
+    case 32: return pick_nt<BITS, D, 32>(p, s, NT, B, st, occ);
+    case 64: return pick_nt<BITS, D, 64>(p, s, NT, B, st, occ);
+    case 128:
+      if constexpr (D >= 128) return pick_nt<BITS, D, 128>(p, s, NT, B, st, occ);
+      break;
+  }
+  return fail(KVQ_ERR_ARG, "attention: unsupported group_size for this head_dim");
+}
+
+template <int BITS>
+int32_t pick_d(Params& p, const LaunchShape& s, int Dv, int GSv, int NT, int B, cudaStream_t st,
+               int* occ) {
+  switch (Dv) {
+    case 64: return pick_gs<BITS, 64>(p, s, GSv, NT, B, st, occ);
+    case 128: return pick_gs<BITS, 128>(p, s, GSv, NT, B, st, occ);
+    case 256: return pick_gs<BITS, 256>(p, s, GSv, NT, B, st, occ);
+  }
+  return fail(KVQ_ERR_ARG, "attention: head_dim must be 64, 128 or 256");
+}
+
+// Per-width launchers (one translation unit each, compiled in parallel);
+// s.ctas > 0 selects the balanced kernel.  With occ != nullptr they only
+// report that kernel's resident blocks per SM.
 int32_t dispatch_b4(Params& p, const LaunchShape& s, int Dv, int GSv, int NT, int B, cudaStream_t st, int* occ);
 int32_t dispatch_b8(Params& p, const LaunchShape& s, int Dv, int GSv, int NT, int B, cudaStream_t st, int* occ);
 

@@ -86,6 +86,24 @@ def test_decode_ragged_seq_lens():
     assert max_abs(got, want, F16) <= TOL[F16]
 
 
+@pytest.mark.parametrize("lens", [[0, 3000, 0, 17, 1, 0], [1, 17, 0], [0, 0], [2999, 3000, 5, 2048]])
+def test_decode_ragged_with_empty_entries(lens):
+    """Entries with no keys give zero rows; a batch with fewer key tiles than
+    the launch has CTAs still covers every tile exactly once."""
+    got, want = run_decode(len(lens), 8, 2, 3000, 128, 64, 8, F16, seed=5, seq_lens=lens)
+    assert max_abs(got, want, F16) <= TOL[F16]
+    for b, n in enumerate(lens):
+        if n == 0:
+            assert not np.any(O.from_dtype_bits(got[b], F16))
+
+
+def test_decode_one_long_unit_many_holders():
+    """One (batch, kv head) unit over 20000 keys: its tiles spread over more
+    CTAs than one merge pass takes, so the merge runs in several passes."""
+    got, want = run_decode(1, 8, 1, 20000, 128, 64, 4, F16, seed=6)
+    assert max_abs(got, want, F16) <= TOL[F16]
+
+
 def test_decode_through_ring_cache_config3():
     """Config 3 local layer: window 1024 ring after 4096 writes (3 wraps), kv8 D256."""
     import kvq
