@@ -21,10 +21,13 @@
 //     kernel raises a device error flag and leaves its loops.
 //   * consumer warp w takes rows [w*RW, (w+1)*RW) of every chunk.
 // Per consumer slice (RW = 16 or 32 key rows):
-//   * codes become exact fp16 integers in registers with the 0x6400 (=1024)
-//     magic: (bits | 0x6400) - 1024 = c.  Four-bit codes in odd nibbles are
-//     taken unshifted (1024 + 16c) and the factor 16 is folded into the
-//     query.  Scales and biases are factored out of the inner products
+//   * a code c becomes the exact fp16 subnormal c * 2^-24 with one logic op
+//     per pair (the code's bits in the low mantissa bits, exponent field
+//     zero); the tensor cores take subnormal f16 operands exactly, and the
+//     2^24 goes into the K scales and the output factor.  Four-bit codes in
+//     odd nibbles are taken unshifted (16c) and the factor 16 is folded into
+//     the query (K) or the output (V).  Scales and biases are factored out
+//     of the inner products
 //     (qdot factoring, as in mlx-bun's Metal decode kernel,
 //     src/model/fused-decode-kernel.ts:62-114):
 //        q . (s*c + b) = s * (q . c) + b * sum(q)
@@ -38,8 +41,7 @@
 //   * PV: O^T[d x q] += V^T[d x n] (p*s)^T[n x q]; the probability tile goes
 //     from the QK accumulator layout to the B-operand layout with one
 //     movmatrix.trans per 8x8 block; V codes of a (d, 2 rows) pair are
-//     interleaved with one prmt per 16-bit chunk and made exact with one
-//     f16x2 subtract.
+//     interleaved with one prmt per 16-bit chunk.
 //   * splits of the key range merge in fixed order (deterministic) in the
 //     last CTA to finish, found by an atomic ticket — no second launch.
 //
@@ -168,12 +170,8 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
-// (x as f16x2) - (1024, 1024): exact integer codes from the 0x6400 magic.
-__device__ __forceinline__ uint32_t sub1024(uint32_t x) {
-  uint32_t r;
-  asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(0x64006400u));
-  return r;
-}
+// Codes enter the MMAs as f16 subnormals: value = code * 2^-24.
+constexpr float kCodeUnitInv = 16777216.0f;  // 2^24
 
 // 2^x (approximate; flushes results below 2^-126 to zero).
 __device__ __forceinline__ float ex2(float x) {
@@ -205,32 +203,33 @@ __device__ __forceinline__ float round_dt(float f) {
   else return __half2float(__float2half_rn(f));
 }
 
-// K operand (pairs along d within one row), exact: a 4-bit word w holds
-// nibbles e0..e7: x0 = (e0, e4), x1 = 16*(e1, e5), x2 = (e2, e6), x3 =
-// 16*(e3, e7); an 8-bit word: x0 = (b0, b1), x1 = (b2, b3).  (Keeping the
-// 1024 offset and cancelling it in the accumulator loses ~10 bits of the
-// 4-bit products, enough to flip the dtype rounding of large logits.)
+// K operand (pairs along d within one row), in units of 2^-24: a 4-bit
+// word w holds nibbles e0..e7: x0 = (e0, e4), x1 = 16*(e1, e5), x2 = (e2,
+// e6), x3 = 16*(e3, e7); an 8-bit word: x0 = (b0, b1), x1 = (b2, b3).
+// (A normal-range form, 1024 + c with the offset cancelled in the
+// accumulator, loses ~10 bits of the 4-bit products — enough to flip the
+// dtype rounding of large logits; the subnormal form is exact.)
 template <int BITS>
 __device__ __forceinline__ uint32_t k_extract(uint32_t w, int x) {
   if (BITS == 4) {
     const uint32_t s = (x >= 2) ? (w >> 8) : w;
     const uint32_t m = (x & 1) ? 0x00F000F0u : 0x000F000Fu;
-    return sub1024((s & m) | 0x64006400u);
+    return s & m;
   } else {
-    return sub1024(prmt(w, 0x64u, x ? 0x4342u : 0x4140u));
+    return prmt(w, 0u, x ? 0x4342u : 0x4140u);
   }
 }
 
 // V operand: T holds a 16-bit chunk of row r0 (low half) and of row r1 (high
-// half); element j of the chunk as the exact pair (r0, r1).
+// half); element j of the chunk as the pair (r0, r1) in units of 2^-24.
 template <int BITS>
 __device__ __forceinline__ uint32_t v_extract(uint32_t T, int j) {
   if (BITS == 4) {
     const uint32_t s = (j >= 2) ? (T >> 8) : T;
     const uint32_t m = (j & 1) ? 0x00F000F0u : 0x000F000Fu;
-    return sub1024((s & m) | 0x64006400u);
+    return s & m;
   } else {
-    return sub1024(prmt(T, 0x64u, j ? 0x4341u : 0x4240u));
+    return prmt(T, 0u, j ? 0x4341u : 0x4240u);
   }
 }
 
@@ -256,15 +255,15 @@ __device__ __forceinline__ void lds_words(uint32_t* w, const uint8_t* p) {
   }
 }
 
-// All NG scales (or biases) of one row as f32.
+// All NG scales (or biases) of one row as f32, times `mul` (a power of two).
 template <int NG, bool BF>
-__device__ __forceinline__ void lds_scales(float* out, const uint16_t* row) {
+__device__ __forceinline__ void lds_scales(float* out, const uint16_t* row, float mul = 1.0f) {
   uint32_t w[(NG + 1) / 2];
   lds_words<NG * 2>(w, reinterpret_cast<const uint8_t*>(row));
 #pragma unroll
   for (int i = 0; i < NG; i++) {
     const uint16_t h = (uint16_t)((i & 1) ? (w[i / 2] >> 16) : (w[i / 2] & 0xffffu));
-    out[i] = dt_to_f<BF>(h);
+    out[i] = dt_to_f<BF>(h) * mul;
   }
 }
 
@@ -490,9 +489,11 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
   for (int mt = 0; mt < MTS; mt++) {
     const int R0 = r_base + mt * 16 + g, R1 = R0 + 8;
     float ks0[G::NG], kb0[G::NG], ks1[G::NG], kb1[G::NG];
-    lds_scales<G::NG, BF>(ks0, reinterpret_cast<const uint16_t*>(st + Lay::O_KS) + R0 * G::NG);
+    lds_scales<G::NG, BF>(ks0, reinterpret_cast<const uint16_t*>(st + Lay::O_KS) + R0 * G::NG,
+                          kCodeUnitInv);
     lds_scales<G::NG, BF>(kb0, reinterpret_cast<const uint16_t*>(st + Lay::O_KB) + R0 * G::NG);
-    lds_scales<G::NG, BF>(ks1, reinterpret_cast<const uint16_t*>(st + Lay::O_KS) + R1 * G::NG);
+    lds_scales<G::NG, BF>(ks1, reinterpret_cast<const uint16_t*>(st + Lay::O_KS) + R1 * G::NG,
+                          kCodeUnitInv);
     lds_scales<G::NG, BF>(kb1, reinterpret_cast<const uint16_t*>(st + Lay::O_KB) + R1 * G::NG);
 #pragma unroll
     for (int grp = 0; grp < G::NG; grp++) {
@@ -767,7 +768,7 @@ __device__ __forceinline__ void store_warp(const WarpAcc<BITS, D, GS, NT>& A, fl
 #pragma unroll
   for (int mtg = 0; mtg < G::MT; mtg++) {
     const int grp = mtg / G::MTG, mt = mtg % G::MTG;
-    const float fac = (BITS == 4 && (mt & 1)) ? 0.0625f : 1.0f;
+    const float fac = (BITS == 4 && (mt & 1)) ? kCodeUnitInv * 0.0625f : kCodeUnitInv;
 #pragma unroll
     for (int half = 0; half < 2; half++) {
       const int sl = half * G::MTG + mt;
