@@ -222,8 +222,10 @@ int32_t kvq_debug_scores(const kvq_qtensor* keys, const void* q, int32_t q_heads
  * a device looks up that array's device address (make it before any stream
  * capture).  Each call clears the scratch's flag and tickets with a
  * stream-ordered memset; all calls share the array, so calls that overlap
- * on the GPU race — issue them on one stream.  Shapes whose split partials
- * do not fit return KVQ_ERR_WORKSPACE with the sizes in kvq_last_error(). */
+ * on the GPU race — issue them on one stream.  When the full launch's split
+ * partials would not fit, the decode runs on fewer CTAs so that they do;
+ * shapes whose partials do not fit even then return KVQ_ERR_WORKSPACE with
+ * the sizes in kvq_last_error(). */
 int32_t kvq_sdpa_decode_noalloc(const kvq_qtensor* keys, const kvq_qtensor* values,
                                 const void* q, int32_t q_heads, float scale,
                                 const int32_t* seq_lens, void* out, void* stream);

@@ -89,8 +89,10 @@ struct Plan {
   int64_t tickets;  // merge tickets it uses (zero before and after the call)
 };
 
+// budget: the workspace bytes available; the balanced decode spreads over
+// fewer CTAs when its partials would not fit (fewer slots), down to one.
 int32_t make_plan(const AttnArgs& a, int L, int mask_mode, int window, bool scores, Params& p,
-                  int& NT, Plan& pl) {
+                  int& NT, Plan& pl, size_t budget = SIZE_MAX) {
   int32_t rc = prepare(a, L, mask_mode, window, p, NT);
   if (rc) return rc;
   int dev = 0;
@@ -109,11 +111,17 @@ int32_t make_plan(const AttnArgs& a, int L, int mask_mode, int window, bool scor
     const int Tu = (a.N + kTile - 1) / kTile;
     int64_t C = (int64_t)num_sms(dev) * occ;
     C = std::min<int64_t>(C, std::max<int64_t>(1, units * Tu / kBalMinTiles));
+    // the merge takes at most kMergeSlots partials of one unit
+    C = std::min<int64_t>(C, kMergeSlots / kWarps - 1);
+    if (budget != SIZE_MAX && budget > kPartialOff) {
+      const int64_t fit = (int64_t)((budget - kPartialOff) / bal_group_bytes(NT, a.D)) - units;
+      if (fit >= 1) C = std::min<int64_t>(C, fit);
+    }
     pl.s = LaunchShape{1, 1, kTile};
     pl.s.ctas = (int)C;
     p.B = a.B;
     p.Tu = Tu;
-    pl.tickets = units;
+    pl.tickets = 0;
   } else {
     pl.s = shape_for(a.B, a.Hkv, p.nrep, L, std::max(a.N, 1), NT, num_sms(dev) * occ);
     if (units * pl.s.QB > kMaxTickets) {  // too many merge groups: no key split
@@ -128,11 +136,12 @@ int32_t make_plan(const AttnArgs& a, int L, int mask_mode, int window, bool scor
 
 int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void* out, float* pm,
             float* pl_, float* po, void* ws, size_t ws_bytes, cudaStream_t st,
-            float* scores = nullptr) {
+            float* scores = nullptr, bool fit_to_ws = false) {
   Params p;
   int NT = 1;
   Plan pl;
-  int32_t rc = make_plan(a, L, mask_mode, window, scores != nullptr, p, NT, pl);
+  int32_t rc = make_plan(a, L, mask_mode, window, scores != nullptr, p, NT, pl,
+                         fit_to_ws ? ws_bytes : SIZE_MAX);
   if (rc) return rc;
   if (a.B == 0 || a.Hq == 0) return KVQ_OK;
   int dev = 0;
@@ -146,9 +155,10 @@ int32_t run(const AttnArgs& a, int L, int mask_mode, int window, int mode, void*
   }
   uint8_t* w = static_cast<uint8_t*>(ws);
   p.err = reinterpret_cast<int*>(w);
-  if (pl.tickets > 0) {
-    const size_t slots = s.ctas > 0 ? ((size_t)s.ctas + (size_t)a.B * a.Hkv) * 8 * NT
-                                    : (size_t)a.B * a.Hkv * s.QB * s.nsplit * 8 * NT;
+  if (s.ctas > 0) {
+    p.ws_o = reinterpret_cast<float*>(w + kPartialOff);
+  } else if (pl.tickets > 0) {
+    const size_t slots = (size_t)a.B * a.Hkv * s.QB * s.nsplit * 8 * NT;
     p.counters = reinterpret_cast<unsigned*>(w + kTicketOff);
     p.ws_ml = reinterpret_cast<float*>(w + kPartialOff);
     p.ws_o = reinterpret_cast<float*>(w + kPartialOff + (slots * 2 * 4 + 255) / 256 * 256);
@@ -188,11 +198,12 @@ size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D) {
   return std::max(ws_bytes_for(B, Hkv, s, NT, D), ws_bytes_for(B, Hkv, sb, NT, D));
 }
 
-int32_t decode_workspace_exact(const AttnArgs& a, size_t* bytes, size_t* zero_prefix) {
+int32_t decode_workspace_exact(const AttnArgs& a, size_t* bytes, size_t* zero_prefix,
+                               size_t budget) {
   Params p;
   int NT = 1;
   Plan pl;
-  int32_t rc = make_plan(a, 1, 0, 0, false, p, NT, pl);
+  int32_t rc = make_plan(a, 1, 0, 0, false, p, NT, pl, budget);
   if (rc) return rc;
   *bytes = pl.ws_bytes;
   *zero_prefix =
@@ -201,8 +212,8 @@ int32_t decode_workspace_exact(const AttnArgs& a, size_t* bytes, size_t* zero_pr
 }
 
 int32_t launch_decode(const AttnArgs& a, void* out, float* pm, float* pl, float* po, void* ws,
-                      size_t ws_bytes, cudaStream_t st) {
-  return run(a, 1, 0, 0, out ? 0 : 1, out, pm, pl, po, ws, ws_bytes, st);
+                      size_t ws_bytes, cudaStream_t st, bool fit_to_ws) {
+  return run(a, 1, 0, 0, out ? 0 : 1, out, pm, pl, po, ws, ws_bytes, st, nullptr, fit_to_ws);
 }
 
 int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void* out, void* ws,

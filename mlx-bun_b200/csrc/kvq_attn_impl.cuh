@@ -65,6 +65,7 @@ constexpr int kTile = 16;                     // rows per MMA tile; row-alignmen
 constexpr long long kWaitLimit = 1ll << 30;   // mbarrier polls before declaring a hang
 constexpr uint64_t kWaitNs = 2000000000ull;   // ... or 2 s of %globaltimer, whichever first
 constexpr int kMergeMax = 64;                 // splits the last CTA merges through shared memory
+constexpr int kRowPad = 4;                    // warp-merge rows are D + kRowPad floats apart (bank spread)
 constexpr int kBalMinTiles = 8;                // balanced decode: key tiles per CTA at least (one chunk)
 
 struct Params {
@@ -314,16 +315,18 @@ struct Smem {
   static constexpr int WL = WM + W * HQ * 4;                   // f32 [W][HQ] warp sums
   static constexpr int RM = WL + W * HQ * 4;                   // f32 [HQ] block maxima
   static constexpr int RL = RM + HQ * 4;                       // f32 [HQ] block sums
-  static constexpr int SW = RL + HQ * 4;                       // f32 [HQ][kMergeMax] split weights
-  static constexpr int STAGES_OFF = (SW + HQ * kMergeMax * 4 + 127) / 128 * 128;
+  static constexpr int SW = RL + HQ * 4;                       // f32 [HQ][kMergeMax] split m / weights
+  static constexpr int SL = SW + HQ * kMergeMax * 4;           // f32 [HQ][kMergeMax] split l
+  static constexpr int RA = SL + HQ * kMergeMax * 4;           // f32 [HQ] merge rescale
+  static constexpr int STAGES_OFF = (RA + HQ * 4 + 127) / 128 * 128;
   static constexpr int STAGE_BYTES = STAGES * STAGE;
-  static constexpr int MERGE_BYTES = W * HQ * D * 4;
+  static constexpr int MERGE_BYTES = W * HQ * (D + kRowPad) * 4;
   static constexpr int TOTAL =
       STAGES_OFF + (STAGE_BYTES > MERGE_BYTES ? STAGE_BYTES : MERGE_BYTES);
 };
 
-// Shared memory of the balanced kernel: the ring keeps streaming while the
-// consumer warps close a segment, so the warp-merge buffer is separate.
+// Shared memory of the balanced kernel: barriers, the per-entry tile table
+// (ragged batches) and the ring.
 constexpr int kBalMaxBatch = 256;  // ragged batches up to this size use the balanced kernel
 template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
 struct BalSmem {
@@ -333,15 +336,9 @@ struct BalSmem {
   static constexpr int STAGE = StageLayout<BITS, D, GS, CH>::STAGE;
   static constexpr int BARS = 0;
   static constexpr int CTRL = BARS + 2 * STAGES * 8;
-  static constexpr int WM = CTRL + 16;
-  static constexpr int WL = WM + W * HQ * 4;
-  static constexpr int RM = WL + W * HQ * 4;
-  static constexpr int RL = RM + HQ * 4;
-  static constexpr int SW = RL + HQ * 4;
-  static constexpr int BS = (SW + HQ * kMergeMax * 4 + 7) / 8 * 8;   // i64 [B+1] first tile of each entry
-  static constexpr int BL = BS + (kBalMaxBatch + 1) * 8;             // int [B] key rows of each entry
-  static constexpr int MRG = (BL + kBalMaxBatch * 4 + 127) / 128 * 128;  // f32 [2][HQ][D]
-  static constexpr int STAGES_OFF = MRG + 2 * HQ * D * 4;
+  static constexpr int BS = CTRL + 16;                          // i64 [B+1] first tile of each entry
+  static constexpr int BL = BS + (kBalMaxBatch + 1) * 8;        // int [B] key rows of each entry
+  static constexpr int STAGES_OFF = (BL + kBalMaxBatch * 4 + 127) / 128 * 128;
   static constexpr int TOTAL = STAGES_OFF + STAGES * STAGE;
 };
 
@@ -760,31 +757,45 @@ __device__ __forceinline__ void rescale_warp(WarpAcc<BITS, D, GS, NT>& A, const 
     }
 }
 
-// Write (or add) a warp's output partial o * fac + sum(p * bias) into wo [HQ][D].
+// Write (or add) a warp's output partial o * fac + sum(p * bias) into wo
+// [HQ][D + kRowPad].  A lane holds GS/8 consecutive d of each (group,
+// column), stored as 16-byte vectors; with the padded row stride a warp's
+// vector store meets at most 2-way bank conflicts.
 template <int BITS, int D, int GS, int NT, bool ADD>
 __device__ __forceinline__ void store_warp(const WarpAcc<BITS, D, GS, NT>& A, float* wo, int g,
                                            int t) {
   using G = Geo<BITS, D, GS>;
+  constexpr int MS = D + kRowPad;
+  constexpr int V = GS / 8;  // consecutive d per lane per (group, column): d = grp*GS + g*V + sl
+  static_assert(V == G::C * G::E && V == 2 * G::MTG && V % 4 == 0, "lane d layout");
 #pragma unroll
-  for (int mtg = 0; mtg < G::MT; mtg++) {
-    const int grp = mtg / G::MTG, mt = mtg % G::MTG;
-    const float fac = (BITS == 4 && (mt & 1)) ? kCodeUnitInv * 0.0625f : kCodeUnitInv;
+  for (int grp = 0; grp < G::NG; grp++)
 #pragma unroll
-    for (int half = 0; half < 2; half++) {
-      const int sl = half * G::MTG + mt;
-      const int cc = sl / G::E, j = sl % G::E;
-      const int d = grp * GS + (g * G::C + cc) * G::E + j;
+    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-      for (int nt = 0; nt < NT; nt++)
+      for (int hh = 0; hh < 2; hh++) {
+        float v[V];
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-          const float v = fmaf(A.o_acc[mtg][nt][half * 2 + hh], fac, A.pb[nt][grp][hh]);
-          float* dst = wo + (nt * 8 + 2 * t + hh) * D + d;
-          if (ADD) *dst += v;
-          else *dst = v;
+        for (int sl = 0; sl < V; sl++) {
+          const int mt = sl % G::MTG, half = sl / G::MTG;
+          const float fac = (BITS == 4 && (mt & 1)) ? kCodeUnitInv * 0.0625f : kCodeUnitInv;
+          v[sl] = fmaf(A.o_acc[grp * G::MTG + mt][nt][half * 2 + hh], fac, A.pb[nt][grp][hh]);
         }
-    }
-  }
+        float* dst = wo + (nt * 8 + 2 * t + hh) * MS + grp * GS + g * V;
+#pragma unroll
+        for (int q4 = 0; q4 < V / 4; q4++) {
+          float4* p4 = reinterpret_cast<float4*>(dst + 4 * q4);
+          float4 x = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+          if (ADD) {
+            const float4 y = *p4;
+            x.x += y.x;
+            x.y += y.y;
+            x.z += y.z;
+            x.w += y.w;
+          }
+          *p4 = x;
+        }
+      }
 }
 
 // One output element of query row `orow`: the normalised result (mode 0) or
@@ -803,22 +814,92 @@ __device__ __forceinline__ void write_row(const Params& p, int64_t orow, int d, 
   }
 }
 
-// acc + sum_j o0[j * stride] * w[j], in j order (deterministic).
-__device__ __forceinline__ float merge_sum(const float* o0, int64_t stride, const float* w, int n,
-                                           float acc) {
-  int j = 0;
-  for (; j + 4 <= n; j += 4) {
-    const float v0 = __ldcg(o0 + (int64_t)(j + 0) * stride);
-    const float v1 = __ldcg(o0 + (int64_t)(j + 1) * stride);
-    const float v2 = __ldcg(o0 + (int64_t)(j + 2) * stride);
-    const float v3 = __ldcg(o0 + (int64_t)(j + 3) * stride);
-    acc = fmaf(v0, w[j], acc);
-    acc = fmaf(v1, w[j + 1], acc);
-    acc = fmaf(v2, w[j + 2], acc);
-    acc = fmaf(v3, w[j + 3], acc);
+// Barrier among the first `nthreads` threads of the CTA (barrier 1; the
+// kernels use barrier 0 only through __syncthreads).
+__device__ __forceinline__ void bar_sync1(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// Merge the partials (m, l, o) that `nseg` key ranges wrote to consecutive
+// slots slot0.. of the workspace (HQ rows each; rows [0, rows) are live) and
+// write each live row through row_of(r): o = sum_j o_j e^(m_j - M) /
+// sum_j l_j e^(m_j - M), M = max_j m_j, summed in j order (deterministic).
+// Run by threads [0, NTH) together.  Every (m, l) is fetched in one round of
+// loads into shared memory, and the o sums issue their loads in batches, so
+// the merge pays a few L2 round trips rather than one per range.
+template <int D, int HQ, int NTH, bool BF, class RowOf>
+__device__ __forceinline__ void merge_slots(const Params& p, int64_t slot0, int nseg, int rows,
+                                            float* sm, float* sl, float* rm, float* rl,
+                                            float* ra, float* carry, int tid, RowOf row_of) {
+  constexpr int KB = 4;  // output elements whose loads are batched together
+  const int live = rows * D;
+  for (int j0 = 0; j0 < nseg; j0 += kMergeMax) {
+    const int nj = min(kMergeMax, nseg - j0);
+    const bool last = j0 + nj >= nseg;
+    if (j0) bar_sync1(NTH);  // the previous pass is done with sm / ra / carry
+    for (int e = tid; e < nj * rows; e += NTH) {
+      const int j = e / rows, r = e - j * rows;
+      const float* ml = p.ws_ml + ((slot0 + j0 + j) * HQ + r) * 2;
+      sm[r * kMergeMax + j] = __ldcg(ml);
+      sl[r * kMergeMax + j] = __ldcg(ml + 1);
+    }
+    bar_sync1(NTH);
+    if (tid < rows) {
+      const int r = tid;
+      const float Mo = j0 ? rm[r] : kNeg;
+      float M = Mo;
+      for (int j = 0; j < nj; j++) M = fmaxf(M, sm[r * kMergeMax + j]);
+      const float a = ex2((Mo - M) * kLog2e);
+      float L = j0 ? rl[r] * a : 0.0f;
+      for (int j = 0; j < nj; j++) {
+        const float w = ex2((sm[r * kMergeMax + j] - M) * kLog2e);
+        sm[r * kMergeMax + j] = w;
+        L = fmaf(sl[r * kMergeMax + j], w, L);
+      }
+      rm[r] = M;
+      rl[r] = L;
+      ra[r] = a;
+    }
+    bar_sync1(NTH);
+    // output elements e = tid + k*NTH, KB of them at a time (a sum carried
+    // between passes waits in `carry`)
+#pragma unroll 1
+    for (int e0 = tid; e0 < live; e0 += KB * NTH) {
+      float acc[KB];
+      int rr[KB];
+      const float* src[KB];
+      bool ok[KB];
+#pragma unroll
+      for (int kb = 0; kb < KB; kb++) {
+        const int e = e0 + kb * NTH;
+        ok[kb] = e < live;
+        const int r = ok[kb] ? e / D : 0, d = ok[kb] ? e - r * D : 0;
+        rr[kb] = r;
+        src[kb] = p.ws_o + ((slot0 + j0) * HQ + r) * D + d;
+        acc[kb] = (ok[kb] && j0) ? carry[e] * ra[r] : 0.0f;
+      }
+      for (int j = 0; j < nj; j += 4) {
+        float v[KB][4];
+#pragma unroll
+        for (int kb = 0; kb < KB; kb++)
+#pragma unroll
+          for (int jj = 0; jj < 4; jj++)
+            v[kb][jj] = (ok[kb] && j + jj < nj) ? __ldcg(src[kb] + (int64_t)(j + jj) * HQ * D) : 0.0f;
+#pragma unroll
+        for (int kb = 0; kb < KB; kb++)
+#pragma unroll
+          for (int jj = 0; jj < 4; jj++)
+            if (j + jj < nj) acc[kb] = fmaf(v[kb][jj], sm[rr[kb] * kMergeMax + j + jj], acc[kb]);
+      }
+#pragma unroll
+      for (int kb = 0; kb < KB; kb++) {
+        const int e = e0 + kb * NTH;
+        if (!ok[kb]) continue;
+        if (last) write_row<D, BF>(p, row_of(rr[kb]), e - rr[kb] * D, acc[kb], rm[rr[kb]], rl[rr[kb]]);
+        else carry[e] = acc[kb];
+      }
+    }
   }
-  for (; j < n; j++) acc = fmaf(__ldcg(o0 + (int64_t)j * stride), w[j], acc);
-  return acc;
 }
 
 // Issue the six bulk copies of `rows` (a multiple of 16) key rows starting
@@ -840,9 +921,7 @@ __device__ __forceinline__ void issue_chunk(const Params& p, uint8_t* st, uint64
 }
 
 // Barrier among the consumer warps only (the producer warp streams on).
-__device__ __forceinline__ void consumer_sync(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-}
+__device__ __forceinline__ void consumer_sync(int nthreads) { bar_sync1(nthreads); }
 
 // ------------------------------------------------------------ split kernel --
 
@@ -862,6 +941,8 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_kernel(con
   float* rm = reinterpret_cast<float*>(smem + S::RM);
   float* rl = reinterpret_cast<float*>(smem + S::RL);
   float* sw = reinterpret_cast<float*>(smem + S::SW);
+  float* sl = reinterpret_cast<float*>(smem + S::SL);
+  float* ra = reinterpret_cast<float*>(smem + S::RA);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
   const bool producer = warp == W;
@@ -972,7 +1053,7 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_kernel(con
   __syncthreads();  // every stage consumed (ring reusable) and warp maxima visible
   if (!producer) {
     rescale_warp<BITS, D, GS, NT, W>(A, wm, wl, rm, warp, g, t);
-    store_warp<BITS, D, GS, NT, false>(A, mrg + warp * HQ * D, g, t);
+    store_warp<BITS, D, GS, NT, false>(A, mrg + warp * HQ * (D + kRowPad), g, t);
   }
   __syncthreads();
   if (tid < HQ) {
@@ -991,7 +1072,7 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_kernel(con
     const int r = i / D, d = i - r * D;
     float O = 0.0f;
 #pragma unroll
-    for (int w = 0; w < W; w++) O += mrg[(w * HQ + r) * D + d];
+    for (int w = 0; w < W; w++) O += mrg[(w * HQ + r) * (D + kRowPad) + d];
     const float Lsum = rl[r], M = rm[r];
     const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
     const int64_t orow = ((int64_t)b * p.Hq + hq) * L + l;
@@ -1018,67 +1099,97 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_kernel(con
   __syncthreads();
   if (!ctrl[0]) return;
   __threadfence();
-  // Per-row split weights exp(M_s - M) in shared memory (nact <= kMergeMax
-  // is guaranteed by the launch shape), then independent loads of the O rows.
-  if (tid < rows_here) {
-    const int r = tid;
-    float M = kNeg;
-    for (int sp = 0; sp < nact; sp++)
-      M = fmaxf(M, __ldcg(&p.ws_ml[((cta * p.nsplit + sp) * HQ + r) * 2]));
-    float Ls = 0.0f;
-    for (int sp = 0; sp < nact; sp++) {
-      const int64_t slot = (cta * p.nsplit + sp) * HQ + r;
-      const float e = ex2((__ldcg(&p.ws_ml[slot * 2]) - M) * kLog2e);
-      sw[r * kMergeMax + sp] = e;
-      Ls += __ldcg(&p.ws_ml[slot * 2 + 1]) * e;
-    }
-    rl[r] = Ls;
-    rm[r] = M;
-  }
-  __syncthreads();
-  for (int i = tid; i < rows_here * D; i += (W + 1) * 32) {
-    const int r = i / D, d = i - r * D;
-    const float O = merge_sum(p.ws_o + ((cta * p.nsplit) * HQ + r) * D + d, (int64_t)HQ * D,
-                              sw + r * kMergeMax, nact, 0.0f);
-    const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
-    write_row<D, BF>(p, ((int64_t)b * p.Hq + hq) * L + l, d, O, rm[r], rl[r]);
-  }
+  merge_slots<D, HQ, (W + 1) * 32, BF>(
+      p, cta * p.nsplit, nact, rows_here, sw, sl, rm, rl, ra, mrg, tid, [&](int r) -> int64_t {
+        const int qr = qr0 + r, l = qr / nrep, hq = kvh * nrep + (qr - l * nrep);
+        return ((int64_t)b * p.Hq + hq) * L + l;
+      });
   if (tid == 0) p.counters[cta] = 0u;  // leave the ticket ready for the next call
 }
 
 // --------------------------------------------------------- balanced kernel --
 //
-// Decode (L = 1, no window) over one resident wave of C CTAs.  The
-// key tiles (16 rows) of all units u = b*Hkv + kvh are laid end to end,
-// unit u owning tiles [U_u, U_u + T_u); CTA i streams tiles
-// [i*RT/C, (i+1)*RT/C) of the RT in total, so every CTA moves the same bytes
-// whatever the lengths in the batch.  Where its range crosses a unit
-// boundary it closes one segment (the part of a unit it holds) and opens
-// the next; the producer warp streams on across segments while the consumer
-// warps close the previous one.  A unit held by one CTA is written directly;
-// otherwise each holder writes its partial (m, l, o) to slot i + u —
-// consecutive slots for the consecutive holders of u — and the last holder
-// to finish (atomic ticket per unit) merges them in holder order.
+// Decode (L = 1, no window) over one resident wave of CTAs, in two launches:
+//
+// attn_bal_kernel: the key tiles (16 rows) of all units u = b*Hkv + kvh are
+// laid end to end, unit u owning tiles [U_u, U_u + T_u); working CTA i of C
+// streams tiles [i*RT/C, (i+1)*RT/C) of the RT in total, so every CTA moves
+// the same bytes whatever the lengths in the batch.  Where its range crosses
+// a unit boundary it closes one segment (the part of a unit it holds) and
+// opens the next.  A segment closes warp by warp, with no block barrier:
+// each consumer warp writes its own partial (m, l, o) of the segment's
+// query rows to partial slot (i + u)*W + warp and goes on streaming, so the
+// ring never stalls at a boundary.  The holders of u are consecutive CTAs,
+// so its partials fill consecutive slots.
+//
+// attn_bal_merge_kernel: one CTA per (unit, query row) combines the unit's
+// partials (log-sum-exp, in slot order: deterministic) into the output.  It
+// is launched as a programmatic dependent of the attention kernel and waits
+// on its completion before reading.
+
+// One consumer warp's partial of the live query rows (qrows): m, l per row
+// and o = o_acc * fac + sum(p * bias) per (row, d), into dst = [HQ] m,
+// [HQ] l, [HQ][D] o.
+template <int BITS, int D, int GS, int NT>
+__device__ __forceinline__ void write_warp_partial(const WarpAcc<BITS, D, GS, NT>& A, float* dst,
+                                                   int qrows, int g, int t) {
+  using G = Geo<BITS, D, GS>;
+  constexpr int HQ = 8 * NT;
+  constexpr int V = GS / 8;  // consecutive d per lane per (group, row): d = grp*GS + g*V + sl
+  static_assert(V == G::C * G::E && V == 2 * G::MTG && V % 4 == 0, "lane d layout");
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      const int col = nt * 8 + 2 * t + hh;
+      if (col >= qrows) continue;
+      if (g == 0) {
+        dst[col] = A.m_run[nt][hh];
+        dst[HQ + col] = A.l_run[nt][hh];
+      }
+#pragma unroll
+      for (int grp = 0; grp < G::NG; grp++) {
+        float v[V];
+#pragma unroll
+        for (int sl = 0; sl < V; sl++) {
+          const int mt = sl % G::MTG, half = sl / G::MTG;
+          const float fac = (BITS == 4 && (mt & 1)) ? kCodeUnitInv * 0.0625f : kCodeUnitInv;
+          v[sl] = fmaf(A.o_acc[grp * G::MTG + mt][nt][half * 2 + hh], fac, A.pb[nt][grp][hh]);
+        }
+        float* o = dst + 2 * HQ + col * D + grp * GS + g * V;
+#pragma unroll
+        for (int q4 = 0; q4 < V / 4; q4++)
+          *reinterpret_cast<float4*>(o + 4 * q4) =
+              make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+      }
+    }
+}
+
+// Working CTAs of the balanced decode: at most one per kBalMinTiles key
+// tiles and at most the launched grid, so every working CTA's range is
+// non-empty and the holders of a unit are consecutive CTAs.
+__device__ __forceinline__ int bal_working_ctas(int64_t RT, int grid) {
+  int64_t c = RT / kBalMinTiles;
+  if (c > grid) c = grid;
+  if (c < 1) c = 1;
+  return (int)c;
+}
+
 template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES, bool BF>
 __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) {
   using S = BalSmem<BITS, D, GS, NT, W, RW, STAGES>;
   constexpr int HQ = S::HQ;
   constexpr int CH = S::CH;
-  constexpr int NC = W * 32;  // consumer threads
-  static_assert(W % 2 == 0, "warps pair up in the combine");
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BARS);
   uint64_t* empty = full + STAGES;
-  volatile int* ctrl = reinterpret_cast<volatile int*>(smem + S::CTRL);  // [0] merge, [1] abort
+  volatile int* ctrl = reinterpret_cast<volatile int*>(smem + S::CTRL);  // [1] abort
   uint8_t* stages = smem + S::STAGES_OFF;
-  float* buf = reinterpret_cast<float*>(smem + S::MRG);  // [2][HQ][D]
-  float* wm = reinterpret_cast<float*>(smem + S::WM);
-  float* wl = reinterpret_cast<float*>(smem + S::WL);
-  float* rm = reinterpret_cast<float*>(smem + S::RM);
-  float* rl = reinterpret_cast<float*>(smem + S::RL);
-  float* sw = reinterpret_cast<float*>(smem + S::SW);
   int* blen = reinterpret_cast<int*>(smem + S::BL);             // [B] key rows of each entry
   int64_t* bfirst = reinterpret_cast<int64_t*>(smem + S::BS);   // [B+1] first tile of each entry
+
+  // The merge kernel may be scheduled now; it waits for this grid to finish.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
   const bool producer = warp == W;
@@ -1119,13 +1230,7 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
   } else {
     __syncthreads();
   }
-  // Working CTAs: at most one per kBalMinTiles tiles (the host sized the grid
-  // that way from N; with per-entry lengths RT is only known here), so every
-  // working CTA's range is non-empty and holders of a unit are consecutive.
-  int64_t c_work = RT / kBalMinTiles;
-  if (c_work > (int64_t)gridDim.x) c_work = gridDim.x;
-  if (c_work < 1) c_work = 1;
-  const int C = (int)c_work;
+  const int C = bal_working_ctas(RT, gridDim.x);
   const int64_t x0 = i < C ? (int64_t)i * RT / C : RT;
   const int64_t x1 = i < C ? (int64_t)(i + 1) * RT / C : RT;
 
@@ -1152,16 +1257,6 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
       U = bfirst[b] + (int64_t)kvh * T;
     }
   };
-  // Holder of tile x: the last CTA whose range starts at or before x.
-  auto cta_of = [&](int64_t x) -> int { return (int)(((x + 1) * C - 1) / RT); };
-
-  // Batch entries with no keys: their rows are written here (zeros, or an
-  // empty partial), spread over the CTAs.
-  if (ragged)
-    for (int bb = i; bb < B; bb += gridDim.x)
-      if (blen[bb] == 0)
-        for (int e = tid; e < p.Hq * D; e += blockDim.x)
-          write_row<D, BF>(p, (int64_t)bb * p.Hq + e / D, e % D, 0.0f, kNeg, 0.0f);
 
   bool hung = false;
   if (producer) {
@@ -1206,8 +1301,7 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
       for (int row = r0; row < r1; row += CH, c++) {
         const int s = c % STAGES;
         // Warp-uniform decision: the slice is full of warp-collective ops.
-        // After a timeout anywhere, skip the waits but keep the structure, so
-        // every consumer still meets every named barrier below.
+        // After a timeout anywhere, skip the waits but keep the structure.
         const bool ok = !hung && !ctrl[1] && mbar_wait(&full[s], (uint32_t)((c / STAGES) & 1));
         if (!__all_sync(0xffffffffu, ok)) {
           if (!hung && lane == 0) ctrl[1] = 1;
@@ -1222,94 +1316,118 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
-
-      // ---- close the segment: combine the warps in a fixed order ----
+      // ---- close the segment: this warp's partial, no block barrier ----
       warp_reduce<BITS, D, GS, NT>(A);
-      if (g == 0) {
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-          for (int hh = 0; hh < 2; hh++) wm[warp * HQ + nt * 8 + 2 * t + hh] = A.m_run[nt][hh];
-      }
-      consumer_sync(NC);
-      rescale_warp<BITS, D, GS, NT, W>(A, wm, wl, rm, warp, g, t);
-      if (warp >= W / 2) store_warp<BITS, D, GS, NT, false>(A, buf + (warp - W / 2) * HQ * D, g, t);
-      consumer_sync(NC);
-      if (warp < W / 2) store_warp<BITS, D, GS, NT, true>(A, buf + warp * HQ * D, g, t);
-      if (tid < HQ) {
-        float Ls = 0.0f;
-#pragma unroll
-        for (int w = 0; w < W; w++) Ls += wl[w * HQ + tid];
-        rl[tid] = Ls;
-      }
-      consumer_sync(NC);
-
-      const int u = b * Hkv + kvh;
-      const int i_first = cta_of(U), nseg = cta_of(U + T - 1) - i_first + 1;
-      const int64_t slot0 = (int64_t)i_first + u;  // partial slots of this unit's holders
-      const int64_t slot = (int64_t)i + u;
-      for (int e = tid; e < qrows * D; e += NC) {
-        const int r = e / D, d = e - r * D;
-        float O = buf[e];
-#pragma unroll
-        for (int w = 1; w < W / 2; w++) O += buf[w * HQ * D + e];
-        const float M = rm[r], Lsum = rl[r];
-        if (nseg == 1) {
-          write_row<D, BF>(p, (int64_t)b * p.Hq + kvh * nrep + r, d, O, M, Lsum);
-        } else {
-          p.ws_o[(slot * HQ + r) * D + d] = O;
-          if (d == 0) {
-            p.ws_ml[(slot * HQ + r) * 2] = M;
-            p.ws_ml[(slot * HQ + r) * 2 + 1] = Lsum;
-          }
-        }
-      }
-      if (nseg > 1) {
-        __threadfence();
-        consumer_sync(NC);
-        if (tid == 0) {
-          const unsigned prev = atomicAdd(&p.counters[u], 1u);
-          ctrl[0] = (prev == (unsigned)(nseg - 1)) ? 1 : 0;
-        }
-        consumer_sync(NC);
-        if (ctrl[0]) {
-          __threadfence();
-          if (tid < qrows) {
-            float M = kNeg;
-            for (int j = 0; j < nseg; j++)
-              M = fmaxf(M, __ldcg(&p.ws_ml[((slot0 + j) * HQ + tid) * 2]));
-            float Ls = 0.0f;
-            for (int j = 0; j < nseg; j++) {
-              const int64_t sj = (slot0 + j) * HQ + tid;
-              Ls += __ldcg(&p.ws_ml[sj * 2 + 1]) * ex2((__ldcg(&p.ws_ml[sj * 2]) - M) * kLog2e);
-            }
-            rm[tid] = M;
-            rl[tid] = Ls;
-          }
-          // holders in order, kMergeMax at a time; the running sum waits in buf
-          for (int j0 = 0; j0 < nseg; j0 += kMergeMax) {
-            const int nj = min(kMergeMax, nseg - j0);
-            consumer_sync(NC);
-            if (tid < qrows)
-              for (int j = 0; j < nj; j++)
-                sw[tid * kMergeMax + j] =
-                    ex2((__ldcg(&p.ws_ml[((slot0 + j0 + j) * HQ + tid) * 2]) - rm[tid]) * kLog2e);
-            consumer_sync(NC);
-            for (int e = tid; e < qrows * D; e += NC) {
-              const int r = e / D, d = e - r * D;
-              const float O = merge_sum(p.ws_o + ((slot0 + j0) * HQ + r) * D + d, (int64_t)HQ * D,
-                                        sw + r * kMergeMax, nj, j0 ? buf[e] : 0.0f);
-              if (j0 + nj < nseg) buf[e] = O;
-              else write_row<D, BF>(p, (int64_t)b * p.Hq + kvh * nrep + r, d, O, rm[r], rl[r]);
-            }
-          }
-          if (tid == 0) p.counters[u] = 0u;  // leave the ticket ready for the next call
-        }
-      }
+      const int64_t slot = ((int64_t)i + b * Hkv + kvh) * W + warp;
+      write_warp_partial<BITS, D, GS, NT>(A, p.ws_o + slot * HQ * (D + 2), qrows, g, t);
       x = xe;
     }
   }
   if (hung && lane == 0) atomicExch(p.err, 1);
+}
+
+// Combine the partial slots of unit blockIdx.x for query row blockIdx.y;
+// blockDim.x == D.  Round 1: the (m, l) of every slot (kMergeSlots at most)
+// -> M = max m, weights w = e^(m - M) in shared memory, L = sum l w.
+// Round 2: thread d sums w * o[d] over the slots in slot order (loads issued
+// eight at a time, coalesced across d).
+constexpr int kMergeSlots = 4096;
+template <int D, int W, int NT, bool BF>
+__global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int grid) {
+  constexpr int HQ = 8 * NT;
+  constexpr int NWARP = D / 32;
+  constexpr int SLOT = HQ * (D + 2);  // floats per partial slot
+  __shared__ float wsm[kMergeSlots];
+  __shared__ float red_m[NWARP], red_l[NWARP];
+  __shared__ int64_t red_t[2];
+  const int u = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int Hkv = p.Hkv, b = u / Hkv, kvh = u - b * Hkv;
+  const int64_t orow = (int64_t)b * p.Hq + kvh * p.nrep + r;
+
+  // The unit's tiles and the partition of the attention launch.
+  int64_t U, RT;
+  int T;
+  if (p.seq_lens == nullptr) {
+    T = p.Tu;
+    U = (int64_t)u * p.Tu;
+    RT = (int64_t)p.B * Hkv * p.Tu;
+  } else {  // tiles of the entries before b and of all entries
+    int64_t before = 0, all = 0;
+    for (int bb = tid; bb < p.B; bb += D) {
+      const int n = min(max(p.seq_lens[bb], 0), p.N);
+      const int64_t tb = (int64_t)Hkv * ((n + kTile - 1) / kTile);
+      all += tb;
+      if (bb < b) before += tb;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      before += __shfl_xor_sync(0xffffffffu, before, o);
+      all += __shfl_xor_sync(0xffffffffu, all, o);
+    }
+    if (tid == 0) red_t[0] = red_t[1] = 0;
+    __syncthreads();
+    if (lane == 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&red_t[0]), (unsigned long long)before);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&red_t[1]), (unsigned long long)all);
+    }
+    __syncthreads();
+    const int n = min(max(p.seq_lens[b], 0), p.N);
+    T = (n + kTile - 1) / kTile;
+    U = red_t[0] + (int64_t)kvh * T;
+    RT = red_t[1];
+  }
+
+  // Everything below reads what the attention grid wrote.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  if (T == 0) {  // an entry with no keys: a zero row (or an empty partial)
+    write_row<D, BF>(p, orow, tid, 0.0f, kNeg, 0.0f);
+    return;
+  }
+  const int C = bal_working_ctas(RT, grid);
+  const int i_first = (int)(((U + 1) * C - 1) / RT);
+  const int i_last = (int)(((U + T) * C - 1) / RT);
+  const int nslots = (i_last - i_first + 1) * W;  // <= kMergeSlots (host launch shape)
+  const float* base = p.ws_o + ((int64_t)i_first + u) * W * SLOT;
+
+  // round 1
+  float mloc = kNeg;
+  for (int j = tid; j < nslots; j += D) mloc = fmaxf(mloc, __ldcg(base + (int64_t)j * SLOT + r));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+  if (lane == 0) red_m[warp] = mloc;
+  __syncthreads();
+  float M = red_m[0];
+#pragma unroll
+  for (int w = 1; w < NWARP; w++) M = fmaxf(M, red_m[w]);
+  float lloc = 0.0f;
+  for (int j = tid; j < nslots; j += D) {
+    const float* sp = base + (int64_t)j * SLOT;
+    const float w = ex2((__ldcg(sp + r) - M) * kLog2e);
+    wsm[j] = w;
+    lloc = fmaf(__ldcg(sp + HQ + r), w, lloc);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, o);
+  if (lane == 0) red_l[warp] = lloc;
+  __syncthreads();
+  float L = 0.0f;
+#pragma unroll
+  for (int w = 0; w < NWARP; w++) L += red_l[w];
+
+  // round 2
+  const float* op = base + 2 * HQ + r * D + tid;
+  float acc = 0.0f;
+  int j = 0;
+  for (; j + 8 <= nslots; j += 8) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = __ldcg(op + (int64_t)(j + k) * SLOT);
+#pragma unroll
+    for (int k = 0; k < 8; k++) acc = fmaf(v[k], wsm[j + k], acc);
+  }
+  for (; j < nslots; j++) acc = fmaf(__ldcg(op + (int64_t)j * SLOT), wsm[j], acc);
+  write_row<D, BF>(p, orow, tid, acc, M, L);
 }
 
 // ------------------------------------------------------------ host side --
@@ -1375,11 +1493,14 @@ constexpr int64_t kMaxTickets = 65536;
 constexpr size_t kTicketOff = 256;
 constexpr size_t kPartialOff = kTicketOff + 4 * kMaxTickets;
 
+// Balanced decode partials: (ctas + units) groups of kWarps slots of
+// [HQ] m, [HQ] l, [HQ][D] o floats.
+inline size_t bal_group_bytes(int NT, int D) { return (size_t)kWarps * 8 * NT * (D + 2) * 4; }
+inline size_t bal_slot_groups(int ctas, int B, int Hkv) { return (size_t)ctas + (size_t)B * Hkv; }
+
 inline size_t ws_bytes_for(int B, int Hkv, const LaunchShape& s, int NT, int D) {
-  if (s.ctas > 0) {  // balanced: partial slots i + u, i < ctas, u < B * Hkv
-    const size_t slots = ((size_t)s.ctas + (size_t)B * Hkv) * 8 * NT;
-    return kPartialOff + (slots * 2 * 4 + 255) / 256 * 256 + slots * D * 4;
-  }
+  if (s.ctas > 0)  // balanced: one (m, l, o) partial per warp, slots (i + u) * W + warp
+    return kPartialOff + bal_slot_groups(s.ctas, B, Hkv) * bal_group_bytes(NT, D);
   if (s.nsplit <= 1) return kPartialOff;
   const size_t slots = (size_t)B * Hkv * s.QB * s.nsplit * 8 * NT;
   return kPartialOff + (slots * 2 * 4 + 255) / 256 * 256 + slots * D * 4;
@@ -1420,6 +1541,23 @@ int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* o
   const dim3 grid = bal ? dim3(s.ctas) : dim3(s.nsplit, p.Hkv * s.QB, B);
   kern<<<grid, (kWarps + 1) * 32, smem, st>>>(p);
   KVQ_CUDA_TRY(cudaGetLastError());
+  if (bal) {
+    // merge of the per-warp partials, a programmatic dependent of the
+    // attention grid (it waits for that grid inside, with griddepcontrol)
+    void (*merge)(Params, int) = p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true>
+                                        : attn_bal_merge_kernel<D, kWarps, NT, false>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(B * p.Hkv), (unsigned)p.nrep);
+    cfg.blockDim = dim3(D);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    KVQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, merge, p, s.ctas));
+  }
   return KVQ_OK;
 }
 

@@ -60,14 +60,18 @@ struct AttnArgs {
 size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D);
 // Exact workspace bytes one decode launch with these arguments uses, and the
 // bytes at the start of the workspace that must be zero before it runs
-// (error flag and split tickets).
-int32_t decode_workspace_exact(const AttnArgs& a, size_t* bytes, size_t* zero_prefix);
+// (error flag and split tickets).  With a budget, the launch is planned to
+// fit in that many bytes where it can (see launch_decode's fit_to_ws).
+int32_t decode_workspace_exact(const AttnArgs& a, size_t* bytes, size_t* zero_prefix,
+                               size_t budget = SIZE_MAX);
 // Fill AttnArgs from two views and a query (checks shapes; no CUDA calls).
 int32_t make_attn_args(const kvq_qtensor* k, const kvq_qtensor* v, const void* q, int32_t q_heads,
                        float scale, const int32_t* seq_lens, AttnArgs& a);
 // mode 0: normalized output in `out` (dtype); mode 1: partials (m, l, o).
+// fit_to_ws: plan the launch to fit in ws_bytes (fewer CTAs) instead of
+// refusing a workspace smaller than the full launch needs.
 int32_t launch_decode(const AttnArgs& a, void* out, float* pm, float* pl, float* po, void* ws,
-                      size_t ws_bytes, cudaStream_t st);
+                      size_t ws_bytes, cudaStream_t st, bool fit_to_ws = false);
 int32_t launch_merge(const float* m, const float* l, const float* o, int parts, int64_t pstride,
                      int rows, int D, int dtype, void* out, cudaStream_t st);
 int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void* out, void* ws,

@@ -3,9 +3,12 @@
 // Some callers must not allocate: code that runs while a CUDA stream
 // capture is open (cudaMalloc is illegal then), and serving processes that
 // hand all device memory to their own pool at start-up.  For them
-// kvq_sdpa_decode_noalloc runs the same decode kernel as kvq_sdpa_decode but
-// keeps the kernel's scratch (device error flag, split tickets, split
-// partials) in the file-scope array below instead of a cudaMalloc'd buffer.
+// kvq_sdpa_decode_noalloc runs the same decode kernels as kvq_sdpa_decode
+// but keeps their scratch (device error flag, split tickets, split partials)
+// in the file-scope array below instead of a cudaMalloc'd buffer.  When the
+// partials of the full launch would not fit, the decode is spread over fewer
+// CTAs (fewer partials) so that they do; shapes whose partials do not fit
+// even with a single CTA are refused.
 //
 // The array is KVQ_NOALLOC_SCRATCH_BYTES long; every GPU that loads the
 // library holds it until the process exits.  Host code cannot use the
@@ -54,7 +57,8 @@ extern "C" int32_t kvq_sdpa_decode_noalloc(const kvq_qtensor* keys, const kvq_qt
   if (rc) return rc;
   if (!out) return fail(KVQ_ERR_ARG, "out is NULL");
   size_t need = 0, zero_prefix = 0;
-  if ((rc = decode_workspace_exact(a, &need, &zero_prefix))) return rc;
+  if ((rc = decode_workspace_exact(a, &need, &zero_prefix, (size_t)KVQ_NOALLOC_SCRATCH_BYTES)))
+    return rc;
   if (need > (size_t)KVQ_NOALLOC_SCRATCH_BYTES)
     return fail(KVQ_ERR_WORKSPACE,
                 "kvq_sdpa_decode_noalloc: these shapes need " + std::to_string(need) +
@@ -68,5 +72,5 @@ extern "C" int32_t kvq_sdpa_decode_noalloc(const kvq_qtensor* keys, const kvq_qt
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   KVQ_CUDA_TRY(cudaMemsetAsync(ws, 0, zero_prefix, st));
   return launch_decode(a, out, nullptr, nullptr, nullptr, ws, (size_t)KVQ_NOALLOC_SCRATCH_BYTES,
-                       st);
+                       st, /*fit_to_ws=*/true);
 }

@@ -63,9 +63,9 @@ def test_noalloc_decode_matches_decode_two_calls():
 def test_noalloc_refuses_shapes_beyond_its_scratch():
     import torch
     from kvq import _lib
-    # 16 query heads per kv head at D 256 split over many CTAs: the split
-    # partials need more than the fixed scratch
-    q, K, V = _inputs(13, 2, 32, 2, 12000, 256, 64, 8)
+    # 64 (batch, kv head) pairs with 16 query heads each at D 256: the split
+    # partials exceed the fixed scratch even when the decode runs on one CTA
+    q, K, V = _inputs(13, 8, 128, 8, 512, 256, 64, 8)
     out = torch.zeros_like(q)
     rc = _noalloc(q, K, V, 0.0625, out)
     assert rc == _lib.ERR_WORKSPACE
