@@ -99,8 +99,10 @@ int32_t make_plan(const AttnArgs& a, int L, int mask_mode, int window, bool scor
   KVQ_CUDA_TRY(cudaGetDevice(&dev));
   const int64_t units = (int64_t)a.B * a.Hkv;
   // Decode over every key of each row: the balanced single-wave kernel.
+  // (its TMA copies of the query rows need a 16-byte aligned q)
   const bool bal = L == 1 && !scores && (mask_mode == 0 || window <= 0) && a.N > 0 &&
-                   units > 0 && units <= kMaxTickets && (!a.seq_lens || a.B <= kBalMaxBatch);
+                   units > 0 && units <= kMaxTickets && (!a.seq_lens || a.B <= kBalMaxBatch) &&
+                   reinterpret_cast<uintptr_t>(a.q) % 16 == 0;
   LaunchShape probe{1, 1, 1};
   probe.ctas = bal ? 1 : 0;
   int occ = 1;

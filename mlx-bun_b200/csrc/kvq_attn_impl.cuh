@@ -338,7 +338,9 @@ struct BalSmem {
   static constexpr int CTRL = BARS + 2 * STAGES * 8;
   static constexpr int BS = CTRL + 16;                          // i64 [B+1] first tile of each entry
   static constexpr int BL = BS + (kBalMaxBatch + 1) * 8;        // int [B] key rows of each entry
-  static constexpr int STAGES_OFF = (BL + kBalMaxBatch * 4 + 127) / 128 * 128;
+  static constexpr int QSLOT = HQ * D * 2;                      // one group's query rows (dtype)
+  static constexpr int QS = (BL + kBalMaxBatch * 4 + 127) / 128 * 128;  // [STAGES] query slots
+  static constexpr int STAGES_OFF = QS + STAGES * QSLOT;
   static constexpr int TOTAL = STAGES_OFF + STAGES * STAGE;
 };
 
@@ -380,9 +382,12 @@ struct QFrag {
 // query row qr0 + nt*8 + g at the d positions its K fragments pair with,
 // read straight from global memory; sum(q) per group comes from the 4 lanes
 // t of the row, then moves to the lanes that own each column of the score tile.
+// qs: the group's query rows already in shared memory ([nrep][D], L = 1),
+// or nullptr to read them from global memory.
 template <int BITS, int D, int GS, int NT, bool BF>
 __device__ __forceinline__ void load_qfrag(QFrag<BITS, D, GS, NT>& f, const Params& p, int b,
-                                           int kvh, int qr0, int qrows, int g, int t) {
+                                           int kvh, int qr0, int qrows, int g, int t,
+                                           const uint16_t* qs = nullptr) {
   using G = Geo<BITS, D, GS>;
   const int nrep = p.nrep, L = p.L;
   const float scale_dt = round_dt<BF>(p.scale);
@@ -391,7 +396,8 @@ __device__ __forceinline__ void load_qfrag(QFrag<BITS, D, GS, NT>& f, const Para
     const int qr = qr0 + nt * 8 + g;
     const bool qvalid = qr < qrows;
     const int l = qvalid ? qr / nrep : 0, hh = qvalid ? qr - l * nrep : 0;
-    const uint16_t* qrow = p.q + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * D;
+    const uint16_t* qrow =
+        qs ? qs + hh * D : p.q + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * D;
     float gsum[G::NG];
 #pragma unroll
     for (int grp = 0; grp < G::NG; grp++) gsum[grp] = 0.0f;
@@ -415,8 +421,10 @@ __device__ __forceinline__ void load_qfrag(QFrag<BITS, D, GS, NT>& f, const Para
           d_lo = base + 2 * x;
           d_hi = base + 2 * x + 1;
         }
-        const float a0 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d_lo)) * scale_dt) : 0.0f;
-        const float a1 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d_hi)) * scale_dt) : 0.0f;
+        const uint16_t h0 = qvalid ? (qs ? qrow[d_lo] : __ldg(qrow + d_lo)) : 0;
+        const uint16_t h1 = qvalid ? (qs ? qrow[d_hi] : __ldg(qrow + d_hi)) : 0;
+        const float a0 = qvalid ? round_dt<BF>(dt_to_f<BF>(h0) * scale_dt) : 0.0f;
+        const float a1 = qvalid ? round_dt<BF>(dt_to_f<BF>(h1) * scale_dt) : 0.0f;
         gsum[grp] += a0 + a1;
         f.qbf[kk][nt][w2] = pack_h2(a0 * fac, a1 * fac);
       }
@@ -904,14 +912,18 @@ __device__ __forceinline__ void merge_slots(const Params& p, int64_t slot0, int 
 
 // Issue the six bulk copies of `rows` (a multiple of 16) key rows starting
 // at row `row` of the (b, h) pair whose first rows are kbase / vbase.
+// With q_dst, also copy q_bytes of query rows from q_src (a segment's
+// first chunk carries its query group).
 template <int BITS, int D, int GS, int CH>
 __device__ __forceinline__ void issue_chunk(const Params& p, uint8_t* st, uint64_t* bar,
                                             int64_t kbase, int64_t vbase, int64_t row,
-                                            uint32_t rows) {
+                                            uint32_t rows, void* q_dst = nullptr,
+                                            const void* q_src = nullptr, uint32_t q_bytes = 0) {
   using G = Geo<BITS, D, GS>;
   using Lay = StageLayout<BITS, D, GS, CH>;
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  mbar_expect_tx(bar, rows * G::ROWB);
+  mbar_expect_tx(bar, rows * G::ROWB + (q_dst ? q_bytes : 0u));
+  if (q_dst) bulk_g2s(q_dst, q_src, q_bytes, bar);
   bulk_g2s(st + Lay::O_KP, p.kp + (kbase + row) * G::KRB, rows * G::KRB, bar);
   bulk_g2s(st + Lay::O_KS, p.ks + (kbase + row) * G::NG, rows * G::SRB, bar);
   bulk_g2s(st + Lay::O_KB, p.kb + (kbase + row) * G::NG, rows * G::SRB, bar);
@@ -1270,6 +1282,7 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
         const int r0 = (int)(x - U) * kTile, r1 = (int)(xe - U) * kTile;
         const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
         const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
+        const uint16_t* qsrc = p.q + ((int64_t)b * p.Hq + (int64_t)kvh * nrep) * D;
         for (int row = r0; row < r1; row += CH, c++) {
           const int s = c % STAGES;
           if (c >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1))) {
@@ -1278,7 +1291,9 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
             break;
           }
           issue_chunk<BITS, D, GS, CH>(p, stages + s * S::STAGE, &full[s], kbase, vbase, row,
-                                       (uint32_t)min(CH, r1 - row));
+                                       (uint32_t)min(CH, r1 - row),
+                                       row == r0 ? smem + S::QS + s * S::QSLOT : nullptr, qsrc,
+                                       (uint32_t)(nrep * D * 2));
         }
         x = xe;
       }
@@ -1294,7 +1309,6 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
       const int64_t xe = x1 < U + T ? x1 : U + T;
       const int r0 = (int)(x - U) * kTile, r1 = (int)(xe - U) * kTile;
       const int n1 = min(r1, n);
-      load_qfrag<BITS, D, GS, NT, BF>(Q, p, b, kvh, 0, qrows, g, t);
       int klo[NT][2], khi[NT][2];
       column_bounds<NT>(klo, khi, p, 0, qrows, n, t);
       A.reset();
@@ -1308,6 +1322,10 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
           hung = true;
           continue;
         }
+        if (row == r0)  // the segment's query group came with its first chunk
+          load_qfrag<BITS, D, GS, NT, BF>(Q, p, b, kvh, 0, qrows, g, t,
+                                          reinterpret_cast<const uint16_t*>(smem + S::QS +
+                                                                            s * S::QSLOT));
         const int srow0 = row + warp * RW;
         if (srow0 < n1)
           process_slice<BITS, D, GS, NT, RW, CH, BF>(A, Q, p, stages + s * S::STAGE, warp * RW,
@@ -1327,18 +1345,15 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
 }
 
 // Combine the partial slots of unit blockIdx.x for query row blockIdx.y;
-// blockDim.x == D.  Round 1: the (m, l) of every slot (kMergeSlots at most)
-// -> M = max m, weights w = e^(m - M) in shared memory, L = sum l w.
-// Round 2: thread d sums w * o[d] over the slots in slot order (loads issued
-// eight at a time, coalesced across d).
-constexpr int kMergeSlots = 4096;
+// blockDim.x == D, thread d.  Slots are taken 32 at a time: every thread
+// loads the batch's (m, l) and its own o[d] in one round (coalesced across
+// d), then folds the batch into a running (M, L, o) in slot order
+// (deterministic, the same sums in every thread).
+constexpr int kMergeSlots = 4096;  // partial slots per unit at most (launch shape)
 template <int D, int W, int NT, bool BF>
 __global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int grid) {
   constexpr int HQ = 8 * NT;
-  constexpr int NWARP = D / 32;
   constexpr int SLOT = HQ * (D + 2);  // floats per partial slot
-  __shared__ float wsm[kMergeSlots];
-  __shared__ float red_m[NWARP], red_l[NWARP];
   __shared__ int64_t red_t[2];
   const int u = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int Hkv = p.Hkv, b = u / Hkv, kvh = u - b * Hkv;
@@ -1390,43 +1405,32 @@ __global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int g
   const int nslots = (i_last - i_first + 1) * W;  // <= kMergeSlots (host launch shape)
   const float* base = p.ws_o + ((int64_t)i_first + u) * W * SLOT;
 
-  // round 1
-  float mloc = kNeg;
-  for (int j = tid; j < nslots; j += D) mloc = fmaxf(mloc, __ldcg(base + (int64_t)j * SLOT + r));
+  float M = kNeg, L = 0.0f, acc = 0.0f;
+  for (int j0 = 0; j0 < nslots; j0 += 32) {
+    const int nj = min(32, nslots - j0);
+    float m[32], l[32], o[32];
 #pragma unroll
-  for (int o = 16; o; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
-  if (lane == 0) red_m[warp] = mloc;
-  __syncthreads();
-  float M = red_m[0];
+    for (int k = 0; k < 32; k++) {
+      const bool v = k < nj;
+      const float* sp = base + (int64_t)(j0 + k) * SLOT;
+      m[k] = v ? __ldcg(sp + r) : kNeg;
+      l[k] = v ? __ldcg(sp + HQ + r) : 0.0f;
+      o[k] = v ? __ldcg(sp + 2 * HQ + r * D + tid) : 0.0f;
+    }
+    float Mn = M;
 #pragma unroll
-  for (int w = 1; w < NWARP; w++) M = fmaxf(M, red_m[w]);
-  float lloc = 0.0f;
-  for (int j = tid; j < nslots; j += D) {
-    const float* sp = base + (int64_t)j * SLOT;
-    const float w = ex2((__ldcg(sp + r) - M) * kLog2e);
-    wsm[j] = w;
-    lloc = fmaf(__ldcg(sp + HQ + r), w, lloc);
+    for (int k = 0; k < 32; k++) Mn = fmaxf(Mn, m[k]);
+    const float a = ex2((M - Mn) * kLog2e);
+    L *= a;
+    acc *= a;
+#pragma unroll
+    for (int k = 0; k < 32; k++) {
+      const float w = ex2((m[k] - Mn) * kLog2e);
+      L = fmaf(l[k], w, L);
+      acc = fmaf(o[k], w, acc);
+    }
+    M = Mn;
   }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, o);
-  if (lane == 0) red_l[warp] = lloc;
-  __syncthreads();
-  float L = 0.0f;
-#pragma unroll
-  for (int w = 0; w < NWARP; w++) L += red_l[w];
-
-  // round 2
-  const float* op = base + 2 * HQ + r * D + tid;
-  float acc = 0.0f;
-  int j = 0;
-  for (; j + 8 <= nslots; j += 8) {
-    float v[8];
-#pragma unroll
-    for (int k = 0; k < 8; k++) v[k] = __ldcg(op + (int64_t)(j + k) * SLOT);
-#pragma unroll
-    for (int k = 0; k < 8; k++) acc = fmaf(v[k], wsm[j + k], acc);
-  }
-  for (; j < nslots; j++) acc = fmaf(__ldcg(op + (int64_t)j * SLOT), wsm[j], acc);
   write_row<D, BF>(p, orow, tid, acc, M, L);
 }
 
