@@ -257,14 +257,37 @@ __device__ __forceinline__ void lds_words(uint32_t* w, const uint8_t* p) {
 }
 
 // All NG scales (or biases) of one row as f32, times `mul` (a power of two).
+// Each 32-bit word holds two: converted straight from its halves.
 template <int NG, bool BF>
 __device__ __forceinline__ void lds_scales(float* out, const uint16_t* row, float mul = 1.0f) {
   uint32_t w[(NG + 1) / 2];
   lds_words<NG * 2>(w, reinterpret_cast<const uint8_t*>(row));
 #pragma unroll
   for (int i = 0; i < NG; i++) {
-    const uint16_t h = (uint16_t)((i & 1) ? (w[i / 2] >> 16) : (w[i / 2] & 0xffffu));
-    out[i] = dt_to_f<BF>(h) * mul;
+    const uint32_t word = w[i / 2];
+    float v;
+    if constexpr (BF) {
+      v = __uint_as_float((i & 1) ? (word & 0xffff0000u) : (word << 16));
+    } else {
+      const __half2 h2 = *reinterpret_cast<const __half2*>(&word);
+      v = (i & 1) ? __high2float(h2) : __low2float(h2);
+    }
+    out[i] = v * mul;
+  }
+}
+
+// Two f32 values rounded to the dtype (one packed conversion).
+template <bool BF>
+__device__ __forceinline__ void round_dt2(float a, float b, float& ra, float& rb) {
+  if constexpr (BF) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(&h);
+    ra = __uint_as_float(w << 16);
+    rb = __uint_as_float(w & 0xffff0000u);
+  } else {
+    const __half2 h = __floats2half2_rn(a, b);
+    ra = __low2float(h);
+    rb = __high2float(h);
   }
 }
 
@@ -464,13 +487,14 @@ __device__ __forceinline__ void column_bounds(int (&klo)[NT][2], int (&khi)[NT][
 // One consumer slice: RW key rows of the stage at `st` (chunk rows r_base..,
 // global key rows srow0..), valid below n1; `fast` = every row valid for
 // every column (no masking work).
-template <int BITS, int D, int GS, int NT, int RW, int CH, bool BF>
+template <int BITS, int D, int GS, int NT, int RW, int CH, bool BF, bool FAST>
 __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
                                               const QFrag<BITS, D, GS, NT>& Q, const Params& p,
                                               const uint8_t* st, int r_base, int srow0, int n1,
-                                              bool fast, const int (&klo)[NT][2],
+                                              const int (&klo)[NT][2],
                                               const int (&khi)[NT][2], int qr0, int qrows,
                                               int kvh, int b, int g, int t) {
+  constexpr bool fast = FAST;
   using G = Geo<BITS, D, GS>;
   using Lay = StageLayout<BITS, D, GS, CH>;
   constexpr int MTS = RW / 16;  // 16-row m-tiles per consumer slice
@@ -547,6 +571,14 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
   float x[NT][2][MTS][2];
   bool vv[NT][2][MTS][2];
   bool above = false;
+  float rsc[MTS][NT][4];  // logits rounded to the dtype, two per conversion
+#pragma unroll
+  for (int mt = 0; mt < MTS; mt++)
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      round_dt2<BF>(sc[mt][nt][0], sc[mt][nt][1], rsc[mt][nt][0], rsc[mt][nt][1]);
+      round_dt2<BF>(sc[mt][nt][2], sc[mt][nt][3], rsc[mt][nt][2], rsc[mt][nt][3]);
+    }
 #pragma unroll
   for (int nt = 0; nt < NT; nt++)
 #pragma unroll
@@ -556,7 +588,7 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
 #pragma unroll
         for (int e = 0; e < 2; e++) {
           const int r = srow0 + mt * 16 + g + 8 * e;
-          const float rs = round_dt<BF>(sc[mt][nt][2 * e + hh]);
+          const float rs = rsc[mt][nt][2 * e + hh];
           if (fast) {
             vv[nt][hh][mt][e] = true;
             x[nt][hh][mt][e] = rs;
@@ -708,6 +740,22 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
           mma16816(o_acc[grp * G::MTG + mt][nt], af[mt], bfr[nt][0], bfr[nt][1]);
     }
   }
+}
+
+// process_slice with the full-slice flag as a compile-time branch.
+template <int BITS, int D, int GS, int NT, int RW, int CH, bool BF>
+__device__ __forceinline__ void run_slice(WarpAcc<BITS, D, GS, NT>& A,
+                                          const QFrag<BITS, D, GS, NT>& Q, const Params& p,
+                                          const uint8_t* st, int r_base, int srow0, int n1,
+                                          bool fast, const int (&klo)[NT][2],
+                                          const int (&khi)[NT][2], int qr0, int qrows, int kvh,
+                                          int b, int g, int t) {
+  if (fast)
+    process_slice<BITS, D, GS, NT, RW, CH, BF, true>(A, Q, p, st, r_base, srow0, n1, klo, khi, qr0,
+                                                     qrows, kvh, b, g, t);
+  else
+    process_slice<BITS, D, GS, NT, RW, CH, BF, false>(A, Q, p, st, r_base, srow0, n1, klo, khi,
+                                                      qr0, qrows, kvh, b, g, t);
 }
 
 // Row-lane reductions of l and the bias sums at the end of a warp's work.
@@ -1044,7 +1092,7 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_kernel(con
       if (srow0 < n1) {
         const bool fast = !p.scores && srow0 + RW <= n1 && srow0 + RW - 1 <= kz_min &&
                           srow0 >= ka_max;
-        process_slice<BITS, D, GS, NT, RW, CH, BF>(A, Q, p, stages + s * S::STAGE, warp * RW,
+        run_slice<BITS, D, GS, NT, RW, CH, BF>(A, Q, p, stages + s * S::STAGE, warp * RW,
                                                    srow0, n1, fast, klo, khi, qr0, qrows, kvh, b,
                                                    g, t);
       }
@@ -1188,7 +1236,7 @@ __device__ __forceinline__ int bal_working_ctas(int64_t RT, int grid) {
 }
 
 template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES, bool BF>
-__global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) {
+__global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel(const Params p) {
   using S = BalSmem<BITS, D, GS, NT, W, RW, STAGES>;
   constexpr int HQ = S::HQ;
   constexpr int CH = S::CH;
@@ -1328,7 +1376,7 @@ __global__ void __launch_bounds__((W + 1) * 32) attn_bal_kernel(const Params p) 
                                                                             s * S::QSLOT));
         const int srow0 = row + warp * RW;
         if (srow0 < n1)
-          process_slice<BITS, D, GS, NT, RW, CH, BF>(A, Q, p, stages + s * S::STAGE, warp * RW,
+          run_slice<BITS, D, GS, NT, RW, CH, BF>(A, Q, p, stages + s * S::STAGE, warp * RW,
                                                      srow0, n1, srow0 + RW <= n1, klo, khi, 0,
                                                      qrows, kvh, b, g, t);
         __syncwarp();
