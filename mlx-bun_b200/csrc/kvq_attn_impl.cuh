@@ -1004,6 +1004,10 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_kernel(con
   float* sl = reinterpret_cast<float*>(smem + S::SL);
   float* ra = reinterpret_cast<float*>(smem + S::RA);
 
+  // launched as a programmatic dependent (launch_pdl)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
   const bool producer = warp == W;
   const int split = blockIdx.x;
@@ -1265,6 +1269,9 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     ctrl[1] = 0;
   }
+  // launched as a programmatic dependent (launch_pdl): the previous kernel
+  // (the append, typically) is complete past this point
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   int64_t RT = (int64_t)B * Hkv * p.Tu;
   if (ragged) {
     for (int bb = tid; bb < B; bb += blockDim.x) blen[bb] = min(max(p.seq_lens[bb], 0), p.N);
@@ -1333,7 +1340,11 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
         const uint16_t* qsrc = p.q + ((int64_t)b * p.Hq + (int64_t)kvh * nrep) * D;
         for (int row = r0; row < r1; row += CH, c++) {
           const int s = c % STAGES;
-          if (c >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1))) {
+          // Staggered start: the rest of the ring is requested once the first
+          // chunk has landed, so every CTA's first chunk (and its math) comes
+          // ahead of the bulk of the initial fill.
+          if ((c == 1 && !mbar_wait(&full[0], 0u)) ||
+              (c >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1)))) {
             hung = true;
             ctrl[1] = 1;
             break;
@@ -1440,7 +1451,9 @@ __global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int g
     RT = red_t[1];
   }
 
-  // Everything below reads what the attention grid wrote.
+  // Everything below reads what the attention grid wrote.  (The next
+  // kernel on the stream may be scheduled meanwhile; it waits likewise.)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (T == 0) {  // an entry with no keys: a zero row (or an empty partial)
@@ -1591,24 +1604,14 @@ int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* o
     return KVQ_OK;
   }
   const dim3 grid = bal ? dim3(s.ctas) : dim3(s.nsplit, p.Hkv * s.QB, B);
-  kern<<<grid, (kWarps + 1) * 32, smem, st>>>(p);
-  KVQ_CUDA_TRY(cudaGetLastError());
+  KVQ_CUDA_TRY(launch_pdl(kern, grid, dim3((kWarps + 1) * 32), (size_t)smem, st, p));
   if (bal) {
     // merge of the per-warp partials, a programmatic dependent of the
     // attention grid (it waits for that grid inside, with griddepcontrol)
     void (*merge)(Params, int) = p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true>
                                         : attn_bal_merge_kernel<D, kWarps, NT, false>;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(B * p.Hkv), (unsigned)p.nrep);
-    cfg.blockDim = dim3(D);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    KVQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, merge, p, s.ctas));
+    KVQ_CUDA_TRY(launch_pdl(merge, dim3((unsigned)(B * p.Hkv), (unsigned)p.nrep), dim3(D), 0, st,
+                            p, s.ctas));
   }
   return KVQ_OK;
 }

@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "kvq.h"
 
@@ -56,6 +57,28 @@ struct AttnArgs {
   const void* q;
   const int32_t* seq_lens;  // device, nullable
 };
+
+// Launch `kern` as a programmatic dependent of the previous kernel on the
+// stream: it may be scheduled before that kernel finishes, so every kernel
+// launched this way executes `griddepcontrol.wait` before its first access
+// to global memory (and `griddepcontrol.launch_dependents` early, to let the
+// next one do the same).  Hides the launch gap between the append, attention
+// and merge kernels of a decode step.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 size_t decode_workspace_bytes(int B, int Hkv, int Hq, int N, int D);
 // Exact workspace bytes one decode launch with these arguments uses, and the

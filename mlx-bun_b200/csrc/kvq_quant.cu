@@ -62,6 +62,10 @@ __device__ __forceinline__ float word_to_f(uint32_t w, int half) {
 // BITS: 4 or 8.  TPG: threads per group (gs * BITS / 32).  VEC: 16-B loads.
 template <int BITS, int TPG, bool BF16, bool VEC>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const Jobs jobs) {
+  // launched as a programmatic dependent (launch_pdl): let the next kernel be
+  // scheduled, then wait for the previous one before reading anything
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   constexpr int PER = 32 / BITS;
   constexpr float NB = (float)((1 << BITS) - 1);
   const Job& J = jobs.j[blockIdx.y];
@@ -144,10 +148,9 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const Jobs jobs) {
 template <int BITS, int TPG, bool BF16>
 int32_t dispatch_vec(bool vec, dim3 grid, cudaStream_t st, const Jobs& jobs) {
   if (vec)
-    quantize_rows_kernel<BITS, TPG, BF16, true><<<grid, 256, 0, st>>>(jobs);
+    KVQ_CUDA_TRY(launch_pdl(quantize_rows_kernel<BITS, TPG, BF16, true>, grid, dim3(256), 0, st, jobs));
   else
-    quantize_rows_kernel<BITS, TPG, BF16, false><<<grid, 256, 0, st>>>(jobs);
-  KVQ_CUDA_TRY(cudaGetLastError());
+    KVQ_CUDA_TRY(launch_pdl(quantize_rows_kernel<BITS, TPG, BF16, false>, grid, dim3(256), 0, st, jobs));
   return KVQ_OK;
 }
 
