@@ -552,10 +552,18 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
       }
 #pragma unroll
       for (int nt = 0; nt < NT; nt++) {
-        sc[mt][nt][0] = fmaf(ks0[grp], acc[nt][0], fmaf(kb0[grp], qs_r[nt][grp][0], sc[mt][nt][0]));
-        sc[mt][nt][1] = fmaf(ks0[grp], acc[nt][1], fmaf(kb0[grp], qs_r[nt][grp][1], sc[mt][nt][1]));
-        sc[mt][nt][2] = fmaf(ks1[grp], acc[nt][2], fmaf(kb1[grp], qs_r[nt][grp][0], sc[mt][nt][2]));
-        sc[mt][nt][3] = fmaf(ks1[grp], acc[nt][3], fmaf(kb1[grp], qs_r[nt][grp][1], sc[mt][nt][3]));
+        // s += ks * acc + kb * sum(q), two query columns per paired fp32 op
+        const float2 qs2 = make_float2(qs_r[nt][grp][0], qs_r[nt][grp][1]);
+        float2 s01 = make_float2(sc[mt][nt][0], sc[mt][nt][1]);
+        float2 s23 = make_float2(sc[mt][nt][2], sc[mt][nt][3]);
+        s01 = __ffma2_rn(make_float2(kb0[grp], kb0[grp]), qs2, s01);
+        s23 = __ffma2_rn(make_float2(kb1[grp], kb1[grp]), qs2, s23);
+        s01 = __ffma2_rn(make_float2(ks0[grp], ks0[grp]), make_float2(acc[nt][0], acc[nt][1]), s01);
+        s23 = __ffma2_rn(make_float2(ks1[grp], ks1[grp]), make_float2(acc[nt][2], acc[nt][3]), s23);
+        sc[mt][nt][0] = s01.x;
+        sc[mt][nt][1] = s01.y;
+        sc[mt][nt][2] = s23.x;
+        sc[mt][nt][3] = s23.y;
       }
     }
   }
@@ -605,7 +613,8 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
           }
           above |= x[nt][hh][mt][e] > m_run[nt][hh];
         }
-  if (__any_sync(0xffffffffu, above)) {
+  const bool rescale_all = __any_sync(0xffffffffu, above);
+  if (rescale_all) {
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
@@ -627,36 +636,39 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
         alpha[nt][hh] = al;
         m_run[nt][hh] = mn;
         mls_run[nt][hh] = mn * kLog2e;
-        float lsum = 0.0f;
-#pragma unroll
-        for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-          for (int e = 0; e < 2; e++) {
-            const float pe = ex2(fmaf(x[nt][hh][mt][e], kLog2e, -mls_run[nt][hh]));
-            const float pv = (fast || vv[nt][hh][mt][e]) ? pe : 0.0f;
-            pr[mt][nt][2 * e + hh] = pv;
-            lsum += pv;
-          }
-        l_run[nt][hh] = fmaf(l_run[nt][hh], al, lsum);
       }
     }
-  } else {
+  }
+  // p = 2^(x log2e - m log2e) for both columns of a lane at once (paired
+  // fp32 ops); the lazy path keeps l, the update path rescales it by alpha
+  {
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++)
+    for (int nt = 0; nt < NT; nt++) {
+      const float2 nm = make_float2(-mls_run[nt][0], -mls_run[nt][1]);
+      float2 lsum = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int hh = 0; hh < 2; hh++) {
-        float lsum = 0.0f;
+      for (int mt = 0; mt < MTS; mt++)
 #pragma unroll
-        for (int mt = 0; mt < MTS; mt++)
-#pragma unroll
-          for (int e = 0; e < 2; e++) {
-            const float pe = ex2(fmaf(x[nt][hh][mt][e], kLog2e, -mls_run[nt][hh]));
-            const float pv = (fast || vv[nt][hh][mt][e]) ? pe : 0.0f;
-            pr[mt][nt][2 * e + hh] = pv;
-            lsum += pv;
+        for (int e = 0; e < 2; e++) {
+          const float2 arg = __ffma2_rn(make_float2(x[nt][0][mt][e], x[nt][1][mt][e]),
+                                        make_float2(kLog2e, kLog2e), nm);
+          float2 pv = make_float2(ex2(arg.x), ex2(arg.y));
+          if (!fast) {
+            pv.x = vv[nt][0][mt][e] ? pv.x : 0.0f;
+            pv.y = vv[nt][1][mt][e] ? pv.y : 0.0f;
           }
-        l_run[nt][hh] += lsum;
+          pr[mt][nt][2 * e] = pv.x;
+          pr[mt][nt][2 * e + 1] = pv.y;
+          lsum = __fadd2_rn(lsum, pv);
+        }
+      if (rescale_all) {
+        l_run[nt][0] = fmaf(l_run[nt][0], alpha[nt][0], lsum.x);
+        l_run[nt][1] = fmaf(l_run[nt][1], alpha[nt][1], lsum.y);
+      } else {
+        l_run[nt][0] += lsum.x;
+        l_run[nt][1] += lsum.y;
       }
+    }
   }
   if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
@@ -695,13 +707,18 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
         const float p0 = pr[kk][nt][0], p1 = pr[kk][nt][1], p2 = pr[kk][nt][2],
                     p3 = pr[kk][nt][3];
         float q0, q1, q2, q3;
-        if (fast) {
-          pb[nt][grp][0] = fmaf(p0, vb0[grp], fmaf(p2, vb1[grp], pb[nt][grp][0]));
-          pb[nt][grp][1] = fmaf(p1, vb0[grp], fmaf(p3, vb1[grp], pb[nt][grp][1]));
-          q0 = p0 * vs0[grp];
-          q1 = p1 * vs0[grp];
-          q2 = p2 * vs1[grp];
-          q3 = p3 * vs1[grp];
+        if (fast) {  // paired fp32 ops: the two query columns of a lane
+          float2 pbv = make_float2(pb[nt][grp][0], pb[nt][grp][1]);
+          pbv = __ffma2_rn(make_float2(p2, p3), make_float2(vb1[grp], vb1[grp]), pbv);
+          pbv = __ffma2_rn(make_float2(p0, p1), make_float2(vb0[grp], vb0[grp]), pbv);
+          pb[nt][grp][0] = pbv.x;
+          pb[nt][grp][1] = pbv.y;
+          const float2 q01 = __fmul2_rn(make_float2(p0, p1), make_float2(vs0[grp], vs0[grp]));
+          const float2 q23 = __fmul2_rn(make_float2(p2, p3), make_float2(vs1[grp], vs1[grp]));
+          q0 = q01.x;
+          q1 = q01.y;
+          q2 = q23.x;
+          q3 = q23.y;
         } else {
           pb[nt][grp][0] += (p0 != 0.0f ? p0 * vb0[grp] : 0.0f) + (p2 != 0.0f ? p2 * vb1[grp] : 0.0f);
           pb[nt][grp][1] += (p1 != 0.0f ? p1 * vb0[grp] : 0.0f) + (p3 != 0.0f ? p3 * vb1[grp] : 0.0f);
