@@ -363,6 +363,108 @@ def run_gpu(args, rank, world, local_rank):
     return res
 
 
+CFG4 = dict(B=1, Hq=32, Hkv=8, D=128, N_prior=16384, L=512, bits=8, gs=64, outliers=4)
+
+
+def prefill_flops(c):
+    """Causal chunk of L rows after N_prior keys: 4 * Hq * L * D * (N_prior + (L + 1) / 2)."""
+    return 4 * c["Hq"] * c["L"] * c["D"] * (c["N_prior"] + (c["L"] + 1) / 2)
+
+
+def run_prefill(args):
+    """Config 4: chunked prefill of 512 query rows (causal in the chunk) over a
+    kv8 cache of 16,384 prior rows plus the chunk, appended first.  One step =
+    append of the 512 K/V rows + prefill attention; both timed with CUDA
+    events over graph replays of NL distinct layers; the attention alone is
+    timed the same way for the tensor-core roofline."""
+    import numpy as np
+    import torch
+    import kvq
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    c = CFG4
+    B, Hq, Hkv, D, Np, L = c["B"], c["Hq"], c["Hkv"], c["D"], c["N_prior"], c["L"]
+    scale = 1.0 / np.sqrt(D)
+    NL = 4  # 4 x 36.8 MB of K/V: above L2 across a replay
+    g = torch.Generator(device=device)
+    g.manual_seed(11)
+    layers = []
+    for _ in range(NL):
+        cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=(Np + L + 255) // 256 * 256)
+        k = torch.randn(B, Hkv, Np, D, generator=g, device=device)
+        k[..., :c["outliers"]] *= 8.0
+        v = torch.randn(B, Hkv, Np, D, generator=g, device=device)
+        cache.update_and_fetch_quantized(k.half(), v.half())
+        kn = torch.randn(B, Hkv, L, D, generator=g, device=device)
+        kn[..., :c["outliers"]] *= 8.0
+        layers.append(dict(cache=cache, kn=kn.half(),
+                           vn=torch.randn(B, Hkv, L, D, generator=g, device=device).half(),
+                           q=torch.randn(B, Hq, L, D, generator=g, device=device).half()))
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    mask = None
+
+    def step(Ly):
+        qk, qv = Ly["cache"].update_and_fetch_quantized(Ly["kn"], Ly["vn"])
+        Ly["out"] = kvq.quantized_sdpa(Ly["q"], qk, qv, scale, Ly["cache"].make_mask(L, None))
+        Ly["cache"].trim(L)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            for Ly in layers:
+                step(Ly)
+        torch.cuda.synchronize()
+        g_step = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step, stream=stream):
+            for Ly in layers:
+                step(Ly)
+        views, masks = [], []
+        for Ly in layers:
+            views.append(Ly["cache"].update_and_fetch_quantized(Ly["kn"], Ly["vn"]))
+            masks.append(Ly["cache"].make_mask(L, None))
+        g_att = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_att, stream=stream):
+            for Ly, (qk, qv), m in zip(layers, views, masks):
+                kvq.quantized_sdpa(Ly["q"], qk, qv, scale, m)
+        for Ly in layers:
+            Ly["cache"].trim(L)
+        for _ in range(3):
+            g_step.replay()
+            g_att.replay()
+        torch.cuda.synchronize()
+        reps = max(1, args.steps // NL)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(stream)
+        for _ in range(reps):
+            g_step.replay()
+        ev[1].record(stream)
+        for _ in range(reps):
+            g_att.replay()
+        ev[2].record(stream)
+        ev[2].synchronize()
+    step_ms = ev[0].elapsed_time(ev[1]) / (reps * NL)
+    att_ms = ev[1].elapsed_time(ev[2]) / (reps * NL)
+    fl = prefill_flops(c)
+    try:
+        peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+        pk = "measured (bf16 dense burst; fp16 runs at the same rate)"
+    except Exception:
+        peak, pk = 1590.0, "fallback"
+    att_tf = fl / (att_ms / 1e3) / 1e12
+    print(json.dumps({
+        "metric": "quantized-KV chunked prefill TFLOP/s (config 4: B1 Hq32 Hkv8 D128, 16384 prior + 512-row causal chunk, kv8 gs64)",
+        "value": round(fl / (step_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": reps * NL, "warmup": args.warmup, "ms_per_step": round(step_ms, 5),
+        "higher_is_better": True, "dtype": "u8 codes/f16", "data": "synthetic (seeded torch.randn)",
+        "config": {"workload": "config4-kv8-prefill-append", "flops_per_step": fl,
+                   "layers_cycled": NL, "l2": "4 distinct layers (147 MB of K/V) per replay"},
+        "roofline": {"bound": "tensor", "achieved": round(att_tf, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(att_tf / peak, 4), "peak_kind": pk,
+                     "kernel": "attn_kernel (split, mma.sync m16n8k16)",
+                     "kernel_us": round(att_ms * 1e3, 3)},
+        "gpu_launches": 2 * reps * NL}))
+
+
 def profile_run(args):
     """Fixed small workload for ncu: 3 config-2 layers (227 MB, above L2),
     `--steps` launches of one kernel, cycling layers."""
@@ -396,12 +498,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="kvq", choices=["kvq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: the config-2 step the driver reads (default); prefill: "
+                         "config 4 chunked prefill, a separate JSON line")
     ap.add_argument("--profile", choices=["decode", "append"], default=None,
                     help="run only the named kernel over 3 config-2 layers, `--steps` "
                          "launches, no timing (a small, fixed workload for ncu captures)")
     args = ap.parse_args()
     if args.profile:
         return profile_run(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
