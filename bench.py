@@ -74,7 +74,8 @@ def peaks():
 
 
 def traffic_from_profiles():
-    """dram bytes per decode launch from the committed ncu summary (or None)."""
+    """dram bytes of the decode's attention launch from the committed ncu summary
+    (the merge reads the partials from L2), or None."""
     p = os.path.join(ROOT, "profiles", "attn_decode_config2.md")
     try:
         for line in open(p):
@@ -349,10 +350,11 @@ def run_gpu(args, rank, world, local_rank):
                     "d2h_bytes_per_step": int(ho[0].numel() * 2),
                     "us_per_step": round(1e3 * e2e_ms / K2, 3), "steps": K2,
                     "path": "kvq Python API per step (eager), pinned host buffers"},
-            "gpu_launches": 2 * K,  # one fused K/V append + one decode per step
+            "gpu_launches": 3 * K,  # per step: fused K/V append, attention, merge of partials
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind, "kernel": "attn_kernel<4,128,64,1> (decode)",
+                         "peak_kind": peak_kind,
+                         "kernel": "decode = attn_bal_kernel<4,128,64,1> + attn_bal_merge_kernel",
                          "kernel_us": round(kmean * 1e3, 3),
                          "bytes_per_launch": decode_launch_bytes(c),
                          "traffic": traffic_from_profiles(),
