@@ -462,7 +462,7 @@ def run_prefill(args):
                    "layers_cycled": NL, "l2": "4 distinct layers (147 MB of K/V) per replay"},
         "roofline": {"bound": "tensor", "achieved": round(att_tf, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(att_tf / peak, 4), "peak_kind": pk,
-                     "kernel": "attn_kernel (split, mma.sync m16n8k16)",
+                     "kernel": "prefill_tc_kernel (tcgen05 UMMA, TMEM accumulators)",
                      "kernel_us": round(att_ms * 1e3, 3)},
         "gpu_launches": 2 * reps * NL}))
 

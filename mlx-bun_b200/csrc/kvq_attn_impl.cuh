@@ -1662,6 +1662,10 @@ int32_t pick_d(Params& p, const LaunchShape& s, int Dv, int GSv, int NT, int B, 
   return fail(KVQ_ERR_ARG, "attention: head_dim must be 64, 128 or 256");
 }
 
+// The tcgen05 chunked prefill (kvq_prefill_tc.cu): 8-bit codes, D 128, group 64.
+bool prefill_tc_supported(int bits, int D, int gs, int L, bool scores);
+int32_t launch_prefill_tc(Params& p, int B, cudaStream_t st);
+
 // Per-width launchers (one translation unit each, compiled in parallel);
 // s.ctas > 0 selects the balanced kernel.  With occ != nullptr they only
 // report that kernel's resident blocks per SM.

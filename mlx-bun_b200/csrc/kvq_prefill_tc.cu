@@ -1,0 +1,506 @@
+// kvq_prefill_tc.cu — chunked prefill attention on the 5th-generation tensor
+// cores (tcgen05 / UMMA with TMEM accumulators) for 8-bit codes, D = 128,
+// group 64 (the config-4 shape); other shapes take the split kernel.
+//
+// A CTA owns 128 query rows of one (batch, kv head): rows are (position,
+// head) pairs of the GQA group (row qr -> position qr / nrep, head qr %
+// nrep), so every key tile serves all query heads that share it.  Thread r
+// of the 4 softmax warps owns query row r — the row of TMEM lane r — so the
+// online softmax needs no cross-lane traffic.  A fifth warp streams the key
+// rows in tiles of 128 with 1-D TMA bulk copies (the decode ring).
+//
+// Per key tile:
+//   1. the codes become fp16 subnormals (code * 2^-24, exact) in shared
+//      memory, 128-byte-swizzled rows of 64 d: the K tile is the K-major B
+//      operand of QK^T, the V tile (same layout) the MN-major B operand of PV;
+//   2. QK^T per quantisation group g: S_g = Q_g . C_g^T (M 128, N 128, K 64)
+//      into TMEM (qdot factoring: logit = sum_g ks*2^24*S_g + kb*sum(q_g));
+//   3. softmax, two passes over TMEM: logits rounded to the dtype and masked
+//      (written back over S_0) with the tile maximum, then p = 2^((x - m)
+//      log2 e) against the row's running maximum m, P'_g = fp16(p * vs_g)
+//      into TMEM (the A operand of PV) and sum(p * vb_g) in registers.  O is
+//      rescaled only when the maximum grows by more than 2^8 (lazy rescale:
+//      P' stays far inside fp16, the final O / l is the same);
+//   4. PV per group: O_g += P'_g . V_g (M 128, N 64, K 128) in TMEM.
+// The steps run in order (commit -> mbarrier between them).  Every wait is
+// bounded; on timeout the kernel raises the device error flag and skips the
+// rest of its tiles.
+//
+// TMEM (512 columns, one CTA per SM): S_0 [0,128) S_1 [128,256) P'_0
+// [256,320) P'_1 [320,384) O_0 [384,448) O_1 [448,512).
+#include "kvq_attn_impl.cuh"
+
+namespace kvq {
+namespace attn {
+namespace {
+
+constexpr int kRows = 128;     // query rows per CTA (TMEM lanes)
+constexpr int kKeys = 128;     // keys per tile
+constexpr int kTcStages = 2;   // raw TMA ring stages
+constexpr int TD = 128, TGS = 64, TNG = 2;
+
+// shared memory (offsets from a 1024-byte aligned base)
+constexpr int kQOff = 0;                        // [TNG] SW128 [128 rows][64] fp16
+constexpr int kKcOff = kQOff + TNG * 16384;     // [TNG] SW128 [128 keys][64] fp16
+constexpr int kVcOff = kKcOff + TNG * 16384;    // [TNG] SW128 [128 keys][64] fp16
+constexpr int kSclOff = kVcOff + TNG * 16384;   // f32 [4][TNG][128]: ks*2^24, kb, vs, vb
+constexpr int kRawOff = kSclOff + 4 * TNG * kKeys * 4;
+using RawLay = StageLayout<8, TD, TGS, kKeys>;
+constexpr int kBarOff = kRawOff + kTcStages * RawLay::STAGE;  // full[2], empty[2], qk, pv
+constexpr int kCtlOff = kBarOff + (2 * kTcStages + 2) * 8;   // tmem base, abort flag
+constexpr int kTcSmem = kCtlOff + 16 + 1024;                  // + alignment slack
+
+// byte offset of element (row, c) of a 128-byte-swizzled tile of 64-element rows
+__device__ __forceinline__ uint32_t sw128(int row, int c) {
+  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + (((c >> 3) ^ (row & 7)) << 4) + (c & 7) * 2);
+}
+
+// UMMA shared-memory descriptor: 128-byte swizzle, 8-row groups 1024 B apart
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// instruction descriptor, kind::f16: f16 A/B, f32 accumulate
+__device__ __forceinline__ uint32_t idesc_f16(int M, int N, int b_mn_major) {
+  return (1u << 4) | ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u));
+}
+
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc), "r"(0u));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive TMEM columns of this thread's lane
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]),
+        "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
+        "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(addr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(addr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]),
+      "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]),
+      "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(addr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 8 byte codes (two words) as four fp16-subnormal pairs (code in the low
+// mantissa bits, exponent zero)
+__device__ __forceinline__ uint4 codes8_to_f16(uint32_t w0, uint32_t w1) {
+  uint4 r;
+  r.x = prmt(w0, 0u, 0x4140u);
+  r.y = prmt(w0, 0u, 0x4342u);
+  r.z = prmt(w1, 0u, 0x4140u);
+  r.w = prmt(w1, 0u, 0x4342u);
+  return r;
+}
+
+template <bool BF>
+__global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kBarOff);
+  uint64_t* empty = full + kTcStages;
+  uint64_t* qk_bar = empty + kTcStages;
+  uint64_t* pv_bar = qk_bar + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sm + kCtlOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + kCtlOff + 4);
+  float* scl = reinterpret_cast<float*>(sm + kSclOff);  // [4][TNG][128]
+
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool producer = warp == 4;
+  const int qt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int nrep = p.nrep, L = p.L, qrows = nrep * L;
+  const int qr0 = qt * kRows;
+  int Nb = p.N;
+  if (p.seq_lens) Nb = min(max(p.seq_lens[b], 0), p.N);
+
+  // key range of this query block (union over its rows), tile aligned at the front
+  int lo = 0, hi = Nb;
+  const int qr_last = min(qr0 + kRows, qrows) - 1;
+  if (p.mask_mode == 1) {
+    hi = min(Nb, Nb - L + qr_last / nrep + 1);
+    if (p.window > 0) lo = max(0, Nb - L + qr0 / nrep - p.window + 1) / kTile * kTile;
+    if (hi < lo) hi = lo;
+  }
+  const int ntiles = (hi - lo + kKeys - 1) / kKeys;
+
+  if (tid == 0) {
+    for (int s = 0; s < kTcStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);
+    }
+    mbar_init(qk_bar, 1);
+    mbar_init(pv_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    *abort_flag = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = *tmem_holder;
+
+  const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
+  const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
+  bool hung = false;
+
+  if (producer) {
+    if (lane == 0) {
+      for (int j = 0; j < ntiles; j++) {
+        const int s = j % kTcStages;
+        if (j >= kTcStages &&
+            (*abort_flag || !mbar_wait(&empty[s], (uint32_t)(((j / kTcStages) & 1) ^ 1)))) {
+          hung = true;
+          *abort_flag = 1;
+          break;
+        }
+        const int row = lo + j * kKeys;
+        const int rows = min(kKeys, hi - row);
+        issue_chunk<8, TD, TGS, kKeys>(p, sm + kRawOff + s * RawLay::STAGE, &full[s], kbase, vbase,
+                                       row, (uint32_t)((rows + kTile - 1) / kTile * kTile));
+      }
+    }
+  } else {
+    // ---- query row of this thread: q * dtype(scale) rounded to the dtype ----
+    const int r = tid;  // 0..127, TMEM lane r
+    const int qr = qr0 + r;
+    const bool qvalid = qr < qrows;
+    const int l = qvalid ? qr / nrep : 0, hh = qvalid ? qr - l * nrep : 0;
+    const int pos = Nb - L + l;  // key position of this query row (bottom-right aligned)
+    int klo = 0, khi = Nb - 1;
+    if (p.mask_mode == 1) {
+      khi = min(khi, pos);
+      if (p.window > 0) klo = max(0, pos - p.window + 1);
+    }
+    float qs[TNG] = {0.0f, 0.0f};
+    {
+      const float scale_dt = round_dt<BF>(p.scale);
+      const uint16_t* qrow = p.q + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * TD;
+#pragma unroll
+      for (int g = 0; g < TNG; g++) {
+        uint8_t* qg = sm + kQOff + g * 16384;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; c8++) {
+          uint32_t w[4];
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int d = g * TGS + c8 * 8 + 2 * j;
+            const float a0 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d)) * scale_dt) : 0.0f;
+            const float a1 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d + 1)) * scale_dt) : 0.0f;
+            qs[g] += a0 + a1;
+            w[j] = pack_h2(a0, a1);
+          }
+          *reinterpret_cast<uint4*>(qg + sw128(r, c8 * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+    float m_used = kNeg, lsum = 0.0f, pbs[TNG] = {0.0f, 0.0f};
+    const uint32_t lane_base = tm + ((uint32_t)(warp * 32) << 16);
+    const uint32_t idesc_qk = idesc_f16(kRows, kKeys, 0);
+    const uint32_t idesc_pv = idesc_f16(kRows, TGS, 1);
+
+    for (int j = 0; j < ntiles; j++) {
+      const int s = j % kTcStages;
+      const int n0 = lo + j * kKeys;
+      // ---- 1. codes -> fp16 subnormals (K and V), scales -> f32 ----
+      {
+        const bool ok = !hung && !*abort_flag && mbar_wait(&full[s], (uint32_t)((j / kTcStages) & 1));
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (!hung && lane == 0) *abort_flag = 1;
+          hung = true;
+        }
+      }
+      if (!hung) {
+        const uint8_t* st = sm + kRawOff + s * RawLay::STAGE;
+#pragma unroll 4
+        for (int it = 0; it < (kKeys * TNG * 8) / 128; it++) {
+          const int idx = tid + it * 128;
+          const int key = idx >> 4, g = (idx >> 3) & 1, c8 = idx & 7;
+          const uint2 kw = *reinterpret_cast<const uint2*>(st + RawLay::O_KP + key * TD + g * TGS + c8 * 8);
+          const uint2 vw = *reinterpret_cast<const uint2*>(st + RawLay::O_VP + key * TD + g * TGS + c8 * 8);
+          const uint32_t o = sw128(key, c8 * 8);
+          *reinterpret_cast<uint4*>(sm + kKcOff + g * 16384 + o) = codes8_to_f16(kw.x, kw.y);
+          *reinterpret_cast<uint4*>(sm + kVcOff + g * 16384 + o) = codes8_to_f16(vw.x, vw.y);
+        }
+        {
+          // keys past the range hold stale ring bytes: their scales and
+          // biases become 0 so that p = 0 never meets a non-finite value
+          const int key = tid;
+          const bool live = n0 + key < hi;
+          const uint32_t ksw = live ? *reinterpret_cast<const uint32_t*>(st + RawLay::O_KS + key * 4) : 0u;
+          const uint32_t kbw = live ? *reinterpret_cast<const uint32_t*>(st + RawLay::O_KB + key * 4) : 0u;
+          const uint32_t vsw = live ? *reinterpret_cast<const uint32_t*>(st + RawLay::O_VS + key * 4) : 0u;
+          const uint32_t vbw = live ? *reinterpret_cast<const uint32_t*>(st + RawLay::O_VB + key * 4) : 0u;
+#pragma unroll
+          for (int g = 0; g < TNG; g++) {
+            const auto half_of = [&](uint32_t wv) -> float {
+              const uint16_t h = (uint16_t)(g ? (wv >> 16) : (wv & 0xffffu));
+              return dt_to_f<BF>(h);
+            };
+            scl[(0 * TNG + g) * kKeys + key] = half_of(ksw) * kCodeUnitInv;
+            scl[(1 * TNG + g) * kKeys + key] = half_of(kbw);
+            scl[(2 * TNG + g) * kKeys + key] = half_of(vsw);
+            scl[(3 * TNG + g) * kKeys + key] = half_of(vbw);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // raw stage free
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      tc_fence_after();
+
+      // ---- 2. S_g = Q_g . C_g^T ----
+      if (tid == 0 && !hung && !*abort_flag) {
+#pragma unroll
+        for (int g = 0; g < TNG; g++)
+#pragma unroll
+          for (int ks = 0; ks < TGS / 16; ks++)
+            umma_ss(tm + g * 128, desc_sw128(smem_u32(sm + kQOff + g * 16384) + 32 * ks),
+                    desc_sw128(smem_u32(sm + kKcOff + g * 16384) + 32 * ks), idesc_qk,
+                    ks > 0 ? 1u : 0u);
+        umma_commit(qk_bar);
+      }
+      {
+        const bool ok = !hung && !*abort_flag && mbar_wait(qk_bar, (uint32_t)(j & 1));
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (!hung && lane == 0) *abort_flag = 1;
+          hung = true;
+        }
+      }
+      tc_fence_after();
+
+      // ---- 3a. logits (rounded, masked) over S_0, tile maximum ----
+      float tmax = kNeg;
+      if (!hung) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < kKeys; c0 += 32) {
+          uint32_t s0[32], s1[32];
+          tmem_ld32(lane_base + 0 + c0, s0);
+          tmem_ld32(lane_base + 128 + c0, s1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; k++) {
+            const int key = c0 + k;
+            float sc = fmaf(scl[(0 * TNG + 0) * kKeys + key], __uint_as_float(s0[k]),
+                            fmaf(scl[(1 * TNG + 0) * kKeys + key], qs[0], 0.0f));
+            sc = fmaf(scl[(0 * TNG + 1) * kKeys + key], __uint_as_float(s1[k]),
+                      fmaf(scl[(1 * TNG + 1) * kKeys + key], qs[1], sc));
+            const int n = n0 + key;
+            const bool valid = qvalid && n < hi && n >= klo && n <= khi;
+            const float x = valid ? round_dt<BF>(sc) : kNeg;
+            tmax = fmaxf(tmax, x);
+            s0[k] = __float_as_uint(x);
+          }
+          tmem_st32(lane_base + 0 + c0, s0);
+        }
+        tmem_wait_st();
+      }
+      // ---- 3b. lazy rescale: only when a row's maximum grows by more than
+      // 2^8.  The decision is warp-uniform (tcgen05.ld / st are collective);
+      // rows that need none scale by 1.
+      const bool want = tmax > m_used && ((tmax - m_used) * kLog2e > 8.0f || m_used == kNeg);
+      if (!hung && __any_sync(0xffffffffu, want)) {
+        const float alpha = want ? ex2((m_used - tmax) * kLog2e) : 1.0f;
+        lsum *= alpha;
+#pragma unroll
+        for (int g = 0; g < TNG; g++) pbs[g] *= alpha;
+        if (j > 0) {
+#pragma unroll 1
+          for (int c0 = 0; c0 < 2 * TGS; c0 += 32) {
+            uint32_t o[32];
+            tmem_ld32(lane_base + 384 + c0, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 32; k++) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+            tmem_st32(lane_base + 384 + c0, o);
+          }
+          tmem_wait_st();
+        }
+        if (want) m_used = tmax;
+      }
+      // ---- 3c. p, P'_g = fp16(p vs_g) into TMEM, l and sum(p vb_g) ----
+      if (!hung) {
+        const float mls = m_used * kLog2e;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kKeys; c0 += 32) {
+          uint32_t x[32];
+          tmem_ld32(lane_base + 0 + c0, x);
+          tmem_wait_ld();
+          uint32_t pw0[16], pw1[16];
+#pragma unroll
+          for (int k = 0; k < 32; k += 2) {
+            const int key = c0 + k;
+            const float2 arg = __ffma2_rn(make_float2(__uint_as_float(x[k]), __uint_as_float(x[k + 1])),
+                                          make_float2(kLog2e, kLog2e), make_float2(-mls, -mls));
+            // masked keys carry the kNeg sentinel: p = 0 for them, even while
+            // the row's running maximum is still the sentinel itself
+            const float pa = x[k] != __float_as_uint(kNeg) ? ex2(arg.x) : 0.0f;
+            const float pb2 = x[k + 1] != __float_as_uint(kNeg) ? ex2(arg.y) : 0.0f;
+            lsum += pa;
+            lsum += pb2;
+            pbs[0] = fmaf(pb2, scl[(3 * TNG + 0) * kKeys + key + 1], fmaf(pa, scl[(3 * TNG + 0) * kKeys + key], pbs[0]));
+            pbs[1] = fmaf(pb2, scl[(3 * TNG + 1) * kKeys + key + 1], fmaf(pa, scl[(3 * TNG + 1) * kKeys + key], pbs[1]));
+            const float2 q0 = __fmul2_rn(make_float2(pa, pb2),
+                                         make_float2(scl[(2 * TNG + 0) * kKeys + key], scl[(2 * TNG + 0) * kKeys + key + 1]));
+            const float2 q1 = __fmul2_rn(make_float2(pa, pb2),
+                                         make_float2(scl[(2 * TNG + 1) * kKeys + key], scl[(2 * TNG + 1) * kKeys + key + 1]));
+            pw0[k / 2] = pack_h2(q0.x, q0.y);
+            pw1[k / 2] = pack_h2(q1.x, q1.y);
+          }
+          tmem_st16(lane_base + 256 + c0 / 2, pw0);
+          tmem_st16(lane_base + 320 + c0 / 2, pw1);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      tc_fence_after();
+
+      // ---- 4. O_g += P'_g . V_g ----
+      if (tid == 0 && !hung && !*abort_flag) {
+#pragma unroll
+        for (int g = 0; g < TNG; g++)
+#pragma unroll
+          for (int ks = 0; ks < kKeys / 16; ks++)
+            umma_ts(tm + 384 + g * 64, tm + 256 + g * 64 + 8 * ks,
+                    desc_sw128(smem_u32(sm + kVcOff + g * 16384) + 2048 * ks), idesc_pv,
+                    (j > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(pv_bar);
+      }
+      {
+        const bool ok = !hung && !*abort_flag && mbar_wait(pv_bar, (uint32_t)(j & 1));
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (!hung && lane == 0) *abort_flag = 1;
+          hung = true;
+        }
+      }
+      tc_fence_after();
+    }
+
+    // ---- epilogue: out = (2^24 O_g + sum(p vb_g)) / l ----
+    // (TMEM loads in every lane — they are warp-collective; only the stores
+    // depend on the row)
+    {
+      const int64_t orow = ((int64_t)b * p.Hq + kvh * nrep + hh) * L + l;
+      uint16_t* dst = p.out + orow * TD;
+      const bool have_o = !hung && ntiles > 0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < TD; c0 += 32) {
+        uint32_t o[32];
+        if (have_o) {
+          tmem_ld32(lane_base + 384 + c0, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; k++) o[k] = 0u;
+        }
+        const int g = c0 / TGS;
+        uint32_t w[16];
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          const float v0 = lsum > 0.0f ? fmaf(__uint_as_float(o[k]), kCodeUnitInv, pbs[g]) / lsum : 0.0f;
+          const float v1 = lsum > 0.0f ? fmaf(__uint_as_float(o[k + 1]), kCodeUnitInv, pbs[g]) / lsum : 0.0f;
+          w[k / 2] = (uint32_t)f_to_dt<BF>(v0) | ((uint32_t)f_to_dt<BF>(v1) << 16);
+        }
+        if (qvalid) {
+#pragma unroll
+          for (int k = 0; k < 16; k += 4)
+            *reinterpret_cast<uint4*>(dst + c0 + 2 * k) = make_uint4(w[k], w[k + 1], w[k + 2], w[k + 3]);
+        }
+      }
+    }
+  }
+  if (hung && lane == 0) atomicExch(p.err, 1);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(512));
+  }
+}
+
+}  // namespace
+
+bool prefill_tc_supported(int bits, int D, int gs, int L, bool scores) {
+  return bits == 8 && D == TD && gs == TGS && L > 1 && !scores;
+}
+
+int32_t launch_prefill_tc(Params& p, int B, cudaStream_t st) {
+  auto kern = p.bf16 ? prefill_tc_kernel<true> : prefill_tc_kernel<false>;
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[p.bf16]) {
+    KVQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
+    attr_set[p.bf16] = true;
+  }
+  const int qrows = p.nrep * p.L;
+  const dim3 grid((unsigned)((qrows + kRows - 1) / kRows), (unsigned)p.Hkv, (unsigned)B);
+  KVQ_CUDA_TRY(launch_pdl(kern, grid, dim3(160), (size_t)kTcSmem, st, p));
+  return KVQ_OK;
+}
+
+}  // namespace attn
+}  // namespace kvq

@@ -133,6 +133,11 @@ PREFILL_CASES = [
     (2, 8, 4, 900, 40, 128, 64, 8, F16, 256, 0),    # sliding window
     (1, 16, 1, 300, 48, 128, 64, 8, F16, 0, 0),     # GQA 16
     (1, 4, 2, 333, 333, 128, 64, 4, F16, 0, 0),     # full prefill (offset 0)
+    # kv8 / D 128 / group 64 run on the tensor-core (tcgen05) prefill:
+    (1, 32, 8, 1100, 256, 128, 64, 8, BF16, 0, 0),  # bf16 cache
+    (1, 8, 2, 2000, 300, 128, 64, 8, F16, 64, 0),   # window 64: later rows' first tiles all masked
+    (2, 8, 2, 650, 5, 128, 64, 8, F16, 0, 0),       # 20 query rows: one padded 128-row tile
+    (1, 4, 1, 400, 400, 128, 64, 8, F16, 0, 0),     # offset 0, keys end mid-tile
 ]
 
 
