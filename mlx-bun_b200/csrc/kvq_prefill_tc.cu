@@ -7,7 +7,10 @@
 // nrep), so every key tile serves all query heads that share it.  Thread r
 // of the 4 softmax warps owns query row r — the row of TMEM lane r — so the
 // online softmax needs no cross-lane traffic.  A fifth warp streams the key
-// rows in tiles of 128 with 1-D TMA bulk copies (the decode ring).
+// rows in tiles of 128 with 1-D TMA bulk copies (the decode ring).  Two
+// softmax threads share each row (warps w and w + 4 reach the same TMEM
+// lanes), each taking half of every key tile; they exchange the tile
+// maximum and, at the end, their sums through shared memory.
 //
 // Per key tile:
 //   1. the codes become fp16 subnormals (code * 2^-24, exact) in shared
@@ -46,9 +49,12 @@ constexpr int kVcOff = kKcOff + TNG * 16384;    // [TNG] SW128 [128 keys][64] fp
 constexpr int kSclOff = kVcOff + TNG * 16384;   // f32 [4][TNG][128]: ks*2^24, kb, vs, vb
 constexpr int kRawOff = kSclOff + 4 * TNG * kKeys * 4;
 using RawLay = StageLayout<8, TD, TGS, kKeys>;
-constexpr int kBarOff = kRawOff + kTcStages * RawLay::STAGE;  // full[2], empty[2], qk, pv
+constexpr int kXchOff = kRawOff + kTcStages * RawLay::STAGE;  // f32 [2][4][128] row exchange
+constexpr int kBarOff = kXchOff + 2 * 4 * kRows * 4;          // full[2], empty[2], qk, pv
 constexpr int kCtlOff = kBarOff + (2 * kTcStages + 2) * 8;   // tmem base, abort flag
 constexpr int kTcSmem = kCtlOff + 16 + 1024;                  // + alignment slack
+constexpr int kCWarps = 8;                                    // softmax warps: 2 per query row
+constexpr int kCThreads = kCWarps * 32;
 
 // byte offset of element (row, c) of a 128-byte-swizzled tile of 64-element rows
 __device__ __forceinline__ uint32_t sw128(int row, int c) {
@@ -149,7 +155,7 @@ __device__ __forceinline__ uint4 codes8_to_f16(uint32_t w0, uint32_t w1) {
 }
 
 template <bool BF>
-__global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
+__global__ void __launch_bounds__(288, 1) prefill_tc_kernel(const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + kBarOff);
@@ -159,12 +165,13 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sm + kCtlOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + kCtlOff + 4);
   float* scl = reinterpret_cast<float*>(sm + kSclOff);  // [4][TNG][128]
+  float* xch = reinterpret_cast<float*>(sm + kXchOff);  // [2 halves][4][128] row exchange
 
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool producer = warp == 4;
+  const bool producer = warp == kCWarps;
   const int qt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int nrep = p.nrep, L = p.L, qrows = nrep * L;
   const int qr0 = qt * kRows;
@@ -184,7 +191,7 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
   if (tid == 0) {
     for (int s = 0; s < kTcStages; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4);
+      mbar_init(&empty[s], kCWarps);
     }
     mbar_init(qk_bar, 1);
     mbar_init(pv_bar, 1);
@@ -223,8 +230,11 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
       }
     }
   } else {
-    // ---- query row of this thread: q * dtype(scale) rounded to the dtype ----
-    const int r = tid;  // 0..127, TMEM lane r
+    // Two threads per query row: warps w and w + 4 share TMEM lanes 32(w%4)..
+    // and take the first / second half of every key tile (and, at the end,
+    // of the output columns: half kh owns group kh's d).
+    const int kh = warp >> 2;                  // key half
+    const int r = (warp & 3) * 32 + lane;      // query row, TMEM lane
     const int qr = qr0 + r;
     const bool qvalid = qr < qrows;
     const int l = qvalid ? qr / nrep : 0, hh = qvalid ? qr - l * nrep : 0;
@@ -234,13 +244,15 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
       khi = min(khi, pos);
       if (p.window > 0) klo = max(0, pos - p.window + 1);
     }
-    float qs[TNG] = {0.0f, 0.0f};
+    // ---- query row (half kh writes group kh): q * dtype(scale) rounded to the dtype ----
+    float qs[TNG];
     {
       const float scale_dt = round_dt<BF>(p.scale);
       const uint16_t* qrow = p.q + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * TD;
 #pragma unroll
       for (int g = 0; g < TNG; g++) {
         uint8_t* qg = sm + kQOff + g * 16384;
+        float sum = 0.0f;
 #pragma unroll
         for (int c8 = 0; c8 < 8; c8++) {
           uint32_t w[4];
@@ -249,17 +261,20 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
             const int d = g * TGS + c8 * 8 + 2 * j;
             const float a0 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d)) * scale_dt) : 0.0f;
             const float a1 = qvalid ? round_dt<BF>(dt_to_f<BF>(__ldg(qrow + d + 1)) * scale_dt) : 0.0f;
-            qs[g] += a0 + a1;
+            sum += a0 + a1;
             w[j] = pack_h2(a0, a1);
           }
-          *reinterpret_cast<uint4*>(qg + sw128(r, c8 * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+          if (g == kh)
+            *reinterpret_cast<uint4*>(qg + sw128(r, c8 * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
+        qs[g] = sum;
       }
     }
     float m_used = kNeg, lsum = 0.0f, pbs[TNG] = {0.0f, 0.0f};
-    const uint32_t lane_base = tm + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tm + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t idesc_qk = idesc_f16(kRows, kKeys, 0);
     const uint32_t idesc_pv = idesc_f16(kRows, TGS, 1);
+    const int kbeg = kh * (kKeys / 2);  // this thread's keys in a tile: [kbeg, kbeg + 64)
 
     for (int j = 0; j < ntiles; j++) {
       const int s = j % kTcStages;
@@ -275,8 +290,8 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
       if (!hung) {
         const uint8_t* st = sm + kRawOff + s * RawLay::STAGE;
 #pragma unroll 4
-        for (int it = 0; it < (kKeys * TNG * 8) / 128; it++) {
-          const int idx = tid + it * 128;
+        for (int it = 0; it < (kKeys * TNG * 8) / kCThreads; it++) {
+          const int idx = tid + it * kCThreads;
           const int key = idx >> 4, g = (idx >> 3) & 1, c8 = idx & 7;
           const uint2 kw = *reinterpret_cast<const uint2*>(st + RawLay::O_KP + key * TD + g * TGS + c8 * 8);
           const uint2 vw = *reinterpret_cast<const uint2*>(st + RawLay::O_VP + key * TD + g * TGS + c8 * 8);
@@ -285,24 +300,19 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
           *reinterpret_cast<uint4*>(sm + kVcOff + g * 16384 + o) = codes8_to_f16(vw.x, vw.y);
         }
         {
-          // keys past the range hold stale ring bytes: their scales and
-          // biases become 0 so that p = 0 never meets a non-finite value
-          const int key = tid;
+          // thread t: key t & 127, arrays (K scale+bias) or (V scale+bias) by t >> 7;
+          // keys past the range hold stale ring bytes and get 0
+          const int key = tid & (kKeys - 1), which = tid >> 7;
           const bool live = n0 + key < hi;
-          const uint32_t ksw = live ? *reinterpret_cast<const uint32_t*>(st + RawLay::O_KS + key * 4) : 0u;
-          const uint32_t kbw = live ? *reinterpret_cast<const uint32_t*>(st + RawLay::O_KB + key * 4) : 0u;
-          const uint32_t vsw = live ? *reinterpret_cast<const uint32_t*>(st + RawLay::O_VS + key * 4) : 0u;
-          const uint32_t vbw = live ? *reinterpret_cast<const uint32_t*>(st + RawLay::O_VB + key * 4) : 0u;
+          const int oa = which ? RawLay::O_VS : RawLay::O_KS, ob = which ? RawLay::O_VB : RawLay::O_KB;
+          const uint32_t sw = live ? *reinterpret_cast<const uint32_t*>(st + oa + key * 4) : 0u;
+          const uint32_t bw = live ? *reinterpret_cast<const uint32_t*>(st + ob + key * 4) : 0u;
 #pragma unroll
           for (int g = 0; g < TNG; g++) {
-            const auto half_of = [&](uint32_t wv) -> float {
-              const uint16_t h = (uint16_t)(g ? (wv >> 16) : (wv & 0xffffu));
-              return dt_to_f<BF>(h);
-            };
-            scl[(0 * TNG + g) * kKeys + key] = half_of(ksw) * kCodeUnitInv;
-            scl[(1 * TNG + g) * kKeys + key] = half_of(kbw);
-            scl[(2 * TNG + g) * kKeys + key] = half_of(vsw);
-            scl[(3 * TNG + g) * kKeys + key] = half_of(vbw);
+            const float sv = dt_to_f<BF>((uint16_t)(g ? (sw >> 16) : (sw & 0xffffu)));
+            const float bv = dt_to_f<BF>((uint16_t)(g ? (bw >> 16) : (bw & 0xffffu)));
+            scl[((which * 2 + 0) * TNG + g) * kKeys + key] = which ? sv : sv * kCodeUnitInv;
+            scl[((which * 2 + 1) * TNG + g) * kKeys + key] = bv;
           }
         }
       }
@@ -310,7 +320,7 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
       if (lane == 0) mbar_arrive(&empty[s]);  // raw stage free
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(kCThreads) : "memory");
       tc_fence_after();
 
       // ---- 2. S_g = Q_g . C_g^T ----
@@ -333,35 +343,61 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
       }
       tc_fence_after();
 
-      // ---- 3a. logits (rounded, masked) over S_0, tile maximum ----
+      // every key of this thread's half valid for this row (warp-uniform test)?
+      const bool fast = __all_sync(0xffffffffu, qvalid && n0 + kbeg >= klo &&
+                                                    n0 + kbeg + kKeys / 2 - 1 <= khi &&
+                                                    n0 + kbeg + kKeys / 2 <= hi);
+      // ---- 3a. logits (rounded, masked) over S_0, half-tile maximum ----
       float tmax = kNeg;
       if (!hung) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < kKeys; c0 += 32) {
+        for (int c0 = kbeg; c0 < kbeg + kKeys / 2; c0 += 32) {
           uint32_t s0[32], s1[32];
           tmem_ld32(lane_base + 0 + c0, s0);
           tmem_ld32(lane_base + 128 + c0, s1);
           tmem_wait_ld();
 #pragma unroll
-          for (int k = 0; k < 32; k++) {
-            const int key = c0 + k;
-            float sc = fmaf(scl[(0 * TNG + 0) * kKeys + key], __uint_as_float(s0[k]),
-                            fmaf(scl[(1 * TNG + 0) * kKeys + key], qs[0], 0.0f));
-            sc = fmaf(scl[(0 * TNG + 1) * kKeys + key], __uint_as_float(s1[k]),
-                      fmaf(scl[(1 * TNG + 1) * kKeys + key], qs[1], sc));
-            const int n = n0 + key;
-            const bool valid = qvalid && n < hi && n >= klo && n <= khi;
-            const float x = valid ? round_dt<BF>(sc) : kNeg;
-            tmax = fmaxf(tmax, x);
-            s0[k] = __float_as_uint(x);
+          for (int k = 0; k < 32; k += 4) {
+            const float4 ks0 = *reinterpret_cast<const float4*>(scl + (0 * TNG + 0) * kKeys + c0 + k);
+            const float4 ks1 = *reinterpret_cast<const float4*>(scl + (0 * TNG + 1) * kKeys + c0 + k);
+            const float4 kb0 = *reinterpret_cast<const float4*>(scl + (1 * TNG + 0) * kKeys + c0 + k);
+            const float4 kb1 = *reinterpret_cast<const float4*>(scl + (1 * TNG + 1) * kKeys + c0 + k);
+            const float a0[4] = {ks0.x, ks0.y, ks0.z, ks0.w}, a1[4] = {ks1.x, ks1.y, ks1.z, ks1.w};
+            const float b0[4] = {kb0.x, kb0.y, kb0.z, kb0.w}, b1[4] = {kb1.x, kb1.y, kb1.z, kb1.w};
+            float sc[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+              sc[u] = fmaf(a0[u], __uint_as_float(s0[k + u]), fmaf(b0[u], qs[0], 0.0f));
+              sc[u] = fmaf(a1[u], __uint_as_float(s1[k + u]), fmaf(b1[u], qs[1], sc[u]));
+            }
+            float x[4];
+            round_dt2<BF>(sc[0], sc[1], x[0], x[1]);
+            round_dt2<BF>(sc[2], sc[3], x[2], x[3]);
+            if (!fast) {
+#pragma unroll
+              for (int u = 0; u < 4; u++) {
+                const int n = n0 + c0 + k + u;
+                x[u] = (qvalid && n < hi && n >= klo && n <= khi) ? x[u] : kNeg;
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+              tmax = fmaxf(tmax, x[u]);
+              s0[k + u] = __float_as_uint(x[u]);
+            }
           }
           tmem_st32(lane_base + 0 + c0, s0);
         }
         tmem_wait_st();
       }
+      // row maximum of the tile from both halves
+      xch[(kh * 4 + 0) * kKeys + r] = tmax;
+      asm volatile("bar.sync 1, %0;" ::"r"(kCThreads) : "memory");
+      tmax = fmaxf(xch[(0 * 4 + 0) * kKeys + r], xch[(1 * 4 + 0) * kKeys + r]);
+
       // ---- 3b. lazy rescale: only when a row's maximum grows by more than
       // 2^8.  The decision is warp-uniform (tcgen05.ld / st are collective);
-      // rows that need none scale by 1.
+      // rows that need none scale by 1.  Half kh rescales group kh's O.
       const bool want = tmax > m_used && ((tmax - m_used) * kLog2e > 8.0f || m_used == kNeg);
       if (!hung && __any_sync(0xffffffffu, want)) {
         const float alpha = want ? ex2((m_used - tmax) * kLog2e) : 1.0f;
@@ -370,13 +406,13 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
         for (int g = 0; g < TNG; g++) pbs[g] *= alpha;
         if (j > 0) {
 #pragma unroll 1
-          for (int c0 = 0; c0 < 2 * TGS; c0 += 32) {
+          for (int c0 = 0; c0 < TGS; c0 += 32) {
             uint32_t o[32];
-            tmem_ld32(lane_base + 384 + c0, o);
+            tmem_ld32(lane_base + 384 + kh * TGS + c0, o);
             tmem_wait_ld();
 #pragma unroll
             for (int k = 0; k < 32; k++) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-            tmem_st32(lane_base + 384 + c0, o);
+            tmem_st32(lane_base + 384 + kh * TGS + c0, o);
           }
           tmem_wait_st();
         }
@@ -386,38 +422,52 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
       if (!hung) {
         const float mls = m_used * kLog2e;
 #pragma unroll 1
-        for (int c0 = 0; c0 < kKeys; c0 += 32) {
+        for (int c0 = kbeg; c0 < kbeg + kKeys / 2; c0 += 32) {
           uint32_t x[32];
           tmem_ld32(lane_base + 0 + c0, x);
           tmem_wait_ld();
           uint32_t pw0[16], pw1[16];
+          float2 ls2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            const int key = c0 + k;
-            const float2 arg = __ffma2_rn(make_float2(__uint_as_float(x[k]), __uint_as_float(x[k + 1])),
-                                          make_float2(kLog2e, kLog2e), make_float2(-mls, -mls));
-            // masked keys carry the kNeg sentinel: p = 0 for them, even while
-            // the row's running maximum is still the sentinel itself
-            const float pa = x[k] != __float_as_uint(kNeg) ? ex2(arg.x) : 0.0f;
-            const float pb2 = x[k + 1] != __float_as_uint(kNeg) ? ex2(arg.y) : 0.0f;
-            lsum += pa;
-            lsum += pb2;
-            pbs[0] = fmaf(pb2, scl[(3 * TNG + 0) * kKeys + key + 1], fmaf(pa, scl[(3 * TNG + 0) * kKeys + key], pbs[0]));
-            pbs[1] = fmaf(pb2, scl[(3 * TNG + 1) * kKeys + key + 1], fmaf(pa, scl[(3 * TNG + 1) * kKeys + key], pbs[1]));
-            const float2 q0 = __fmul2_rn(make_float2(pa, pb2),
-                                         make_float2(scl[(2 * TNG + 0) * kKeys + key], scl[(2 * TNG + 0) * kKeys + key + 1]));
-            const float2 q1 = __fmul2_rn(make_float2(pa, pb2),
-                                         make_float2(scl[(2 * TNG + 1) * kKeys + key], scl[(2 * TNG + 1) * kKeys + key + 1]));
-            pw0[k / 2] = pack_h2(q0.x, q0.y);
-            pw1[k / 2] = pack_h2(q1.x, q1.y);
+          for (int k = 0; k < 32; k += 4) {
+            const float4 vs0 = *reinterpret_cast<const float4*>(scl + (2 * TNG + 0) * kKeys + c0 + k);
+            const float4 vs1 = *reinterpret_cast<const float4*>(scl + (2 * TNG + 1) * kKeys + c0 + k);
+            const float4 vb0 = *reinterpret_cast<const float4*>(scl + (3 * TNG + 0) * kKeys + c0 + k);
+            const float4 vb1 = *reinterpret_cast<const float4*>(scl + (3 * TNG + 1) * kKeys + c0 + k);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; h2++) {
+              const int kk = k + 2 * h2;
+              const float2 arg = __ffma2_rn(
+                  make_float2(__uint_as_float(x[kk]), __uint_as_float(x[kk + 1])),
+                  make_float2(kLog2e, kLog2e), make_float2(-mls, -mls));
+              float2 pv = make_float2(ex2(arg.x), ex2(arg.y));
+              if (!fast) {
+                // masked keys carry the kNeg sentinel: p = 0 for them, even
+                // while the row's running maximum is still the sentinel
+                pv.x = x[kk] != __float_as_uint(kNeg) ? pv.x : 0.0f;
+                pv.y = x[kk + 1] != __float_as_uint(kNeg) ? pv.y : 0.0f;
+              }
+              ls2 = __fadd2_rn(ls2, pv);
+              const float2 vsa = h2 ? make_float2(vs0.z, vs0.w) : make_float2(vs0.x, vs0.y);
+              const float2 vsb = h2 ? make_float2(vs1.z, vs1.w) : make_float2(vs1.x, vs1.y);
+              const float2 vba = h2 ? make_float2(vb0.z, vb0.w) : make_float2(vb0.x, vb0.y);
+              const float2 vbb = h2 ? make_float2(vb1.z, vb1.w) : make_float2(vb1.x, vb1.y);
+              pbs[0] = fmaf(pv.y, vba.y, fmaf(pv.x, vba.x, pbs[0]));
+              pbs[1] = fmaf(pv.y, vbb.y, fmaf(pv.x, vbb.x, pbs[1]));
+              const float2 q0 = __fmul2_rn(pv, vsa);
+              const float2 q1 = __fmul2_rn(pv, vsb);
+              pw0[kk / 2] = pack_h2(q0.x, q0.y);
+              pw1[kk / 2] = pack_h2(q1.x, q1.y);
+            }
           }
+          lsum += ls2.x + ls2.y;
           tmem_st16(lane_base + 256 + c0 / 2, pw0);
           tmem_st16(lane_base + 320 + c0 / 2, pw1);
         }
         tmem_wait_st();
       }
       tc_fence_before();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(kCThreads) : "memory");
       tc_fence_after();
 
       // ---- 4. O_g += P'_g . V_g ----
@@ -441,29 +491,32 @@ __global__ void __launch_bounds__(160, 1) prefill_tc_kernel(const Params p) {
       tc_fence_after();
     }
 
-    // ---- epilogue: out = (2^24 O_g + sum(p vb_g)) / l ----
-    // (TMEM loads in every lane — they are warp-collective; only the stores
-    // depend on the row)
+    // ---- epilogue: out = (2^24 O_g + sum(p vb_g)) / l, half kh writes group kh ----
+    xch[(kh * 4 + 1) * kKeys + r] = lsum;
+    xch[(kh * 4 + 2) * kKeys + r] = pbs[0];
+    xch[(kh * 4 + 3) * kKeys + r] = pbs[1];
+    asm volatile("bar.sync 1, %0;" ::"r"(kCThreads) : "memory");
+    const float lt = xch[(0 * 4 + 1) * kKeys + r] + xch[(1 * 4 + 1) * kKeys + r];
+    const float pbt = xch[(0 * 4 + 2 + kh) * kKeys + r] + xch[(1 * 4 + 2 + kh) * kKeys + r];
     {
       const int64_t orow = ((int64_t)b * p.Hq + kvh * nrep + hh) * L + l;
-      uint16_t* dst = p.out + orow * TD;
-      const bool have_o = !hung && ntiles > 0;
+      uint16_t* dst = p.out + orow * TD + kh * TGS;
+      const bool have_o = !hung && ntiles > 0;  // warp-uniform: TMEM loads are collective
 #pragma unroll 1
-      for (int c0 = 0; c0 < TD; c0 += 32) {
+      for (int c0 = 0; c0 < TGS; c0 += 32) {
         uint32_t o[32];
         if (have_o) {
-          tmem_ld32(lane_base + 384 + c0, o);
+          tmem_ld32(lane_base + 384 + kh * TGS + c0, o);
           tmem_wait_ld();
         } else {
 #pragma unroll
           for (int k = 0; k < 32; k++) o[k] = 0u;
         }
-        const int g = c0 / TGS;
         uint32_t w[16];
 #pragma unroll
         for (int k = 0; k < 32; k += 2) {
-          const float v0 = lsum > 0.0f ? fmaf(__uint_as_float(o[k]), kCodeUnitInv, pbs[g]) / lsum : 0.0f;
-          const float v1 = lsum > 0.0f ? fmaf(__uint_as_float(o[k + 1]), kCodeUnitInv, pbs[g]) / lsum : 0.0f;
+          const float v0 = lt > 0.0f ? fmaf(__uint_as_float(o[k]), kCodeUnitInv, pbt) / lt : 0.0f;
+          const float v1 = lt > 0.0f ? fmaf(__uint_as_float(o[k + 1]), kCodeUnitInv, pbt) / lt : 0.0f;
           w[k / 2] = (uint32_t)f_to_dt<BF>(v0) | ((uint32_t)f_to_dt<BF>(v1) << 16);
         }
         if (qvalid) {
@@ -498,7 +551,7 @@ int32_t launch_prefill_tc(Params& p, int B, cudaStream_t st) {
   }
   const int qrows = p.nrep * p.L;
   const dim3 grid((unsigned)((qrows + kRows - 1) / kRows), (unsigned)p.Hkv, (unsigned)B);
-  KVQ_CUDA_TRY(launch_pdl(kern, grid, dim3(160), (size_t)kTcSmem, st, p));
+  KVQ_CUDA_TRY(launch_pdl(kern, grid, dim3(kCThreads + 32), (size_t)kTcSmem, st, p));
   return KVQ_OK;
 }
 
