@@ -61,6 +61,10 @@ namespace attn {
 
 constexpr float kNeg = -1.0e30f;             // finite "minus infinity" for masked logits
 constexpr float kLog2e = 1.4426950408889634f;
+// Lazy rescale: a column's running max moves only when a logit exceeds it
+// by more than 4 ln 2, so p <= 16 between updates (p * scale stays far from
+// the f16 limit) and most slices skip the reduction and the rescale.
+constexpr float kLazyLogit = 2.7725887222397811f;
 constexpr int kTile = 16;                     // rows per MMA tile; row-alignment unit
 constexpr long long kWaitLimit = 1ll << 30;   // mbarrier polls before declaring a hang
 constexpr uint64_t kWaitNs = 2000000000ull;   // ... or 2 s of %globaltimer, whichever first
@@ -348,8 +352,19 @@ struct Smem {
       STAGES_OFF + (STAGE_BYTES > MERGE_BYTES ? STAGE_BYTES : MERGE_BYTES);
 };
 
+// Query fragments of one lane group in shared memory: lane l's words at
+// uint4 index k*32 + l (conflict-free 16-byte stores and loads).
+template <int BITS, int D, int GS, int NT>
+struct QFragSlot {
+  using G = Geo<BITS, D, GS>;
+  static constexpr int NQ = G::KSTEPS * NT * 2;  // qbf words
+  static constexpr int NS = NT * G::NG * 2;      // qs_r floats
+  static constexpr int W4 = (NQ + NS + 3) / 4;   // uint4 per lane
+  static constexpr int BYTES = 32 * W4 * 16;
+};
+
 // Shared memory of the balanced kernel: barriers, the per-entry tile table
-// (ragged batches) and the ring.
+// (ragged batches), query slots, one query-fragment slot and the ring.
 constexpr int kBalMaxBatch = 256;  // ragged batches up to this size use the balanced kernel
 template <int BITS, int D, int GS, int NT, int W, int RW, int STAGES>
 struct BalSmem {
@@ -363,7 +378,8 @@ struct BalSmem {
   static constexpr int BL = BS + (kBalMaxBatch + 1) * 8;        // int [B] key rows of each entry
   static constexpr int QSLOT = HQ * D * 2;                      // one group's query rows (dtype)
   static constexpr int QS = (BL + kBalMaxBatch * 4 + 127) / 128 * 128;  // [STAGES] query slots
-  static constexpr int STAGES_OFF = QS + STAGES * QSLOT;
+  static constexpr int QF = QS + STAGES * QSLOT;                // second segment's fragments
+  static constexpr int STAGES_OFF = (QF + QFragSlot<BITS, D, GS, NT>::BYTES + 127) / 128 * 128;
   static constexpr int TOTAL = STAGES_OFF + STAGES * STAGE;
 };
 
@@ -401,19 +417,42 @@ struct QFrag {
   float qs_r[NT][G::NG][2];
 };
 
-// Lane (g, t) holds q * dtype(scale) (rounded to dtype, like mulScalar) of
-// query row qr0 + nt*8 + g at the d positions its K fragments pair with,
-// read straight from global memory; sum(q) per group comes from the 4 lanes
-// t of the row, then moves to the lanes that own each column of the score tile.
-// qs: the group's query rows already in shared memory ([nrep][D], L = 1),
-// or nullptr to read them from global memory.
-template <int BITS, int D, int GS, int NT, bool BF>
-__device__ __forceinline__ void load_qfrag(QFrag<BITS, D, GS, NT>& f, const Params& p, int b,
-                                           int kvh, int qr0, int qrows, int g, int t,
-                                           const uint16_t* qs = nullptr) {
+// d positions of the query halves that fragment word (kk, w2) of lane t
+// pairs with the K codes, and the factor folded into them (1/16 for the
+// odd nibbles of 4-bit codes, which the K fragments take as 16c).
+template <int BITS, int GS>
+__device__ __forceinline__ void q_positions(int kk, int w2, int t, int mtg, int& d_lo, int& d_hi,
+                                            float& fac) {
+  const int grp = kk / mtg, kin = kk % mtg, v = 2 * kin + w2;
+  fac = 1.0f;
+  if (BITS == 4) {
+    const int wi = v / 4, x = v % 4;
+    const int base = grp * GS + t * (GS / 4) + 8 * wi;
+    d_lo = base + x;
+    d_hi = base + x + 4;
+    if (x & 1) fac = 0.0625f;
+  } else {
+    const int wi = v / 2, x = v % 2;
+    const int base = grp * GS + t * (GS / 4) + 4 * wi;
+    d_lo = base + 2 * x;
+    d_hi = base + 2 * x + 1;
+  }
+}
+
+// A lane's raw query halves (dtype bits, lo | hi << 16 per fragment word),
+// zero for rows past qrows.  qs: the group's query rows in shared memory
+// ([nrep][D], L = 1), or nullptr to read them from global memory.
+template <int BITS, int D, int GS, int NT>
+struct QRaw {
+  uint32_t w[NT][Geo<BITS, D, GS>::KSTEPS][2];
+};
+
+template <int BITS, int D, int GS, int NT>
+__device__ __forceinline__ void load_qraw(QRaw<BITS, D, GS, NT>& r, const Params& p, int b,
+                                          int kvh, int qr0, int qrows, int g, int t,
+                                          const uint16_t* qs = nullptr) {
   using G = Geo<BITS, D, GS>;
   const int nrep = p.nrep, L = p.L;
-  const float scale_dt = round_dt<BF>(p.scale);
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
     const int qr = qr0 + nt * 8 + g;
@@ -421,37 +460,49 @@ __device__ __forceinline__ void load_qfrag(QFrag<BITS, D, GS, NT>& f, const Para
     const int l = qvalid ? qr / nrep : 0, hh = qvalid ? qr - l * nrep : 0;
     const uint16_t* qrow =
         qs ? qs + hh * D : p.q + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * D;
+#pragma unroll
+    for (int kk = 0; kk < G::KSTEPS; kk++)
+#pragma unroll
+      for (int w2 = 0; w2 < 2; w2++) {
+        int d_lo, d_hi;
+        float fac;
+        q_positions<BITS, GS>(kk, w2, t, G::MTG, d_lo, d_hi, fac);
+        const uint32_t h0 = qvalid ? (qs ? qrow[d_lo] : __ldg(qrow + d_lo)) : 0u;
+        const uint32_t h1 = qvalid ? (qs ? qrow[d_hi] : __ldg(qrow + d_hi)) : 0u;
+        r.w[nt][kk][w2] = h0 | (h1 << 16);
+      }
+  }
+}
+
+// Lane (g, t) holds q * dtype(scale) (rounded to dtype, like mulScalar) of
+// query row qr0 + nt*8 + g at the d positions its K fragments pair with;
+// sum(q) per group comes from the 4 lanes t of the row, then moves to the
+// lanes that own each column of the score tile.
+template <int BITS, int D, int GS, int NT, bool BF>
+__device__ __forceinline__ void qfrag_from_raw(QFrag<BITS, D, GS, NT>& f,
+                                               const QRaw<BITS, D, GS, NT>& r, const Params& p,
+                                               int t) {
+  using G = Geo<BITS, D, GS>;
+  const float scale_dt = round_dt<BF>(p.scale);
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
     float gsum[G::NG];
 #pragma unroll
     for (int grp = 0; grp < G::NG; grp++) gsum[grp] = 0.0f;
 #pragma unroll
-    for (int kk = 0; kk < G::KSTEPS; kk++) {
-      const int grp = kk / G::MTG, kin = kk % G::MTG;
+    for (int kk = 0; kk < G::KSTEPS; kk++)
 #pragma unroll
       for (int w2 = 0; w2 < 2; w2++) {
-        const int v = 2 * kin + w2;
         int d_lo, d_hi;
-        float fac = 1.0f;
-        if (BITS == 4) {
-          const int wi = v / 4, x = v % 4;
-          const int base = grp * GS + t * (GS / 4) + 8 * wi;
-          d_lo = base + x;
-          d_hi = base + x + 4;
-          if (x & 1) fac = 0.0625f;
-        } else {
-          const int wi = v / 2, x = v % 2;
-          const int base = grp * GS + t * (GS / 4) + 4 * wi;
-          d_lo = base + 2 * x;
-          d_hi = base + 2 * x + 1;
-        }
-        const uint16_t h0 = qvalid ? (qs ? qrow[d_lo] : __ldg(qrow + d_lo)) : 0;
-        const uint16_t h1 = qvalid ? (qs ? qrow[d_hi] : __ldg(qrow + d_hi)) : 0;
-        const float a0 = qvalid ? round_dt<BF>(dt_to_f<BF>(h0) * scale_dt) : 0.0f;
-        const float a1 = qvalid ? round_dt<BF>(dt_to_f<BF>(h1) * scale_dt) : 0.0f;
-        gsum[grp] += a0 + a1;
+        float fac;
+        q_positions<BITS, GS>(kk, w2, t, G::MTG, d_lo, d_hi, fac);
+        const uint32_t hw = r.w[nt][kk][w2];
+        // zero halves (rows past qrows) stay zero
+        const float a0 = round_dt<BF>(dt_to_f<BF>((uint16_t)(hw & 0xffffu)) * scale_dt);
+        const float a1 = round_dt<BF>(dt_to_f<BF>((uint16_t)(hw >> 16)) * scale_dt);
+        gsum[kk / G::MTG] += a0 + a1;
         f.qbf[kk][nt][w2] = pack_h2(a0 * fac, a1 * fac);
       }
-    }
 #pragma unroll
     for (int grp = 0; grp < G::NG; grp++) {
       float v = gsum[grp];
@@ -462,6 +513,52 @@ __device__ __forceinline__ void load_qfrag(QFrag<BITS, D, GS, NT>& f, const Para
       f.qs_r[nt][grp][1] = __shfl_sync(0xffffffffu, v, (2 * t + 1) << 2);
     }
   }
+}
+
+template <int BITS, int D, int GS, int NT, bool BF>
+__device__ __forceinline__ void load_qfrag(QFrag<BITS, D, GS, NT>& f, const Params& p, int b,
+                                           int kvh, int qr0, int qrows, int g, int t,
+                                           const uint16_t* qs = nullptr) {
+  QRaw<BITS, D, GS, NT> r;
+  load_qraw<BITS, D, GS, NT>(r, p, b, kvh, qr0, qrows, g, t, qs);
+  qfrag_from_raw<BITS, D, GS, NT, BF>(f, r, p, t);
+}
+
+template <int BITS, int D, int GS, int NT>
+__device__ __forceinline__ void store_qfrag(const QFrag<BITS, D, GS, NT>& f, uint8_t* slot,
+                                            int lane) {
+  using QS = QFragSlot<BITS, D, GS, NT>;
+  uint32_t w[QS::W4 * 4];
+  const uint32_t* qb = &f.qbf[0][0][0];
+  const float* qs = &f.qs_r[0][0][0];
+#pragma unroll
+  for (int k = 0; k < QS::W4 * 4; k++)
+    w[k] = k < QS::NQ ? qb[k] : (k < QS::NQ + QS::NS ? __float_as_uint(qs[k - QS::NQ]) : 0u);
+#pragma unroll
+  for (int k = 0; k < QS::W4; k++)
+    *reinterpret_cast<uint4*>(slot + (k * 32 + lane) * 16) =
+        make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+}
+
+template <int BITS, int D, int GS, int NT>
+__device__ __forceinline__ void load_qfrag_slot(QFrag<BITS, D, GS, NT>& f, const uint8_t* slot,
+                                                int lane) {
+  using QS = QFragSlot<BITS, D, GS, NT>;
+  uint32_t w[QS::W4 * 4];
+#pragma unroll
+  for (int k = 0; k < QS::W4; k++) {
+    const uint4 v = *reinterpret_cast<const uint4*>(slot + (k * 32 + lane) * 16);
+    w[4 * k] = v.x;
+    w[4 * k + 1] = v.y;
+    w[4 * k + 2] = v.z;
+    w[4 * k + 3] = v.w;
+  }
+  uint32_t* qb = &f.qbf[0][0][0];
+  float* qs = &f.qs_r[0][0][0];
+#pragma unroll
+  for (int k = 0; k < QS::NQ; k++) qb[k] = w[k];
+#pragma unroll
+  for (int k = 0; k < QS::NS; k++) qs[k] = __uint_as_float(w[QS::NQ + k]);
 }
 
 // Key-index limits (inclusive) of this lane's query columns.
@@ -611,7 +708,7 @@ __device__ __forceinline__ void process_slice(WarpAcc<BITS, D, GS, NT>& A,
               }
             }
           }
-          above |= x[nt][hh][mt][e] > m_run[nt][hh];
+          above |= x[nt][hh][mt][e] > m_run[nt][hh] + kLazyLogit;
         }
   const bool rescale_all = __any_sync(0xffffffffu, above);
   if (rescale_all) {
@@ -1265,6 +1362,7 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BARS);
   uint64_t* empty = full + STAGES;
   volatile int* ctrl = reinterpret_cast<volatile int*>(smem + S::CTRL);  // [1] abort
+  uint64_t* qfb = reinterpret_cast<uint64_t*>(smem + S::CTRL + 8);  // second segment's fragments built
   uint8_t* stages = smem + S::STAGES_OFF;
   int* blen = reinterpret_cast<int*>(smem + S::BL);             // [B] key rows of each entry
   int64_t* bfirst = reinterpret_cast<int64_t*>(smem + S::BS);   // [B+1] first tile of each entry
@@ -1283,6 +1381,7 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], W);
     }
+    mbar_init(qfb, 32);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     ctrl[1] = 0;
   }
@@ -1344,41 +1443,71 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
 
   bool hung = false;
   if (producer) {
-    if (lane == 0) {
-      int c = 0;
-      for (int64_t x = x0; x < x1 && !hung;) {
-        int b, kvh, T, n;
-        int64_t U;
-        unit_at(x, b, kvh, U, T, n);
-        const int64_t xe = x1 < U + T ? x1 : U + T;
-        const int r0 = (int)(x - U) * kTile, r1 = (int)(xe - U) * kTile;
-        const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
-        const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
-        const uint16_t* qsrc = p.q + ((int64_t)b * p.Hq + (int64_t)kvh * nrep) * D;
-        for (int row = r0; row < r1; row += CH, c++) {
-          const int s = c % STAGES;
-          // Staggered start: the rest of the ring is requested once the first
-          // chunk has landed, so every CTA's first chunk (and its math) comes
-          // ahead of the bulk of the initial fill.
-          if ((c == 1 && !mbar_wait(&full[0], 0u)) ||
-              (c >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1)))) {
-            hung = true;
-            ctrl[1] = 1;
-            break;
-          }
+    // The whole warp walks the chunks (lane 0 issues the copies); after the
+    // first chunk it loads the second segment's query halves, and once the
+    // ring is first filled it turns them into fragments for the consumers.
+    QRaw<BITS, D, GS, NT> qr1;
+    bool q1 = false;  // raw halves of segment 1 loaded, fragments not yet built
+    int c = 0, j = 0;
+    for (int64_t x = x0; x < x1 && !hung; j++) {
+      int b, kvh, T, n;
+      int64_t U;
+      unit_at(x, b, kvh, U, T, n);
+      const int64_t xe = x1 < U + T ? x1 : U + T;
+      const int r0 = (int)(x - U) * kTile, r1 = (int)(xe - U) * kTile;
+      const int64_t kbase = (int64_t)b * p.k_bstride + (int64_t)kvh * p.k_hstride;
+      const int64_t vbase = (int64_t)b * p.v_bstride + (int64_t)kvh * p.v_hstride;
+      const uint16_t* qsrc = p.q + ((int64_t)b * p.Hq + (int64_t)kvh * nrep) * D;
+      for (int row = r0; row < r1; row += CH, c++) {
+        const int s = c % STAGES;
+        // Staggered start: the rest of the ring is requested once the first
+        // chunk has landed, so every CTA's first chunk (and its math) comes
+        // ahead of the bulk of the initial fill.
+        bool ok = !ctrl[1];
+        if (ok && c == 1) ok = mbar_wait(&full[0], 0u);
+        if (ok && c >= STAGES) ok = mbar_wait(&empty[s], (uint32_t)(((c / STAGES) & 1) ^ 1));
+        if (!__all_sync(0xffffffffu, ok)) {
+          hung = true;
+          if (lane == 0) ctrl[1] = 1;
+          break;
+        }
+        if (lane == 0)
           issue_chunk<BITS, D, GS, CH>(p, stages + s * S::STAGE, &full[s], kbase, vbase, row,
                                        (uint32_t)min(CH, r1 - row),
-                                       row == r0 ? smem + S::QS + s * S::QSLOT : nullptr, qsrc,
-                                       (uint32_t)(nrep * D * 2));
+                                       row == r0 && j >= 2 ? smem + S::QS + s * S::QSLOT : nullptr,
+                                       qsrc, (uint32_t)(nrep * D * 2));
+        if (c == 0 && xe < x1) {
+          int b1, kvh1, T1, n1;
+          int64_t U1;
+          unit_at(xe, b1, kvh1, U1, T1, n1);
+          load_qraw<BITS, D, GS, NT>(qr1, p, b1, kvh1, 0, qrows, g, t);
+          q1 = true;
         }
-        x = xe;
+        if (q1 && c == STAGES - 1) {
+          QFrag<BITS, D, GS, NT> Q1;
+          qfrag_from_raw<BITS, D, GS, NT, BF>(Q1, qr1, p, t);
+          store_qfrag<BITS, D, GS, NT>(Q1, smem + S::QF, lane);
+          mbar_arrive(qfb);  // every lane, after its own stores
+          q1 = false;
+        }
       }
+      x = xe;
+    }
+    if (q1 && !hung) {  // fewer chunks than ring stages
+      QFrag<BITS, D, GS, NT> Q1;
+      qfrag_from_raw<BITS, D, GS, NT, BF>(Q1, qr1, p, t);
+      store_qfrag<BITS, D, GS, NT>(Q1, smem + S::QF, lane);
+      mbar_arrive(qfb);
     }
   } else {
     WarpAcc<BITS, D, GS, NT> A;
     QFrag<BITS, D, GS, NT> Q;
-    int c = 0;
-    for (int64_t x = x0; x < x1;) {
+    // Query groups: the first segment's straight from global memory into
+    // every warp's registers, while the ring's first chunk is in flight;
+    // the second's built by the producer warp into shared memory; later
+    // segments' carried by their first chunk.
+    int c = 0, j = 0;
+    for (int64_t x = x0; x < x1; j++) {
       int b, kvh, T, n;
       int64_t U;
       unit_at(x, b, kvh, U, T, n);
@@ -1388,6 +1517,16 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
       int klo[NT][2], khi[NT][2];
       column_bounds<NT>(klo, khi, p, 0, qrows, n, t);
       A.reset();
+      if (j == 0) {
+        load_qfrag<BITS, D, GS, NT, BF>(Q, p, b, kvh, 0, qrows, g, t);
+      } else if (j == 1) {
+        const bool ok = !hung && !ctrl[1] && mbar_wait(qfb, 0u);
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (!hung && lane == 0) ctrl[1] = 1;
+          hung = true;
+        }
+        load_qfrag_slot<BITS, D, GS, NT>(Q, smem + S::QF, lane);
+      }
       for (int row = r0; row < r1; row += CH, c++) {
         const int s = c % STAGES;
         // Warp-uniform decision: the slice is full of warp-collective ops.
@@ -1398,7 +1537,7 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
           hung = true;
           continue;
         }
-        if (row == r0)  // the segment's query group came with its first chunk
+        if (row == r0 && j >= 2)  // a later segment's query group came with its first chunk
           load_qfrag<BITS, D, GS, NT, BF>(Q, p, b, kvh, 0, qrows, g, t,
                                           reinterpret_cast<const uint16_t*>(smem + S::QS +
                                                                             s * S::QSLOT));
