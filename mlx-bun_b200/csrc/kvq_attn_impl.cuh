@@ -1074,8 +1074,8 @@ __device__ __forceinline__ void merge_slots(const Params& p, int64_t slot0, int 
 
 // Issue the six bulk copies of `rows` (a multiple of 16) key rows starting
 // at row `row` of the (b, h) pair whose first rows are kbase / vbase.
-// With q_dst, also copy q_bytes of query rows from q_src (a segment's
-// first chunk carries its query group).
+// With q_dst, also copy q_bytes of query rows from q_src (the first chunk
+// of a segment after the second carries its query group).
 template <int BITS, int D, int GS, int CH>
 __device__ __forceinline__ void issue_chunk(const Params& p, uint8_t* st, uint64_t* bar,
                                             int64_t kbase, int64_t vbase, int64_t row,
