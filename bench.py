@@ -467,6 +467,210 @@ def run_prefill(args):
         "gpu_launches": 2 * reps * NL}))
 
 
+# ------------------------------------------------------ other configs --
+#
+# Secondary measurement lines for the other BASELINE configs (one JSON line
+# each, not read by the driver): config 1 (one small decode step, many
+# distinct layers so the working set exceeds L2), config 3 (Gemma-style
+# rotating window: 5 window layers + 1 global layer per step, append and
+# decode), config 5 (ragged batch of 64 sequences decoded with seq_lens, kv
+# heads sharded over ranks with no communication) and config 5's single
+# 131,072-token sequence split along the context (partials all-gathered over
+# NCCL and merged).  Synthetic seeded data of the named shapes.
+
+CONFIG_DESC = {
+    "config1": "single decode step: B1 Hq16 Hkv4 D128 N2048 kv8 gs64, 64 distinct layers cycled",
+    "config3": "Gemma-style window: B4 Hq8 Hkv4 D256 kv8 gs64; per step 5 rotating layers (window "
+               "1024, 4096 tokens written) + 1 global layer (4096), append + decode each",
+    "config5": "ragged serving: B64 lengths U[1024, 32768] (seed 5), Hq32 Hkv8 D128 kv4 gs64, "
+               "decode with seq_lens; kv heads sharded over ranks, no collective",
+    "config5-ctx": "one 131072-token sequence, Hq32 Hkv8 D128 kv4 gs64, context split over ranks; "
+                   "(m, l, o) partials all-gathered over NCCL and merged",
+}
+
+
+def _fill_cache(cache, B, H, N, D, g, device, chunk):
+    """Append N seeded rows (fp16) to `cache` in chunks; returns the last views."""
+    import torch
+    views = None
+    for s0 in range(0, N, chunk):
+        S = min(chunk, N - s0)
+        k = torch.randn(B, H, S, D, generator=g, device=device).half()
+        v = torch.randn(B, H, S, D, generator=g, device=device).half()
+        views = cache.update_and_fetch_quantized(k, v)
+        del k, v
+    return views
+
+
+def run_config(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import kvq
+    from kvq.parallel import ContextSplitDecode, context_ranges
+
+    w = args.workload
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device)
+    g.manual_seed(3000 + rank)
+    steps, keep = [], []
+    nbytes = 0  # algorithmic bytes of this rank per pass over `steps`
+    dt = "u8 codes/f16"
+    scaling = "weak"
+    graph_ok = True
+    if w == "config1":
+        B, Hq, Hkv, D, N, bits, gs = 1, 16, 4, 128, 2048, 8, 64
+        rb = 2 * (D * bits // 8 + 2 * (D // gs) * 2)
+        scale = 1.0 / np.sqrt(D)
+        for _ in range(64):
+            cache = kvq.QuantizedKVCache(gs, bits)
+            kq, vq = _fill_cache(cache, B, Hkv, N, D, g, device, N)
+            q = torch.randn(B, Hq, 1, D, generator=g, device=device).half()
+            out = torch.empty_like(q)
+            keep.append((cache, kq, vq, q, out))
+            steps.append(lambda kq=kq, vq=vq, q=q, out=out:
+                         kvq.sdpa_decode(q, kq, vq, scale, out=out))
+            nbytes += B * Hkv * N * rb + 2 * B * Hq * D * 2
+    elif w == "config3":
+        B, Hq, Hkv, D, bits, gs, win = 4, 8, 4, 256, 8, 64, 1024
+        rb = 2 * (D * bits // 8 + 2 * (D // gs) * 2)
+        scale = 1.0 / 16.0
+        for _ in range(3):  # 3 x (5 + 1) layers: 241 MB cycled, above L2
+            for li in range(6):
+                local = li < 5
+                cache = kvq.RotatingQuantizedKVCache(win, gs, bits) if local else \
+                    kvq.QuantizedKVCache(gs, bits, reserve_rows=4352)
+                _fill_cache(cache, B, Hkv, 4096, D, g, device, win)
+                kn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
+                vn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
+                q = torch.randn(B, Hq, 1, D, generator=g, device=device).half()
+                out = torch.empty_like(q)
+                kq, vq = cache.update_and_fetch_quantized(kn, vn)  # steady-state length
+                n = kq.shape[2]
+                if not local:
+                    cache.trim(1)
+                keep.append((cache, kn, vn, q, out))
+
+                def st(cache=cache, kn=kn, vn=vn, q=q, out=out, local=local):
+                    k2, v2 = cache.update_and_fetch_quantized(kn, vn)
+                    kvq.sdpa_decode(q, k2, v2, scale, out=out)
+                    if not local:
+                        cache.trim(1)  # host bookkeeping: every replay the same work
+                steps.append(st)
+                nbytes += B * Hkv * n * rb + 2 * B * Hq * D * 2 + B * Hkv * D * 2 * 2
+    elif w == "config5":
+        B, Hq, Hkv, D, bits, gs = 64, 32, 8, 128, 4, 64
+        if Hkv % world:
+            raise SystemExit("config5 shards 8 kv heads: use 1, 2, 4 or 8 GPUs")
+        rb = 2 * (D * bits // 8 + 2 * (D // gs) * 2)
+        scale = 1.0 / np.sqrt(D)
+        lens = np.random.default_rng(5).integers(1024, 32769, size=B)
+        hk = Hkv // world
+        Nmax = int(lens.max())
+        cache = kvq.QuantizedKVCache(gs, bits, reserve_rows=(Nmax + 255) // 256 * 256)
+        kq, vq = _fill_cache(cache, B, hk, Nmax, D, g, device, 1024)
+        q = torch.randn(B, hk * (Hq // Hkv), 1, D, generator=g, device=device).half()
+        out = torch.empty_like(q)
+        sl = torch.tensor(lens, dtype=torch.int32, device=device)
+        keep.append((cache, kq, vq, q, out, sl))
+        steps.append(lambda: kvq.sdpa_decode(q, kq, vq, scale, seq_lens=sl, out=out))
+        nbytes = int(lens.sum()) * hk * rb + 2 * B * hk * (Hq // Hkv) * D * 2
+        dt = "u4 codes/f16"
+        scaling = "strong"
+    elif w == "config5-ctx":
+        Hq, Hkv, D, bits, gs, N = 32, 8, 128, 4, 64, 131072
+        rb = 2 * (D * bits // 8 + 2 * (D // gs) * 2)
+        scale = 1.0 / np.sqrt(D)
+        a, b = context_ranges(N, world)[rank]
+        cache = kvq.QuantizedKVCache(gs, bits, reserve_rows=(b - a + 255) // 256 * 256)
+        kq, vq = _fill_cache(cache, 1, Hkv, b - a, D, g, device, 4096)
+        gq = torch.Generator(device=device)
+        gq.manual_seed(77)  # the same query on every rank
+        q = torch.randn(1, Hq, 1, D, generator=gq, device=device).half()
+        out = torch.empty_like(q)
+        keep.append((cache, kq, vq, q, out))
+        if world > 1:
+            split = ContextSplitDecode()
+            steps.append(lambda: out.copy_(split.step(q, kq, vq, scale)))
+            graph_ok = False  # the all-gather runs eagerly
+        else:
+            steps.append(lambda: kvq.sdpa_decode(q, kq, vq, scale, out=out))
+        nbytes = (b - a) * Hkv * rb + 2 * Hq * D * 2
+        dt = "u4 codes/f16"
+        scaling = "strong"
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            for s in steps:
+                s()
+    stream.synchronize()
+    graph = None
+    if graph_ok:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for s in steps:
+                s()
+        for _ in range(3):
+            graph.replay()
+    torch.cuda.synchronize()
+    reps = max(1, (args.steps + len(steps) - 1) // len(steps))
+    clocks = Clocks(local_rank) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+        time.sleep(0.1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+        for _ in range(reps):
+            if graph is not None:
+                graph.replay()
+            else:
+                for s in steps:
+                    s()
+        e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    t = torch.tensor([e0.elapsed_time(e1), float(nbytes)], device=device, dtype=torch.float64)
+    if world > 1:
+        tt = t.clone()
+        dist.all_reduce(t[0:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(tt[1:2], op=dist.ReduceOp.SUM)
+        t[1] = tt[1]
+    ms, total_bytes = float(t[0].item()), float(t[1].item())
+    if not torch.isfinite(keep[0][-2 if w == "config5" else -1].float()).all():
+        raise RuntimeError("non-finite decode output")
+    if rank != 0:
+        return None
+    K = reps * len(steps)
+    gbs = total_bytes * reps / (ms / 1e3) / 1e9
+    per_gpu = gbs / world
+    peak, peak_kind = peaks()
+    return {
+        "metric": f"quantized-KV decode SDPA achieved HBM GB/s ({w})", "value": round(gbs, 1),
+        "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+        "ms_per_step": round(ms / K, 5), "us_per_step": round(1e3 * ms / K, 3),
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": dt,
+        "data": "synthetic (seeded torch.randn / numpy lengths)",
+        "config": {"workload": w, "description": CONFIG_DESC[w],
+                   "bytes_per_pass_all_ranks": int(total_bytes), "steps_per_pass": len(steps),
+                   "timing": ("CUDA graph of one pass" if graph is not None else
+                              "eager steps (NCCL all-gather inside)") +
+                             ", CUDA events, max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
+                     "note": "whole step per GPU (append included where the config appends)"},
+        "clocks": clk,
+    }
+
+
 def profile_run(args):
     """Fixed small workload for ncu: 3 config-2 layers (227 MB, above L2),
     `--steps` launches of one kernel, cycling layers."""
@@ -500,9 +704,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="kvq", choices=["kvq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "config1", "config3", "config5",
+                                           "config5-ctx"], default="decode",
                     help="decode: the config-2 step the driver reads (default); prefill: "
-                         "config 4 chunked prefill, a separate JSON line")
+                         "config 4 chunked prefill; config1/3/5/5-ctx: the other BASELINE "
+                         "configs (separate JSON lines)")
     ap.add_argument("--profile", choices=["decode", "append"], default=None,
                     help="run only the named kernel over 3 config-2 layers, `--steps` "
                          "launches, no timing (a small, fixed workload for ncu captures)")
@@ -542,6 +748,15 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    if args.workload in CONFIG_DESC:
+        try:
+            res = run_config(args, rank, world, local_rank)
+            if rank == 0:
+                print(json.dumps(res))
+        finally:
+            if world > 1:
+                dist.destroy_process_group()
+        return
     try:
         res = run_gpu(args, rank, world, local_rank)
         if rank == 0:
