@@ -1385,11 +1385,14 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     ctrl[1] = 0;
   }
-  // launched as a programmatic dependent (launch_pdl): the previous kernel
-  // (the append, typically) is complete past this point
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Launched as a programmatic dependent (launch_pdl): each thread executes
+  // griddepcontrol.wait — the previous kernel (the append, typically) is
+  // complete past it — just before its first global access.  With equal
+  // lengths the split and the first chunk's addresses are arithmetic on the
+  // launch parameters, worked out while the previous kernel still runs.
   int64_t RT = (int64_t)B * Hkv * p.Tu;
   if (ragged) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int bb = tid; bb < B; bb += blockDim.x) blen[bb] = min(max(p.seq_lens[bb], 0), p.N);
     __syncthreads();
     if (warp == 0) {  // exclusive scan of Hkv * ceil(len / 16)
@@ -1471,6 +1474,7 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
           if (lane == 0) ctrl[1] = 1;
           break;
         }
+        if (c == 0 && !ragged) asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane == 0)
           issue_chunk<BITS, D, GS, CH>(p, stages + s * S::STAGE, &full[s], kbase, vbase, row,
                                        (uint32_t)min(CH, r1 - row),
@@ -1518,6 +1522,7 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
       column_bounds<NT>(klo, khi, p, 0, qrows, n, t);
       A.reset();
       if (j == 0) {
+        if (!ragged) asm volatile("griddepcontrol.wait;" ::: "memory");
         load_qfrag<BITS, D, GS, NT, BF>(Q, p, b, kvh, 0, qrows, g, t);
       } else if (j == 1) {
         const bool ok = !hung && !ctrl[1] && mbar_wait(qfb, 0u);
