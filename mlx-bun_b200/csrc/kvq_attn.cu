@@ -111,15 +111,30 @@ int32_t make_plan(const AttnArgs& a, int L, int mask_mode, int window, bool scor
   if (rc) return rc;
   if (bal) {
     const int Tu = (a.N + kTile - 1) / kTile;
-    int64_t C = (int64_t)num_sms(dev) * occ;
-    C = std::min<int64_t>(C, std::max<int64_t>(1, units * Tu / kBalMinTiles));
-    // the merge takes at most kMergeSlots partials of one unit
-    C = std::min<int64_t>(C, kMergeSlots / kWarps - 1);
-    if (budget != SIZE_MAX && budget > kPartialOff) {
-      const int64_t fit = (int64_t)((budget - kPartialOff) / bal_group_bytes(NT, a.D)) - units;
-      if (fit >= 1) C = std::min<int64_t>(C, fit);
-    }
+    auto working = [&](int blocks_per_sm) {
+      int64_t C = (int64_t)num_sms(dev) * blocks_per_sm;
+      C = std::min<int64_t>(C, std::max<int64_t>(1, units * Tu / kBalMinTiles));
+      // the merge takes at most kMergeSlots partials of one unit
+      C = std::min<int64_t>(C, kMergeSlots / kWarps - 1);
+      if (budget != SIZE_MAX && budget > kPartialOff) {
+        const int64_t fit = (int64_t)((budget - kPartialOff) / bal_group_bytes(NT, a.D)) - units;
+        if (fit >= 1) C = std::min<int64_t>(C, fit);
+      }
+      return C;
+    };
+    int64_t C = working(occ);
     pl.s = LaunchShape{1, 1, kTile};
+    // short ranges per CTA: the 16-row-slice instance (with seq_lens the
+    // padded length bounds the range)
+    if (a.D * NT <= 128 && units * Tu * kTile <= (int64_t)kBalSmallRows * C) {
+      pl.s.small = true;
+      LaunchShape probe_s = probe;
+      probe_s.small = true;
+      rc = a.bits == 4 ? dispatch_b4(p, probe_s, a.D, a.gs, NT, a.B, nullptr, &occ)
+                       : dispatch_b8(p, probe_s, a.D, a.gs, NT, a.B, nullptr, &occ);
+      if (rc) return rc;
+      C = working(occ);
+    }
     pl.s.ctas = (int)C;
     p.B = a.B;
     p.Tu = Tu;

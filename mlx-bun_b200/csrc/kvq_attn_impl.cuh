@@ -1674,8 +1674,15 @@ constexpr int stages_for() {
 
 struct LaunchShape {
   int QB, nsplit, rps;
-  int ctas = 0;  // > 0: balanced kernel with this many CTAs (one wave)
+  int ctas = 0;        // > 0: balanced kernel with this many CTAs (one wave)
+  bool small = false;  // balanced kernel with 16-row slices (short per-CTA ranges)
 };
+
+// Balanced decode: at most this many key rows per CTA take the 16-row-slice
+// instance (64-row chunks, 4 ring stages): its first chunk lands sooner and
+// a short range still fills the ring; longer ranges are issue-bound and
+// take the 32-row slices.
+constexpr int kBalSmallRows = 448;
 
 inline int num_sms(int dev) {
   static int g_num_sms[64] = {0};
@@ -1735,9 +1742,8 @@ inline size_t ws_bytes_for(int B, int Hkv, const LaunchShape& s, int NT, int D) 
 // Launch one kernel instance: the balanced decode kernel when s.ctas > 0,
 // else the split kernel.  Blocks per SM are queried once per (kernel,
 // dtype, device) and cached.
-template <int BITS, int D, int GS, int NT>
-int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* occ) {
-  constexpr int RW = rows_per_warp<D, NT>();
+template <int BITS, int D, int GS, int NT, int RW>
+int32_t launch_rw(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* occ) {
   constexpr int ST = stages_for<BITS, D, GS, RW>();
   const bool bal = s.ctas > 0;
   const int smem = bal ? BalSmem<BITS, D, GS, NT, kWarps, RW, ST>::TOTAL
@@ -1775,6 +1781,15 @@ int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* o
                             p, s.ctas));
   }
   return KVQ_OK;
+}
+
+template <int BITS, int D, int GS, int NT>
+int32_t launch_t(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* occ) {
+  constexpr int RW = rows_per_warp<D, NT>();
+  if constexpr (RW == 32) {
+    if (s.ctas > 0 && s.small) return launch_rw<BITS, D, GS, NT, 16>(p, s, B, st, occ);
+  }
+  return launch_rw<BITS, D, GS, NT, RW>(p, s, B, st, occ);
 }
 
 template <int BITS, int D, int GS>
