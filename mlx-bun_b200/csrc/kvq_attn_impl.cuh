@@ -33,8 +33,9 @@
 //        q . (s*c + b) = s * (q . c) + b * sum(q)
 //        sum_n p_n (s_n c_n + b_n) = sum_n (p_n s_n) c_n + sum_n p_n b_n
 //   * QK^T: mma.m16n8k16, key rows as M (codes as A, pairs along d), query
-//     rows as N (8 per n-tile; q as B, loaded once per CTA), d as K; one
-//     accumulator per quantisation group.
+//     rows as N (8 per n-tile; q as B, built once per CTA or, in the
+//     balanced kernel, once per segment), d as K; one accumulator per
+//     quantisation group.
 //   * online softmax in f32 with ex2.approx; scores are first rounded to the
 //     cache dtype, as the reference graph rounds them
 //     (src/model/gemma4-base.ts:1307).
@@ -42,8 +43,10 @@
 //     from the QK accumulator layout to the B-operand layout with one
 //     movmatrix.trans per 8x8 block; V codes of a (d, 2 rows) pair are
 //     interleaved with one prmt per 16-bit chunk.
-//   * splits of the key range merge in fixed order (deterministic) in the
-//     last CTA to finish, found by an atomic ticket — no second launch.
+//   * splits of the key range merge in fixed order (deterministic): in the
+//     split kernel the last CTA to finish, found by an atomic ticket,
+//     merges them; the balanced kernel leaves per-warp partials to a merge
+//     launch.
 //
 // Tensor-core choice: decode is HBM-bound with at most 16 query rows per kv
 // head, so the register-sourced mma.sync keeps the dequantised codes in
