@@ -4,20 +4,22 @@
 //
 // A CTA owns 128 query rows of one (batch, kv head): rows are (position,
 // head) pairs of the GQA group (row qr -> position qr / nrep, head qr %
-// nrep), so every key tile serves all query heads that share it.  Thread r
-// of the 4 softmax warps owns query row r — the row of TMEM lane r — so the
-// online softmax needs no cross-lane traffic.  A fifth warp streams the key
-// rows in tiles of 128 with 1-D TMA bulk copies (the decode ring).  Two
-// softmax threads share each row (warps w and w + 4 reach the same TMEM
-// lanes), each taking half of every key tile; they exchange the tile
-// maximum and, at the end, their sums through shared memory.
+// nrep), so every key tile serves all query heads that share it.  Query
+// row r is the row of TMEM lane r, so the online softmax needs no cross-lane
+// traffic.  A ninth warp streams the key rows in tiles of 128 with 1-D TMA
+// bulk copies (the decode ring).  Two of the 8 softmax warps share each row
+// (warps w and w + 4 reach the same TMEM lanes), each taking half of every
+// key tile; they exchange the tile maximum and, at the end, their sums
+// through shared memory.
 //
 // Per key tile:
 //   1. the codes become fp16 subnormals (code * 2^-24, exact) in shared
 //      memory, 128-byte-swizzled rows of 64 d: the K tile is the K-major B
-//      operand of QK^T, the V tile (same layout) the MN-major B operand of PV;
+//      operand of QK^T, the V tile (same layout, two buffers) the MN-major B
+//      operand of PV;
 //   2. QK^T per quantisation group g: S_g = Q_g . C_g^T (M 128, N 128, K 64)
-//      into TMEM (qdot factoring: logit = sum_g ks*2^24*S_g + kb*sum(q_g));
+//      into TMEM (qdot factoring: logit = sum_g ks*2^24*S_g + kb*sum(q_g)),
+//      issued once the K tile is converted and running while V is;
 //   3. softmax, two passes over TMEM: logits rounded to the dtype and masked
 //      (written back over S_0) with the tile maximum, then p = 2^((x - m)
 //      log2 e) against the row's running maximum m, P'_g = fp16(p * vs_g)
@@ -25,9 +27,10 @@
 //      rescaled only when the maximum grows by more than 2^8 (lazy rescale:
 //      P' stays far inside fp16, the final O / l is the same);
 //   4. PV per group: O_g += P'_g . V_g (M 128, N 64, K 128) in TMEM.
-// The steps run in order (commit -> mbarrier between them).  Every wait is
-// bounded; on timeout the kernel raises the device error flag and skips the
-// rest of its tiles.
+// QK of tile j + 1 waits on its commit, which also covers PV(j); with V in
+// two buffers, PV(j) runs on while tile j + 1's codes are converted.  Every
+// wait is bounded; on timeout the kernel raises the device error flag and
+// skips the rest of its tiles.
 //
 // TMEM (512 columns, one CTA per SM): S_0 [0,128) S_1 [128,256) P'_0
 // [256,320) P'_1 [320,384) O_0 [384,448) O_1 [448,512).
@@ -45,14 +48,16 @@ constexpr int TD = 128, TGS = 64, TNG = 2;
 // shared memory (offsets from a 1024-byte aligned base)
 constexpr int kQOff = 0;                        // [TNG] SW128 [128 rows][64] fp16
 constexpr int kKcOff = kQOff + TNG * 16384;     // [TNG] SW128 [128 keys][64] fp16
-constexpr int kVcOff = kKcOff + TNG * 16384;    // [TNG] SW128 [128 keys][64] fp16
-constexpr int kSclOff = kVcOff + TNG * 16384;   // f32 [4][TNG][128]: ks*2^24, kb, vs, vb
+constexpr int kVcOff = kKcOff + TNG * 16384;    // [2 tiles][TNG] SW128 [128 keys][64] fp16
+constexpr int kVcTile = TNG * 16384;            // V of tile j sits in buffer j & 1
+constexpr int kSclOff = kVcOff + 2 * kVcTile;   // f32 [4][TNG][128]: ks*2^24, kb, vs, vb
 constexpr int kRawOff = kSclOff + 4 * TNG * kKeys * 4;
 using RawLay = StageLayout<8, TD, TGS, kKeys>;
 constexpr int kXchOff = kRawOff + kTcStages * RawLay::STAGE;  // f32 [2][4][128] row exchange
 constexpr int kBarOff = kXchOff + 2 * 4 * kRows * 4;          // full[2], empty[2], qk, pv
 constexpr int kCtlOff = kBarOff + (2 * kTcStages + 2) * 8;   // tmem base, abort flag
 constexpr int kTcSmem = kCtlOff + 16 + 1024;                  // + alignment slack
+static_assert(kTcSmem <= 227 * 1024, "prefill tile buffers exceed the shared memory of a CTA");
 constexpr int kCWarps = 8;                                    // softmax warps: 2 per query row
 constexpr int kCThreads = kCWarps * 32;
 
@@ -287,17 +292,19 @@ __global__ void __launch_bounds__(288, 1) prefill_tc_kernel(const Params p) {
           hung = true;
         }
       }
+      // K codes and all scales first; QK^T is issued as soon as the K tile is
+      // in place and runs while V is converted.  V of tile j goes to buffer
+      // j & 1: PV(j - 1) may still read the other one, and PV(j - 2), the
+      // last reader of this one, completed under tile j - 1's QK commit.
+      const uint8_t* st = sm + kRawOff + s * RawLay::STAGE;
+      uint8_t* vc = sm + kVcOff + (j & 1) * kVcTile;
       if (!hung) {
-        const uint8_t* st = sm + kRawOff + s * RawLay::STAGE;
 #pragma unroll 4
         for (int it = 0; it < (kKeys * TNG * 8) / kCThreads; it++) {
           const int idx = tid + it * kCThreads;
           const int key = idx >> 4, g = (idx >> 3) & 1, c8 = idx & 7;
           const uint2 kw = *reinterpret_cast<const uint2*>(st + RawLay::O_KP + key * TD + g * TGS + c8 * 8);
-          const uint2 vw = *reinterpret_cast<const uint2*>(st + RawLay::O_VP + key * TD + g * TGS + c8 * 8);
-          const uint32_t o = sw128(key, c8 * 8);
-          *reinterpret_cast<uint4*>(sm + kKcOff + g * 16384 + o) = codes8_to_f16(kw.x, kw.y);
-          *reinterpret_cast<uint4*>(sm + kVcOff + g * 16384 + o) = codes8_to_f16(vw.x, vw.y);
+          *reinterpret_cast<uint4*>(sm + kKcOff + g * 16384 + sw128(key, c8 * 8)) = codes8_to_f16(kw.x, kw.y);
         }
         {
           // thread t: key t & 127, arrays (K scale+bias) or (V scale+bias) by t >> 7;
@@ -316,8 +323,6 @@ __global__ void __launch_bounds__(288, 1) prefill_tc_kernel(const Params p) {
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);  // raw stage free
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       asm volatile("bar.sync 1, %0;" ::"r"(kCThreads) : "memory");
@@ -334,7 +339,21 @@ __global__ void __launch_bounds__(288, 1) prefill_tc_kernel(const Params p) {
                     ks > 0 ? 1u : 0u);
         umma_commit(qk_bar);
       }
+      if (!hung) {
+#pragma unroll 4
+        for (int it = 0; it < (kKeys * TNG * 8) / kCThreads; it++) {
+          const int idx = tid + it * kCThreads;
+          const int key = idx >> 4, g = (idx >> 3) & 1, c8 = idx & 7;
+          const uint2 vw = *reinterpret_cast<const uint2*>(st + RawLay::O_VP + key * TD + g * TGS + c8 * 8);
+          *reinterpret_cast<uint4*>(vc + g * 16384 + sw128(key, c8 * 8)) = codes8_to_f16(vw.x, vw.y);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // raw stage free
+      // the V tile is read by PV after the barrier that ends step 3c
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       {
+        // this commit also covers PV(j - 1): after it, P' and O are free
         const bool ok = !hung && !*abort_flag && mbar_wait(qk_bar, (uint32_t)(j & 1));
         if (!__all_sync(0xffffffffu, ok)) {
           if (!hung && lane == 0) *abort_flag = 1;
@@ -358,17 +377,26 @@ __global__ void __launch_bounds__(288, 1) prefill_tc_kernel(const Params p) {
           tmem_wait_ld();
 #pragma unroll
           for (int k = 0; k < 32; k += 4) {
+            // two keys per paired-lane fma (each lane the same IEEE fma as a scalar one)
             const float4 ks0 = *reinterpret_cast<const float4*>(scl + (0 * TNG + 0) * kKeys + c0 + k);
             const float4 ks1 = *reinterpret_cast<const float4*>(scl + (0 * TNG + 1) * kKeys + c0 + k);
             const float4 kb0 = *reinterpret_cast<const float4*>(scl + (1 * TNG + 0) * kKeys + c0 + k);
             const float4 kb1 = *reinterpret_cast<const float4*>(scl + (1 * TNG + 1) * kKeys + c0 + k);
-            const float a0[4] = {ks0.x, ks0.y, ks0.z, ks0.w}, a1[4] = {ks1.x, ks1.y, ks1.z, ks1.w};
-            const float b0[4] = {kb0.x, kb0.y, kb0.z, kb0.w}, b1[4] = {kb1.x, kb1.y, kb1.z, kb1.w};
+            const float2 q0 = make_float2(qs[0], qs[0]), q1 = make_float2(qs[1], qs[1]);
             float sc[4];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-              sc[u] = fmaf(a0[u], __uint_as_float(s0[k + u]), fmaf(b0[u], qs[0], 0.0f));
-              sc[u] = fmaf(a1[u], __uint_as_float(s1[k + u]), fmaf(b1[u], qs[1], sc[u]));
+            for (int h2 = 0; h2 < 2; h2++) {
+              const float2 a0 = h2 ? make_float2(ks0.z, ks0.w) : make_float2(ks0.x, ks0.y);
+              const float2 a1 = h2 ? make_float2(ks1.z, ks1.w) : make_float2(ks1.x, ks1.y);
+              const float2 b0 = h2 ? make_float2(kb0.z, kb0.w) : make_float2(kb0.x, kb0.y);
+              const float2 b1 = h2 ? make_float2(kb1.z, kb1.w) : make_float2(kb1.x, kb1.y);
+              const int u = k + 2 * h2;
+              float2 t = __ffma2_rn(b0, q0, make_float2(0.0f, 0.0f));
+              t = __ffma2_rn(a0, make_float2(__uint_as_float(s0[u]), __uint_as_float(s0[u + 1])), t);
+              t = __ffma2_rn(b1, q1, t);
+              t = __ffma2_rn(a1, make_float2(__uint_as_float(s1[u]), __uint_as_float(s1[u + 1])), t);
+              sc[2 * h2] = t.x;
+              sc[2 * h2 + 1] = t.y;
             }
             float x[4];
             round_dt2<BF>(sc[0], sc[1], x[0], x[1]);
@@ -477,19 +505,20 @@ __global__ void __launch_bounds__(288, 1) prefill_tc_kernel(const Params p) {
 #pragma unroll
           for (int ks = 0; ks < kKeys / 16; ks++)
             umma_ts(tm + 384 + g * 64, tm + 256 + g * 64 + 8 * ks,
-                    desc_sw128(smem_u32(sm + kVcOff + g * 16384) + 2048 * ks), idesc_pv,
+                    desc_sw128(smem_u32(vc + g * 16384) + 2048 * ks), idesc_pv,
                     (j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(pv_bar);
       }
-      {
-        const bool ok = !hung && !*abort_flag && mbar_wait(pv_bar, (uint32_t)(j & 1));
-        if (!__all_sync(0xffffffffu, ok)) {
-          if (!hung && lane == 0) *abort_flag = 1;
-          hung = true;
-        }
-      }
-      tc_fence_after();
     }
+    // the last PV (the earlier ones completed under the following QK commits)
+    if (ntiles > 0) {
+      const bool ok = !hung && !*abort_flag && mbar_wait(pv_bar, (uint32_t)((ntiles - 1) & 1));
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (!hung && lane == 0) *abort_flag = 1;
+        hung = true;
+      }
+    }
+    tc_fence_after();
 
     // ---- epilogue: out = (2^24 O_g + sum(p vb_g)) / l, half kh writes group kh ----
     xch[(kh * 4 + 1) * kKeys + r] = lsum;
