@@ -464,7 +464,7 @@ def run_prefill(args):
                      "unit": "TFLOP/s", "frac": round(att_tf / peak, 4), "peak_kind": pk,
                      "kernel": "prefill_tc_kernel (tcgen05 UMMA, TMEM accumulators)",
                      "kernel_us": round(att_ms * 1e3, 3)},
-        "gpu_launches": 2 * reps * NL}))
+        "gpu_launches": 3 * reps * NL}))
 
 
 # ------------------------------------------------------ other configs --

@@ -194,7 +194,12 @@ int32_t kvq_sdpa_merge(const float* m, const float* l, const float* o, int32_t p
  * Query row i sits at key position keys->len - L + i (bottom-right aligned);
  * mask_mode KVQ_MASK_CAUSAL keeps keys j <= that position, and window > 0
  * additionally keeps only j > position - window (createCausalMask,
- * :1595-1614).  Workspace as for kvq_sdpa_decode (may be NULL). */
+ * :1595-1614).  Workspace as for kvq_sdpa_decode (may be NULL).  For
+ * 8-bit codes, D 128, group 64 without seq_lens, the tensor-core kernel
+ * spreads the key tiles evenly over one CTA per SM and merges the units cut
+ * between CTAs; that needs 262,400 + SMs * 135,168 bytes (20.3 MB on 148
+ * SMs).  A smaller caller buffer runs one CTA per (query block, kv head,
+ * batch entry) instead, with the same results within rounding. */
 int32_t kvq_sdpa_prefill(const kvq_qtensor* keys, const kvq_qtensor* values, const void* q,
                          int32_t q_heads, int32_t L, float scale, int32_t mask_mode,
                          int32_t window, void* out, void* workspace, size_t workspace_bytes,

@@ -238,22 +238,17 @@ int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void
   if (L <= 0) return fail(KVQ_ERR_ARG, "prefill: L must be positive");
   if (L > a.N) return fail(KVQ_ERR_ARG, "prefill: L exceeds the key length");
   if (prefill_tc_supported(a.bits, a.D, a.gs, L, false) && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
-    // tensor-core (tcgen05) prefill; it needs only the workspace's error flag
+    // tensor-core (tcgen05) prefill; its workspace holds the error flag and,
+    // for the balanced grid, the partials of units split between CTAs
     Params p;
     int NT = 1;
     int32_t rc = prepare(a, L, mask_mode, window, p, NT);
     if (rc) return rc;
     if (a.B == 0 || a.Hq == 0) return KVQ_OK;
-    if (!ws) {
-      int dev = 0;
-      KVQ_CUDA_TRY(cudaGetDevice(&dev));
-      ws = managed_workspace(dev, kPartialOff, st, &rc);
-      if (rc) return rc;
-    }
-    p.err = static_cast<int*>(ws);
     p.out = static_cast<uint16_t*>(out);
     p.mode = 0;
-    return launch_prefill_tc(p, a.B, st);
+    p.B = a.B;
+    return launch_prefill_tc(p, a.B, ws, ws_bytes, st);
   }
   return run(a, L, mask_mode, window, 0, out, nullptr, nullptr, nullptr, ws, ws_bytes, st);
 }

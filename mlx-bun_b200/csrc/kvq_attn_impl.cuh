@@ -97,8 +97,10 @@ struct Params {
   int Hq, Hkv, nrep, N, L, QB, rps, nsplit, mode, mask_mode, window;
   float scale;
   int bf16;
-  int B;                 // batch entries (balanced kernel)
-  int Tu;                // key tiles of a unit of N rows (balanced kernel)
+  int B;                 // batch entries (balanced kernels)
+  int Tu;                // key tiles of a unit of N rows (balanced decode); of one
+                         // (b, kv head) pair's query blocks (balanced prefill, whose
+                         // CTA count is QB)
 };
 
 // ---------------------------------------------------------------- PTX ----
@@ -1826,7 +1828,7 @@ int32_t pick_d(Params& p, const LaunchShape& s, int Dv, int GSv, int NT, int B, 
 
 // The tcgen05 chunked prefill (kvq_prefill_tc.cu): 8-bit codes, D 128, group 64.
 bool prefill_tc_supported(int bits, int D, int gs, int L, bool scores);
-int32_t launch_prefill_tc(Params& p, int B, cudaStream_t st);
+int32_t launch_prefill_tc(Params& p, int B, void* ws, size_t ws_bytes, cudaStream_t st);
 
 // Per-width launchers (one translation unit each, compiled in parallel);
 // s.ctas > 0 selects the balanced kernel.  With occ != nullptr they only
