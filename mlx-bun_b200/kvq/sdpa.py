@@ -122,15 +122,23 @@ def sdpa_merge_packed(packed: torch.Tensor, rows: int, head_dim: int, dtype: tor
 
 
 def sdpa_prefill(q: torch.Tensor, keys: QuantizedTensor, values: QuantizedTensor, scale: float,
-                 mask: Mask, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    """L >= 1 query rows per head over the keys (bottom-right aligned)."""
+                 mask: Mask, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                 stream=None) -> torch.Tensor:
+    """L >= 1 query rows per head over the keys (bottom-right aligned).
+
+    `workspace`: None (library-managed) or a zero-initialised device buffer.
+    The tensor-core kernel's balanced grid needs 262,400 + SMs * 135,168
+    bytes of it; with less it runs one CTA per (query block, kv head, batch
+    entry)."""
     B, Hq, L, D = _check_q(q, keys)
     if out is None:
         out = torch.empty_like(q)
     mode, window = mask.codes()
+    ws, wsb = (workspace.data_ptr(), workspace.numel() * workspace.element_size()) \
+        if workspace is not None else (None, 0)
     check(lib().kvq_sdpa_prefill(ctypes.byref(keys.qt), ctypes.byref(values.qt), q.data_ptr(),
-                                 Hq, L, ctypes.c_float(scale), mode, window, out.data_ptr(), None,
-                                 0, _stream(q, stream)))
+                                 Hq, L, ctypes.c_float(scale), mode, window, out.data_ptr(), ws,
+                                 wsb, _stream(q, stream)))
     return out
 
 

@@ -177,6 +177,32 @@ def test_prefill_no_mask_and_single_row():
         assert max_abs(from_torch(out, dt), want, dt) <= TOL[dt]
 
 
+def test_prefill_small_workspace_runs_per_unit_grid():
+    """A caller workspace too small for the balanced grid's partial slots
+    runs the tensor-core prefill with one CTA per (query block, kv head,
+    batch entry); both grids match the oracle and each other."""
+    import kvq
+    import torch
+    dt, B, Hq, Hkv, N, L, D, gs, bits = F16, 2, 8, 2, 1500, 300, 128, 64, 8
+    rng = np.random.default_rng(12)
+    q, kq, vq = quantized_inputs(rng, B, Hq, Hkv, N, D, gs, bits, dt, L=L)
+    scale = 1.0 / np.sqrt(D)
+    want = O.sdpa_unfused(q, kq, vq, scale, gs, bits, dt, mask_mode=1)
+    K = as_qtensor(*upload_triple(*kq, gs, bits)[:3], N, gs, bits, dt)
+    V = as_qtensor(*upload_triple(*vq, gs, bits)[:3], N, gs, bits, dt)
+    qt, m = to_torch_bits(q, dt), kvq.Mask("causal", 0)
+    balanced = kvq.sdpa_prefill(qt, K, V, scale, m)
+    small_ws = torch.zeros(262_400 + (1 << 20), dtype=torch.uint8, device="cuda")  # < 20 MB
+    per_unit = kvq.sdpa_prefill(qt, K, V, scale, m, workspace=small_ws)
+    torch.cuda.synchronize()
+    kvq.sdpa.check_device()  # the library-managed workspace's error flag
+    assert int(small_ws[:4].view(torch.int32).item()) == 0  # the caller workspace's flag
+    got_b, got_u = from_torch(balanced, dt), from_torch(per_unit, dt)
+    assert max_abs(got_b, want, dt) <= TOL[dt]
+    assert max_abs(got_u, want, dt) <= TOL[dt]
+    assert max_abs(got_b, got_u, dt) <= TOL[dt]
+
+
 @pytest.mark.parametrize("dt", [F16, BF16])
 def test_logits_match_oracle(dt):
     import kvq
