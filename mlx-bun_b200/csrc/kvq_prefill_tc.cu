@@ -711,11 +711,15 @@ __global__ void __launch_bounds__(288, 1) prefill_tc_kernel(const Params p) {
 // this run (every split unit has exactly one such CTA).  Its pieces sit in
 // slot 2c' of every CTA c' after the first one (their first unit) and in
 // slot 2c' + 1 of the first CTA when the unit is not where that CTA's run
-// starts (its last unit).  Thread (kh, r) merges row r's group kh columns.
+// starts (its last unit).  Thread (qc, r) merges 32 columns (quarter qc) of
+// row r.
+constexpr int kMergeThreads = 4 * kRows;
+
 template <bool BF>
-__global__ void __launch_bounds__(256) prefill_tc_merge_kernel(const Params p) {
+__global__ void __launch_bounds__(kMergeThreads) prefill_tc_merge_kernel(const Params p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int tid = threadIdx.x, lane = tid & 31, r = tid & (kRows - 1), kh = tid >> 7;
+  const int tid = threadIdx.x, lane = tid & 31, r = tid & (kRows - 1), qc = tid >> 7;
+  const int kh = qc >> 1;  // quantisation group of these columns
   const int nrep = p.nrep, L = p.L, qrows = nrep * L;
   const int nqb = (qrows + kRows - 1) / kRows;
   const int64_t C = p.QB;
@@ -733,23 +737,33 @@ __global__ void __launch_bounds__(256) prefill_tc_merge_kernel(const Params p) {
   while (cf > 0 && cf * T / C > u0) cf--;
   const int qr = qt * kRows + r;
   if (qr >= qrows) return;
+  const int np = (int)(c - cf + 1);  // pieces
+  // piece i's row: slot 2(cf + i), or 2cf + 1 for a first piece that is not
+  // where its CTA's run starts
+  const size_t row0 = ((size_t)(2 * cf + (u0 > cf * T / C ? 1 : 0)) * kRows + r) * kSlotRow;
+  auto piece = [&](int i) -> const float* {
+    return p.ws_o + (i == 0 ? row0 : ((size_t)(2 * (cf + i)) * kRows + r) * kSlotRow);
+  };
   float mx = kNeg;
-  for (int64_t cc = cf; cc <= c; cc++) {
-    const int64_t slot = (cc == cf && u0 > cc * T / C) ? 2 * cc + 1 : 2 * cc;
-    mx = fmaxf(mx, p.ws_o[((size_t)slot * kRows + r) * kSlotRow]);
-  }
-  float lt = 0.0f, pb = 0.0f, o[TGS];
+  for (int i0 = 0; i0 < np; i0 += 4) {
+    float mv[4];
 #pragma unroll
-  for (int k = 0; k < TGS; k++) o[k] = 0.0f;
-  for (int64_t cc = cf; cc <= c; cc++) {
-    const int64_t slot = (cc == cf && u0 > cc * T / C) ? 2 * cc + 1 : 2 * cc;
-    const float* srow = p.ws_o + ((size_t)slot * kRows + r) * kSlotRow;
+    for (int i = 0; i < 4; i++) mv[i] = i0 + i < np ? piece(i0 + i)[0] : kNeg;
+#pragma unroll
+    for (int i = 0; i < 4; i++) mx = fmaxf(mx, mv[i]);
+  }
+  float lt = 0.0f, pb = 0.0f, o[32];
+#pragma unroll
+  for (int k = 0; k < 32; k++) o[k] = 0.0f;
+#pragma unroll 2
+  for (int i = 0; i < np; i++) {
+    const float* srow = piece(i);
     const float w = ex2((srow[0] - mx) * kLog2e);
     lt = fmaf(w, srow[1], lt);
     pb = fmaf(w, srow[2 + kh], pb);
 #pragma unroll
-    for (int k = 0; k < TGS; k += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(srow + 4 + kh * TGS + k);
+    for (int k = 0; k < 32; k += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(srow + 4 + qc * 32 + k);
       o[k] = fmaf(w, v.x, o[k]);
       o[k + 1] = fmaf(w, v.y, o[k + 1]);
       o[k + 2] = fmaf(w, v.z, o[k + 2]);
@@ -758,9 +772,9 @@ __global__ void __launch_bounds__(256) prefill_tc_merge_kernel(const Params p) {
   }
   const int b = (int)(hp / p.Hkv), kvh = (int)(hp - (int64_t)b * p.Hkv);
   const int l = qr / nrep, hh = qr - l * nrep;
-  uint16_t* dst = p.out + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * TD + kh * TGS;
+  uint16_t* dst = p.out + (((int64_t)b * p.Hq + kvh * nrep + hh) * L + l) * TD + qc * 32;
 #pragma unroll
-  for (int k = 0; k < TGS; k += 8) {
+  for (int k = 0; k < 32; k += 8) {
     uint32_t w[4];
 #pragma unroll
     for (int u = 0; u < 4; u++) {
@@ -817,7 +831,7 @@ int32_t launch_prefill_tc(Params& p, int B, void* ws, size_t ws_bytes, cudaStrea
   if (ctas > 0) {
     KVQ_CUDA_TRY(launch_pdl(kern, dim3((unsigned)ctas), dim3(kCThreads + 32), (size_t)kTcSmem, st, p));
     auto merge = p.bf16 ? prefill_tc_merge_kernel<true> : prefill_tc_merge_kernel<false>;
-    KVQ_CUDA_TRY(launch_pdl(merge, dim3((unsigned)ctas), dim3(256), 0, st, p));
+    KVQ_CUDA_TRY(launch_pdl(merge, dim3((unsigned)ctas), dim3(kMergeThreads), 0, st, p));
     return KVQ_OK;
   }
   const dim3 grid((unsigned)nqb, (unsigned)p.Hkv, (unsigned)B);
