@@ -2,7 +2,7 @@
 // cores (tcgen05 / UMMA with TMEM accumulators) for 8-bit codes, D = 128,
 // group 64 (the config-4 shape); other shapes take the split kernel.
 //
-// A CTA owns 128 query rows of one (batch, kv head): rows are (position,
+// A unit is 128 query rows of one (batch, kv head): rows are (position,
 // head) pairs of the GQA group (row qr -> position qr / nrep, head qr %
 // nrep), so every key tile serves all query heads that share it.  Query
 // row r is the row of TMEM lane r, so the online softmax needs no cross-lane
