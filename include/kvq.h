@@ -146,7 +146,14 @@ int32_t kvq_quantize(const void* x, int64_t rows, int32_t head_dim, int32_t grou
 /* ---- attention ---------------------------------------------------------- */
 
 /* Workspace bytes kvq_sdpa_decode / kvq_sdpa_decode_partial need for these
- * shapes.  Replaces nothing in the reference (MLX allocates internally). */
+ * shapes.  Replaces nothing in the reference (MLX allocates internally).
+ *
+ * Library-managed workspace (workspace == NULL in the attention calls): one
+ * buffer per device.  The first call that needs more than it holds
+ * allocates a larger one (cudaMalloc, at least twice the old size), zeroes
+ * it and synchronizes the calling stream; that call must not be made while
+ * a stream capture is open.  The replaced buffer is not freed, so work
+ * queued earlier and graphs captured earlier keep valid memory. */
 int32_t kvq_sdpa_decode_workspace(const kvq_qtensor* keys, int32_t q_heads, size_t* bytes);
 
 /* L = 1 attention over a quantized K/V pair (quantizedSdpa's decode cases:
@@ -217,29 +224,74 @@ int32_t kvq_debug_scores(const kvq_qtensor* keys, const void* q, int32_t q_heads
  * prefix of the decode workspace plus 2 MiB of split partials. */
 #define KVQ_NOALLOC_SCRATCH_BYTES (256u * 1024u + 256u + 2u * 1024u * 1024u)
 
-/* kvq_sdpa_decode for callers that must not allocate device memory: code
- * running while a CUDA stream capture is open (cudaMalloc is illegal then)
- * and serving processes that give all device memory to their own pool at
- * start-up.  No counterpart in the reference (MLX allocates internally).
- * Same arguments and results as kvq_sdpa_decode without the workspace: the
- * kernel's scratch is a fixed KVQ_NOALLOC_SCRATCH_BYTES array inside the
- * library that every GPU loading libkvq keeps until exit.  The first call on
- * a device looks up that array's device address (make it before any stream
- * capture).  Each call clears the scratch's flag and tickets with a
- * stream-ordered memset; all calls share the array, so calls that overlap
- * on the GPU race — issue them on one stream.  When the full launch's split
- * partials would not fit, the decode runs on fewer CTAs so that they do;
- * shapes whose partials do not fit even then return KVQ_ERR_WORKSPACE with
- * the sizes in kvq_last_error(). */
+/* kvq_sdpa_decode for callers that cannot have device memory allocated on
+ * their behalf: serving processes that give all free device memory to their
+ * own pool at start-up, and latency-bound decode loops that must never meet
+ * the implicit device synchronization of a cudaMalloc.  No counterpart in
+ * the reference (MLX allocates internally).  Same arguments and results as
+ * kvq_sdpa_decode without the workspace: the kernel's scratch is a fixed
+ * KVQ_NOALLOC_SCRATCH_BYTES array inside the library that every GPU loading
+ * libkvq keeps until exit.  The first call on a device looks up that
+ * array's device address (make it before any stream capture).  Each call
+ * clears the scratch's split tickets with a stream-ordered memset; all
+ * calls share the array, so calls that overlap on the GPU race — issue them
+ * on one stream.  The error flag at the array's start is left as it is, so
+ * a timed-out wait stays visible until kvq_check_device(NULL, ...) reports
+ * it.  When the full launch's split partials would not fit, the decode runs
+ * on fewer CTAs (or without a key split) so that they do; shapes whose
+ * partials do not fit even then return KVQ_ERR_WORKSPACE with the sizes in
+ * kvq_last_error(). */
 int32_t kvq_sdpa_decode_noalloc(const kvq_qtensor* keys, const kvq_qtensor* values,
                                 const void* q, int32_t q_heads, float scale,
                                 const int32_t* seq_lens, void* out, void* stream);
 
+/* ---- context split across the GPUs of one node (peer memory) ----------- */
+
+/* Exchange of context-split partials among the nranks ranks (one process
+ * per GPU) of one node, over peer memory: no NCCL call on the data path.
+ * No reference counterpart (the reference is single-device).
+ * Each rank allocates an exchange buffer on its current device (flags, a
+ * device-resident step epoch and 2 x nranks slots of rows * (head_dim + 2)
+ * floats) and writes its CUDA IPC handle (64 bytes) to handle_out.
+ * Synchronizes the device. */
+typedef struct kvq_peer_group kvq_peer_group;
+int32_t kvq_peer_group_create(int32_t rank, int32_t nranks, int32_t rows, int32_t head_dim,
+                              void* handle_out, kvq_peer_group** out);
+
+/* Map the other ranks' exchange buffers: handles holds all nranks handles
+ * (64 bytes each) in rank order, as gathered from every rank. */
+int32_t kvq_peer_group_connect(kvq_peer_group* group, const void* handles);
+
+/* One exchange + merge step, stream-ordered: this rank's packed partial
+ * (device [m rows | l rows | o rows*head_dim] f32, the layout
+ * kvq_sdpa_decode_partial writes when its three outputs are carved out of
+ * one buffer) is stored into every rank's buffer, and once all nranks
+ * partials of the step have arrived (bounded wait, 2 s) they are merged in
+ * rank order into out[rows][head_dim] in dtype — identical on every rank.
+ * Every rank must make the same sequence of calls; the step counter lives on
+ * the device, so the call may be recorded in a CUDA graph and replayed. */
+int32_t kvq_peer_exchange_merge(kvq_peer_group* group, const float* packed, int32_t dtype,
+                                void* out, void* stream);
+
+/* Synchronize `stream` and report (then clear) the group's error flag,
+ * raised when a rank's partials did not arrive within the wait limit. */
+int32_t kvq_peer_group_check(kvq_peer_group* group, void* stream);
+
+/* Unmap the peers' buffers and free this rank's (synchronizes the device).
+ * Call only after every rank has finished its last exchange step. */
+int32_t kvq_peer_group_free(kvq_peer_group* group);
+
 /* Synchronize `stream` and report (then clear) the device error flag that a
  * kernel raises when a bounded wait on its own TMA copies times out.
  * workspace: the caller workspace used by the calls, or NULL for the
- * library-managed one of the current device. */
+ * current device's library-managed workspaces (the live one and any it
+ * replaced) and its kvq_sdpa_decode_noalloc scratch. */
 int32_t kvq_check_device(void* workspace, void* stream);
+
+/* Test hook: raise the error flag(s) kvq_check_device(workspace, ...) would
+ * read, stream-ordered, so a test can see a raised flag reported without
+ * making a kernel time out.  Not a hot path; no reference counterpart. */
+int32_t kvq_debug_raise_flag(void* workspace, void* stream);
 
 #ifdef __cplusplus
 }

@@ -145,6 +145,12 @@ int32_t make_plan(const AttnArgs& a, int L, int mask_mode, int window, bool scor
       pl.s.nsplit = 1;
       pl.s.rps = std::max(a.N, 1);
     }
+    // a bounded workspace that cannot hold the split partials: no key split
+    // (an unsplit launch needs only the flag and ticket prefix)
+    if (budget != SIZE_MAX && ws_bytes_for(a.B, a.Hkv, pl.s, NT, a.D) > budget) {
+      pl.s.nsplit = 1;
+      pl.s.rps = std::max(a.N, 1);
+    }
     pl.tickets = pl.s.nsplit > 1 ? units * pl.s.QB : 0;
   }
   pl.ws_bytes = ws_bytes_for(a.B, a.Hkv, pl.s, NT, a.D);

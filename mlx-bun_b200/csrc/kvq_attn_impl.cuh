@@ -1580,7 +1580,7 @@ __global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int g
   constexpr int HQ = 8 * NT;
   constexpr int SLOT = HQ * (D + 2);  // floats per partial slot
   __shared__ int64_t red_t[2];
-  const int u = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int u = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
   const int Hkv = p.Hkv, b = u / Hkv, kvh = u - b * Hkv;
   const int64_t orow = (int64_t)b * p.Hq + kvh * p.nrep + r;
 
@@ -1728,7 +1728,7 @@ inline LaunchShape shape_for(int B, int Hkv, int nrep, int L, int N, int NT, int
 //   [256, 256 + 4*kMaxTickets)    split tickets, zero between calls
 //   then (m, l) and o partials of the splits.
 constexpr int64_t kMaxTickets = 65536;
-constexpr size_t kTicketOff = 256;
+constexpr size_t kTicketOff = kWsFlagBytes;
 constexpr size_t kPartialOff = kTicketOff + 4 * kMaxTickets;
 
 // Balanced decode partials: (ctas + units) groups of kWarps slots of
@@ -1746,7 +1746,7 @@ inline size_t ws_bytes_for(int B, int Hkv, const LaunchShape& s, int NT, int D) 
 
 // Launch one kernel instance: the balanced decode kernel when s.ctas > 0,
 // else the split kernel.  Blocks per SM are queried once per (kernel,
-// dtype, device) and cached.
+// device) and cached (kernel_setup).
 template <int BITS, int D, int GS, int NT, int RW>
 int32_t launch_rw(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* occ) {
   constexpr int ST = stages_for<BITS, D, GS, RW>();
@@ -1760,17 +1760,11 @@ int32_t launch_rw(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* 
   else
     kern = p.bf16 ? attn_kernel<BITS, D, GS, NT, kWarps, RW, ST, true>
                   : attn_kernel<BITS, D, GS, NT, kWarps, RW, ST, false>;
-  static int blocks[2][2][64] = {};
   int dev = 0;
   KVQ_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return fail(KVQ_ERR_ARG, "device ordinal out of range");
-  int& nb = blocks[bal][p.bf16][dev];
-  if (!nb) {
-    KVQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    int n = 0;
-    KVQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kWarps + 1) * 32, smem));
-    nb = n > 0 ? n : 1;
-  }
+  int nb = 1;
+  int32_t rc = kernel_setup(reinterpret_cast<const void*>(kern), (kWarps + 1) * 32, smem, dev, &nb);
+  if (rc) return rc;
   if (occ) {
     *occ = nb;
     return KVQ_OK;

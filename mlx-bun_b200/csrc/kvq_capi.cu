@@ -24,6 +24,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -49,15 +50,20 @@ int32_t cuda_fail(cudaError_t e, const char* what) {
 
 // ------------------------------------------------ library-managed scratch --
 
+// One buffer per device, grown on demand.  A larger shape gets a new,
+// larger buffer; the old one is never freed, because work already queued
+// or recorded in a CUDA graph may still use it (each replay of a captured
+// graph reads the pointer it was captured with).  Sizes at least double on
+// each growth, so the retired buffers together stay below the live one.
 struct ManagedWs {
   void* ptr = nullptr;
   size_t bytes = 0;
+  std::vector<void*> retired;
 };
 static std::mutex g_ws_mu;
 static ManagedWs g_ws[64];
 
 void* managed_workspace(int device, size_t bytes, cudaStream_t st, int32_t* status) {
-  (void)st;
   *status = KVQ_OK;
   if (device < 0 || device >= 64) {
     *status = fail(KVQ_ERR_ARG, "device ordinal out of range");
@@ -66,36 +72,67 @@ void* managed_workspace(int device, size_t bytes, cudaStream_t st, int32_t* stat
   std::lock_guard<std::mutex> lk(g_ws_mu);
   ManagedWs& w = g_ws[device];
   if (w.bytes >= bytes && w.ptr) return w.ptr;
-  // Growth happens on the first call for a larger shape (before any graph
-  // capture): synchronize so no queued kernel still uses the old buffer.
-  cudaError_t e = cudaDeviceSynchronize();
+  const size_t nb = std::max({bytes, (size_t)1 << 20, 2 * w.bytes});
+  void* np = nullptr;
+  cudaError_t e = cudaMalloc(&np, nb);
   if (e != cudaSuccess) {
-    *status = cuda_fail(e, "cudaDeviceSynchronize");
-    return nullptr;
-  }
-  if (w.ptr) cudaFree(w.ptr);
-  w.ptr = nullptr;
-  w.bytes = 0;
-  size_t nb = std::max(bytes, (size_t)1 << 20);
-  e = cudaMalloc(&w.ptr, nb);
-  if (e != cudaSuccess) {
-    w.ptr = nullptr;
     *status = cuda_fail(e, "cudaMalloc(workspace)");
     return nullptr;
   }
-  e = cudaMemset(w.ptr, 0, nb);
+  // Zero it on the calling stream and wait: the buffer is shared by every
+  // stream of the device, so it must be clean before this call returns.
+  e = cudaMemsetAsync(np, 0, nb, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
-    *status = cuda_fail(e, "cudaMemset(workspace)");
+    cudaFree(np);
+    *status = cuda_fail(e, "zeroing the workspace");
     return nullptr;
   }
+  if (w.ptr) w.retired.push_back(w.ptr);
+  w.ptr = np;
   w.bytes = nb;
   return w.ptr;
 }
 
-static void* managed_ptr(int device) {
-  if (device < 0 || device >= 64) return nullptr;
+// Every buffer of `device` whose error flag a kernel may have raised: the
+// live workspace and the retired ones that captured graphs may still use.
+static std::vector<void*> managed_ptrs(int device) {
+  std::vector<void*> v;
+  if (device < 0 || device >= 64) return v;
   std::lock_guard<std::mutex> lk(g_ws_mu);
-  return g_ws[device].ptr;
+  if (g_ws[device].ptr) v.push_back(g_ws[device].ptr);
+  v.insert(v.end(), g_ws[device].retired.begin(), g_ws[device].retired.end());
+  return v;
+}
+
+// ------------------------------------------ per-device kernel attributes --
+
+struct KernelKey {
+  const void* kern;
+  int dev, threads, smem;
+  bool operator<(const KernelKey& o) const {
+    if (kern != o.kern) return kern < o.kern;
+    if (dev != o.dev) return dev < o.dev;
+    if (threads != o.threads) return threads < o.threads;
+    return smem < o.smem;
+  }
+};
+static std::mutex g_kern_mu;
+static std::map<KernelKey, int> g_kern_blocks;
+
+int32_t kernel_setup(const void* kern, int threads, int smem, int dev, int* blocks_per_sm) {
+  std::lock_guard<std::mutex> lk(g_kern_mu);
+  const KernelKey key{kern, dev, threads, smem};
+  auto it = g_kern_blocks.find(key);
+  if (it == g_kern_blocks.end()) {
+    // the attribute is per device: set it with `dev` current
+    KVQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    int n = 0;
+    KVQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, (size_t)smem));
+    it = g_kern_blocks.emplace(key, n > 0 ? n : 1).first;
+  }
+  if (blocks_per_sm) *blocks_per_sm = it->second;
+  return KVQ_OK;
 }
 
 }  // namespace kvq
@@ -620,20 +657,42 @@ int32_t kvq_debug_scores(const kvq_qtensor* keys, const void* q, int32_t q_heads
 int32_t kvq_check_device(void* workspace, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   KVQ_CUDA_TRY(cudaStreamSynchronize(st));
-  void* ws = workspace;
-  if (!ws) {
+  std::vector<void*> flags;
+  if (workspace) {
+    flags.push_back(workspace);
+  } else {
     int dev = 0;
     KVQ_CUDA_TRY(cudaGetDevice(&dev));
-    ws = managed_ptr(dev);
+    flags = managed_ptrs(dev);
+    if (void* s = noalloc_scratch_if_known(dev)) flags.push_back(s);
   }
-  if (!ws) return KVQ_OK;
-  int flag = 0;
-  KVQ_CUDA_TRY(cudaMemcpy(&flag, ws, sizeof(int), cudaMemcpyDeviceToHost));
-  if (flag) {
-    const int zero = 0;
-    KVQ_CUDA_TRY(cudaMemcpy(ws, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  bool raised = false;
+  for (void* f : flags) {
+    int flag = 0;
+    KVQ_CUDA_TRY(cudaMemcpy(&flag, f, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+      const int zero = 0;
+      KVQ_CUDA_TRY(cudaMemcpy(f, &zero, sizeof(int), cudaMemcpyHostToDevice));
+      raised = true;
+    }
+  }
+  if (raised)
     return fail(KVQ_ERR_CUDA, "a kernel gave up waiting for its TMA copies (device error flag set)");
+  return KVQ_OK;
+}
+
+int32_t kvq_debug_raise_flag(void* workspace, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<void*> flags;
+  if (workspace) {
+    flags.push_back(workspace);
+  } else {
+    int dev = 0;
+    KVQ_CUDA_TRY(cudaGetDevice(&dev));
+    flags = managed_ptrs(dev);
+    if (void* s = noalloc_scratch_if_known(dev)) flags.push_back(s);
   }
+  for (void* f : flags) KVQ_CUDA_TRY(cudaMemsetAsync(f, 1, 1, st));
   return KVQ_OK;
 }
 

@@ -102,7 +102,23 @@ int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void
 int32_t launch_debug_scores(const AttnArgs& a, int L, int mask_mode, int window, float* scores,
                             cudaStream_t st);
 
-// Library-managed scratch per device (grown on demand, zero-filled).
+// Library-managed scratch per device (grown on demand, zero-filled; a
+// buffer that a larger shape replaces stays allocated, since queued work or
+// a captured graph may still use it).
 void* managed_workspace(int device, size_t bytes, cudaStream_t st, int32_t* status);
+
+// Every decode/prefill workspace starts with the device error flag (an int
+// at offset 0) in a block of this many bytes.
+constexpr size_t kWsFlagBytes = 256;
+
+// Opt `kern` in to `smem` bytes of dynamic shared memory on device `dev`
+// (the current device) and report its resident blocks per SM at `threads`
+// threads.  The attribute is per device: done once per (kernel, device,
+// shape) under a lock, then cached.
+int32_t kernel_setup(const void* kern, int threads, int smem, int dev, int* blocks_per_sm);
+
+// Device address of kvq_sdpa_decode_noalloc's scratch on `dev`, or nullptr
+// while no call on that device has looked it up (kvq_noalloc.cu).
+void* noalloc_scratch_if_known(int dev);
 
 }  // namespace kvq

@@ -1,14 +1,16 @@
 // kvq_noalloc.cu — decode attention that allocates no device memory.
 //
-// Some callers must not allocate: code that runs while a CUDA stream
-// capture is open (cudaMalloc is illegal then), and serving processes that
-// hand all device memory to their own pool at start-up.  For them
-// kvq_sdpa_decode_noalloc runs the same decode kernels as kvq_sdpa_decode
-// but keeps their scratch (device error flag, split tickets, split partials)
-// in the file-scope array below instead of a cudaMalloc'd buffer.  When the
-// partials of the full launch would not fit, the decode is spread over fewer
-// CTAs (fewer partials) so that they do; shapes whose partials do not fit
-// even with a single CTA are refused.
+// Some callers cannot have device memory allocated on their behalf:
+// serving processes that hand all free device memory to their own pool at
+// start-up (a cudaMalloc then fails, or takes memory the pool counts on),
+// and latency-bound decode loops that must never meet the implicit device
+// synchronization of a cudaMalloc.  For them kvq_sdpa_decode_noalloc runs
+// the same decode kernels as kvq_sdpa_decode but keeps their scratch
+// (device error flag, split tickets, split partials) in the file-scope
+// array below instead of a cudaMalloc'd buffer.  When the partials of the
+// full launch would not fit, the decode is spread over fewer CTAs (fewer
+// partials) so that they do; shapes whose partials do not fit even with a
+// single CTA are refused.
 //
 // The array is KVQ_NOALLOC_SCRATCH_BYTES long; every GPU that loads the
 // library holds it until the process exits.  Host code cannot use the
@@ -16,8 +18,11 @@
 // that device current) looks the address up once with cudaGetSymbolAddress;
 // make that first call before any stream capture.  Every call shares the
 // array and leaves its contents behind, so each call clears the part that
-// must start at zero (flag and tickets) with a stream-ordered memset, and
-// calls that overlap on the GPU race: issue them on one stream.
+// must start at zero (the split tickets) with a stream-ordered memset, and
+// calls that overlap on the GPU race: issue them on one stream.  The device
+// error flag at the start of the array is not cleared by a call: a bounded
+// wait that timed out stays visible until kvq_check_device(NULL, ...) on
+// that device reports and clears it.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -48,6 +53,12 @@ int32_t scratch_address(int dev, void** out) {
 
 }  // namespace
 
+void* kvq::noalloc_scratch_if_known(int dev) {
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  return g_scratch_ptr[dev];
+}
+
 extern "C" int32_t kvq_sdpa_decode_noalloc(const kvq_qtensor* keys, const kvq_qtensor* values,
                                            const void* q, int32_t q_heads, float scale,
                                            const int32_t* seq_lens, void* out, void* stream) {
@@ -70,7 +81,11 @@ extern "C" int32_t kvq_sdpa_decode_noalloc(const kvq_qtensor* keys, const kvq_qt
   void* ws = nullptr;
   if ((rc = scratch_address(dev, &ws))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  KVQ_CUDA_TRY(cudaMemsetAsync(ws, 0, zero_prefix, st));
+  // Clear the tickets only: the error flag (the first kWsFlagBytes) keeps a
+  // timeout raised by an earlier call until kvq_check_device reports it.
+  if (zero_prefix > kWsFlagBytes)
+    KVQ_CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(ws) + kWsFlagBytes, 0,
+                                 zero_prefix - kWsFlagBytes, st));
   return launch_decode(a, out, nullptr, nullptr, nullptr, ws, (size_t)KVQ_NOALLOC_SCRATCH_BYTES,
                        st, /*fit_to_ws=*/true);
 }

@@ -794,13 +794,10 @@ bool prefill_tc_supported(int bits, int D, int gs, int L, bool scores) {
 
 int32_t launch_prefill_tc(Params& p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   auto kern = p.bf16 ? prefill_tc_kernel<true> : prefill_tc_kernel<false>;
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[p.bf16]) {
-    KVQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
-    attr_set[p.bf16] = true;
-  }
   int dev = 0;
   KVQ_CUDA_TRY(cudaGetDevice(&dev));
+  int32_t rc = kernel_setup(reinterpret_cast<const void*>(kern), kCThreads + 32, kTcSmem, dev, nullptr);
+  if (rc) return rc;
   const int qrows = p.nrep * p.L;
   const int nqb = (qrows + kRows - 1) / kRows;
   // Balanced grid (one CTA per SM, equal runs of key tiles, a merge for the
@@ -819,7 +816,6 @@ int32_t launch_prefill_tc(Params& p, int B, void* ws, size_t ws_bytes, cudaStrea
       need = kPartialOff;
     }
   }
-  int32_t rc = KVQ_OK;
   if (!ws) {
     ws = managed_workspace(dev, need, st, &rc);
     if (rc) return rc;

@@ -26,7 +26,9 @@ EXPORTS = (
     "kvq_cache_fetch", "kvq_cache_state", "kvq_cache_trim", "kvq_cache_make_mask",
     "kvq_quantize", "kvq_sdpa_decode_workspace", "kvq_sdpa_decode", "kvq_sdpa_decode_partial",
     "kvq_sdpa_merge", "kvq_sdpa_prefill", "kvq_debug_scores", "kvq_check_device",
-    "kvq_sdpa_decode_noalloc",
+    "kvq_sdpa_decode_noalloc", "kvq_debug_raise_flag", "kvq_peer_group_create",
+    "kvq_peer_group_connect", "kvq_peer_exchange_merge", "kvq_peer_group_check",
+    "kvq_peer_group_free",
 )
 
 
@@ -86,6 +88,12 @@ def lib():
         "kvq_debug_scores": (i32, [P(QTensor), vp, i32, i32, f32, i32, i32, vp, vp]),
         "kvq_check_device": (i32, [vp, vp]),
         "kvq_sdpa_decode_noalloc": (i32, [P(QTensor), P(QTensor), vp, i32, f32, vp, vp, vp]),
+        "kvq_debug_raise_flag": (i32, [vp, vp]),
+        "kvq_peer_group_create": (i32, [i32, i32, i32, i32, vp, P(vp)]),
+        "kvq_peer_group_connect": (i32, [vp, vp]),
+        "kvq_peer_exchange_merge": (i32, [vp, vp, i32, vp, vp]),
+        "kvq_peer_group_check": (i32, [vp, vp]),
+        "kvq_peer_group_free": (i32, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

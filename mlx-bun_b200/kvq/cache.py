@@ -109,6 +109,21 @@ class QuantizedTensor:
         q = self.qt
         return self._view(q.biases, q.head_dim // q.group_size, "<i2", 2, torch_dtype(q.dtype))
 
+    def slice_rows(self, start: int, stop: int) -> "QuantizedTensor":
+        """The view of key rows [start, stop) of every (batch, head) — one
+        rank's range of a context split.  `start` must be a multiple of 16
+        (the kernels' row tile), so every component stays 16-byte aligned."""
+        q = self.qt
+        if not (0 <= start <= stop <= q.len) or start % 16:
+            raise ValueError("slice_rows: need 0 <= start <= stop <= len and start % 16 == 0")
+        word_b = q.head_dim * q.bits // 8
+        grp_b = q.head_dim // q.group_size * 2
+        qt = QTensor(q.packed + start * word_b, q.scales + start * grp_b,
+                     q.biases + start * grp_b, q.batch_stride, q.head_stride, q.batch, q.heads,
+                     stop - start, q.head_dim, q.bits, q.group_size, q.dtype)
+        return QuantizedTensor(qt, self.device, owner=self._owner if self._owner is not None
+                               else self)
+
     @classmethod
     def from_tensors(cls, packed: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                      group_size: int, bits: int) -> "QuantizedTensor":

@@ -11,12 +11,18 @@ quantized-KV attention admits on one 8-GPU node:
 * Split one long context (``ContextSplitDecode``): rank r owns the
   contiguous key range ``context_ranges(N, world)[r]`` of the sequence;
   each rank computes log-sum-exp partials (m, l, o) of its range with
-  ``kvq_sdpa_decode_partial``, one ``all_gather_into_tensor`` exchanges the
-  packed partials (rows * (D + 2) floats per rank), and every rank merges
-  them in rank order with ``kvq_sdpa_merge`` (deterministic).
+  ``kvq_sdpa_decode_partial`` into one packed buffer (rows * (D + 2) floats),
+  the partials move to every rank, and every rank merges them in rank order
+  (deterministic, identical on all ranks).  Two transports:
+    - "peer" (GPUs): ``kvq_peer_exchange_merge`` stores the packed partial
+      into every rank's exchange buffer over peer memory (CUDA IPC, NVLink)
+      and merges once all have arrived — one kernel, no NCCL call and no
+      host synchronisation per step, so a step can live in a CUDA graph;
+    - "collective": ``all_gather_into_tensor`` through torch.distributed
+      (NCCL, or gloo in the CPU tests) followed by ``kvq_sdpa_merge``.
 
-The collectives go through ``torch.distributed`` (NCCL on GPUs; the host
-logic is exercised with gloo on CPU in the tests).
+The process group is used for set-up (exchanging the IPC handles) in the
+peer transport, and for the data in the collective one.
 """
 from __future__ import annotations
 
@@ -76,32 +82,123 @@ def gather_partials(packed, group=None):
     return out.view((world,) + tuple(packed.shape))
 
 
+def _stream_ctx(stream):
+    """`with` context making `stream` (a torch.cuda.Stream, or None for the
+    current stream) current, so partial, exchange and merge share one
+    stream and run in order."""
+    import contextlib
+    import torch
+    return torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
+
+
+class PeerGroup:
+    """This rank's side of a peer-memory exchange among the ranks of
+    `group` (one per GPU of one node) for partial sets of `rows` x
+    `head_dim` (kvq_peer_group_* in include/kvq.h)."""
+
+    def __init__(self, rows: int, head_dim: int, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from ._lib import check, lib
+        self.rows, self.head_dim = rows, head_dim
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        handle = (ctypes.c_uint8 * 64)()
+        h = ctypes.c_void_p()
+        check(lib().kvq_peer_group_create(rank, world, rows, head_dim, handle, ctypes.byref(h)))
+        self._h = h
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        blob = b"".join(handles)
+        check(lib().kvq_peer_group_connect(h, blob))
+        dist.barrier(group=group)  # every rank mapped every buffer
+
+    def exchange_merge(self, packed, dtype, out, stream_handle):
+        from ._lib import check, lib
+        from .cache import dtype_code
+        check(lib().kvq_peer_exchange_merge(self._h, packed.data_ptr(), dtype_code(dtype),
+                                            out.data_ptr(), stream_handle))
+
+    def check(self, stream_handle=None):
+        """Synchronize the device and raise if a step gave up waiting for a rank."""
+        import torch
+        from ._lib import check, lib
+        torch.cuda.synchronize()
+        check(lib().kvq_peer_group_check(self._h, stream_handle))
+
+    def close(self):
+        """Free after every rank's last step (callers barrier first)."""
+        from ._lib import check, lib
+        if self._h:
+            h, self._h = self._h, None
+            check(lib().kvq_peer_group_free(h))
+
+
 class ContextSplitDecode:
     """Decode of one very long sequence whose K/V is split across ranks.
 
     Each rank holds a kvq cache with its own key range; ``step(q)`` returns
     the full attention output on every rank.  Only the partials cross
-    NVLink: B * Hq * (D + 2) floats per rank per step."""
+    NVLink: B * Hq * (D + 2) floats per rank per step.  `transport` is
+    "peer" (peer-memory exchange kernel) or "collective" (all-gather through
+    torch.distributed, then merge)."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, transport: str = "peer"):
+        if transport not in ("peer", "collective"):
+            raise ValueError("transport must be 'peer' or 'collective'")
         self.group = group
+        self.transport = transport
         self._packed = None
         self._gathered = None
+        self._peer = None
+        self._out = None
+
+    def _buffers(self, q, R, D):
+        import torch
+        import torch.distributed as dist
+        if self._packed is None or self._packed.numel() != R * (D + 2) or \
+                self._packed.device != q.device:
+            world = dist.get_world_size(self.group)
+            self._packed = torch.empty(R * (D + 2), dtype=torch.float32, device=q.device)
+            if self.transport == "collective":
+                self._gathered = torch.empty(world * R * (D + 2), dtype=torch.float32,
+                                             device=q.device)
+            else:
+                if self._peer is not None:
+                    self._peer.close()
+                self._peer = PeerGroup(R, D, self.group)
+        if self._out is None or self._out.shape != (R, D) or self._out.dtype != q.dtype or \
+                self._out.device != q.device:
+            self._out = torch.empty(R, D, dtype=q.dtype, device=q.device)
 
     def step(self, q, keys, values, scale: float, stream=None):
+        """One decode step.  `stream`: a torch.cuda.Stream to run on (None:
+        the current stream); partial, exchange and merge are all issued on
+        it, in order.  Returns [B, Hq, 1, D] (a buffer reused by the next
+        step)."""
         import torch
         import torch.distributed as dist
         from . import sdpa
         B, Hq, _, D = q.shape
         R = B * Hq
-        if self._packed is None or self._packed.numel() != R * (D + 2) or \
-                self._packed.device != q.device:
-            world = dist.get_world_size(self.group)
-            self._packed = torch.empty(R * (D + 2), dtype=torch.float32, device=q.device)
-            self._gathered = torch.empty(world * R * (D + 2), dtype=torch.float32,
-                                         device=q.device)
-        sdpa.sdpa_decode_partial(q, keys, values, scale, packed_out=self._packed, stream=stream)
-        dist.all_gather_into_tensor(self._gathered, self._packed, group=self.group)
-        out = sdpa.sdpa_merge_packed(self._gathered.view(-1, R * (D + 2)), R, D, q.dtype,
-                                     stream=stream)
-        return out.view(B, Hq, 1, D)
+        self._buffers(q, R, D)
+        with _stream_ctx(stream):
+            cur = torch.cuda.current_stream(q.device)
+            sdpa.sdpa_decode_partial(q, keys, values, scale, packed_out=self._packed,
+                                     stream=cur.cuda_stream)
+            if self.transport == "peer":
+                self._peer.exchange_merge(self._packed, q.dtype, self._out, cur.cuda_stream)
+            else:
+                dist.all_gather_into_tensor(self._gathered, self._packed, group=self.group)
+                sdpa.sdpa_merge_packed(self._gathered.view(-1, R * (D + 2)), R, D, q.dtype,
+                                       out=self._out, stream=cur.cuda_stream)
+        return self._out.view(B, Hq, 1, D)
+
+    def check(self, stream=None):
+        """Raise if a peer exchange gave up waiting for a rank (peer transport)."""
+        if self._peer is not None:
+            self._peer.check(stream.cuda_stream if stream is not None else None)
+
+    def close(self):
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None

@@ -109,8 +109,24 @@ def ideal_sdpa(q_bits, kq, vq, scale, group_size, bits, dt, mask_mode=0, window=
     return out
 
 
+# (test name, max |diff| vs oracle, fraction of outputs beyond 2e-3, bar) per
+# parity check, printed in the terminal summary of the run (conftest.py)
+PARITY_LOG = []
+
+
+def record_parity(name, got_bits, want_bits, dt, bar):
+    """Log how far the kernel's outputs sit from the oracle's."""
+    g = bits_to_f32(got_bits, dt).astype(np.float64)
+    w = bits_to_f32(want_bits, dt).astype(np.float64)
+    d = np.abs(g - w)
+    m = float(d.max()) if d.size else 0.0
+    beyond = float((d > 2e-3).mean()) if d.size else 0.0
+    PARITY_LOG.append((name, m, beyond, bar))
+    return m, beyond
+
+
 def check_outlier_parity(got_bits, want_bits, ideal, dt, tol=2e-3, frac=0.9999, hard=1e-2,
-                         slack=5e-4):
+                         slack=5e-4, name=None):
     """Parity bar for inputs with key-outlier channels, where logits reach
     |s| ~ 30-50 and one fp16 ulp of a rounded logit (0.03) moves its
     probability by ~3%: any summation order different from the oracle's flips
@@ -120,9 +136,11 @@ def check_outlier_parity(got_bits, want_bits, ideal, dt, tol=2e-3, frac=0.9999, 
     g = bits_to_f32(got_bits, dt).astype(np.float64)
     w = bits_to_f32(want_bits, dt).astype(np.float64)
     d = np.abs(g - w)
-    assert (d <= tol).mean() >= frac, (d > tol).mean()
-    assert d.max() <= hard, d.max()
     e_ours = np.abs(g - ideal).max()
     e_ref = np.abs(w - ideal).max()
+    PARITY_LOG.append((name or "outlier-input case", float(d.max()), float((d > tol).mean()),
+                       f"outlier bar (kernel->f64 {e_ours:.2e}, oracle->f64 {e_ref:.2e})"))
+    assert (d <= tol).mean() >= frac, (d > tol).mean()
+    assert d.max() <= hard, d.max()
     assert e_ours <= e_ref + slack, (e_ours, e_ref)
     return d.max(), e_ours, e_ref

@@ -15,7 +15,7 @@ import numpy as np
 import pytest
 
 from helpers import BF16, F16, as_qtensor, check_outlier_parity, from_torch, ideal_sdpa, max_abs, \
-    quantized_inputs, to_torch_bits, upload_triple
+    quantized_inputs, record_parity, to_torch_bits, upload_triple
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -65,9 +65,11 @@ def test_decode_matches_oracle(case):
     got, want, (q, kq, vq, scale) = run_decode(B, Hq, Hkv, N, D, gs, bits, dt, k_outliers=outl,
                                                inputs=True)
     assert got.shape == want.shape
+    name = "decode " + "-".join(map(str, case))
     if outl:
-        check_outlier_parity(got, want, ideal_sdpa(q, kq, vq, scale, gs, bits, dt), dt)
+        check_outlier_parity(got, want, ideal_sdpa(q, kq, vq, scale, gs, bits, dt), dt, name=name)
     else:
+        record_parity(name, got, want, dt, f"<= {TOL[dt]}")
         err = max_abs(got, want, dt)
         assert err <= TOL[dt], err
     assert np.abs(O.from_dtype_bits(want, dt)).mean() > 1e-3
@@ -77,7 +79,8 @@ def test_decode_config2_full_size():
     """Config 2 at its full size: B 8, Hq 32, Hkv 8, D 128, N 8193, kv4, key outliers."""
     got, want, (q, kq, vq, scale) = run_decode(8, 32, 8, 8193, 128, 64, 4, F16, seed=2,
                                                k_outliers=4, inputs=True)
-    check_outlier_parity(got, want, ideal_sdpa(q, kq, vq, scale, 64, 4, F16), F16)
+    check_outlier_parity(got, want, ideal_sdpa(q, kq, vq, scale, 64, 4, F16), F16,
+                         name="decode config 2 full size (B8 Hq32 Hkv8 N8193 kv4, key outliers)")
 
 
 def test_decode_ragged_seq_lens():
@@ -154,10 +157,12 @@ def test_prefill_matches_oracle(case):
     V = as_qtensor(*upload_triple(*vq, gs, bits)[:3], N, gs, bits, dt)
     out = kvq.sdpa_prefill(to_torch_bits(q, dt), K, V, scale, kvq.Mask("causal", window))
     torch.cuda.synchronize()
+    name = "prefill " + "-".join(map(str, case))
     if outl:
         ideal = ideal_sdpa(q, kq, vq, scale, gs, bits, dt, mask_mode=1, window=window)
-        check_outlier_parity(from_torch(out, dt), want, ideal, dt)
+        check_outlier_parity(from_torch(out, dt), want, ideal, dt, name=name)
     else:
+        record_parity(name, from_torch(out, dt), want, dt, f"<= {TOL[dt]}")
         assert max_abs(from_torch(out, dt), want, dt) <= TOL[dt]
 
 

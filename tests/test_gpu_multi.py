@@ -1,10 +1,12 @@
 """Multi-GPU paths on real GPUs over NCCL (skipped with fewer than two GPUs).
 
-* Context split: one long sequence's keys are split into contiguous ranges,
+* Context split: one 131,072-key sequence is split into contiguous ranges,
   one per rank; each rank computes (m, l, o) partials of its range, the
-  partials are all-gathered over NCCL and merged.  Every rank's result must
+  partials move to every rank — over peer memory (the exchange kernel) or
+  through an NCCL all-gather — and are merged.  Every rank's result must
   match the single-GPU decode over all keys within the decode tolerance
-  (2e-3 on fp16 outputs), and rank 0's must match the oracle.
+  (2e-3 on fp16 outputs), in eager steps and in CUDA-graph replays, and
+  rank 0's must match the oracle.
 * Sharding by kv head: each rank decodes its own kv heads with no
   communication; the concatenated outputs must match the oracle.
 
@@ -45,41 +47,65 @@ def _setup(rank, world, port):
                             device_id=torch.device("cuda", rank))
 
 
-def _context_split_worker(rank, world, port, out_dir):
+def _context_split_worker(rank, world, port, out_dir, transport):
     _setup(rank, world, port)
     import torch
     import torch.distributed as dist
     import kvq
-    from helpers import F16, as_qtensor, from_torch, max_abs, quantized_inputs, to_torch_bits, \
-        upload_triple
+    from helpers import F16, from_torch, max_abs
     from kvq.parallel import ContextSplitDecode, context_ranges
     from oracle import oracle as O
+    split = None
     try:
-        B, Hq, Hkv, N, D, gs, bits = 1, 32, 8, 40000, 128, 64, 4
-        rng = np.random.default_rng(21)  # the same inputs on every rank
-        q, kq, vq = quantized_inputs(rng, B, Hq, Hkv, N, D, gs, bits, F16)
+        # the full-size sequence of config 5: 131,072 keys, drawn on the GPU
+        # from the same seed on every rank; rank r attends its own range
+        B, Hq, Hkv, N, D, gs, bits = 1, 32, 8, 131072, 128, 64, 4
+        g = torch.Generator(device="cuda")
+        g.manual_seed(61)
+        cache = kvq.QuantizedKVCache(gs, bits, reserve_rows=N)
+        for s0 in range(0, N, 8192):
+            k = torch.randn(B, Hkv, 8192, D, generator=g, device="cuda").half()
+            v = torch.randn(B, Hkv, 8192, D, generator=g, device="cuda").half()
+            Kf, Vf = cache.update_and_fetch_quantized(k, v)
+        q = torch.randn(B, Hq, 1, D, generator=g, device="cuda").half()
         scale = 1.0 / np.sqrt(D)
         a, b = context_ranges(N, world)[rank]
-        sk = tuple(np.ascontiguousarray(x[:, :, a:b]) for x in kq)
-        sv = tuple(np.ascontiguousarray(x[:, :, a:b]) for x in vq)
-        K = as_qtensor(*upload_triple(*sk, gs, bits)[:3], b - a, gs, bits, F16)
-        V = as_qtensor(*upload_triple(*sv, gs, bits)[:3], b - a, gs, bits, F16)
-        qt = to_torch_bits(q, F16)
-        split = ContextSplitDecode()
-        out = split.step(qt, K, V, scale)
-        out = split.step(qt, K, V, scale)  # second step reuses the gather buffers
+        K, V = Kf.slice_rows(a, b), Vf.slice_rows(a, b)
+        split = ContextSplitDecode(transport=transport)
+        outs = [split.step(q, K, V, scale).clone() for _ in range(2)]  # buffers reused
+        # the same step recorded once in a CUDA graph and replayed twice
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            gout = split.step(q, K, V, scale)
+        for _ in range(2):
+            graph.replay()
+            torch.cuda.synchronize()
+            outs.append(gout.clone())
+        split.check()
+        full = kvq.sdpa_decode(q, Kf, Vf, scale)
         torch.cuda.synchronize()
-        got = from_torch(out, F16)
-        Kf = as_qtensor(*upload_triple(*kq, gs, bits)[:3], N, gs, bits, F16)
-        Vf = as_qtensor(*upload_triple(*vq, gs, bits)[:3], N, gs, bits, F16)
-        full = from_torch(kvq.sdpa_decode(qt, Kf, Vf, scale), F16)
-        err_full = max_abs(got, full, F16)
+        errs = [max_abs(from_torch(o, F16), from_torch(full, F16), F16) for o in outs]
         err_oracle = -1.0
         if rank == 0:
-            want = O.sdpa_unfused(q, kq, vq, scale, gs, bits, F16)
-            err_oracle = max_abs(got, want, F16)
-        np.save(os.path.join(out_dir, f"ctx_{rank}.npy"), np.array([err_full, err_oracle]))
+            trip = []
+            for t in (Kf, Vf):
+                trip.append(tuple(
+                    x.contiguous().view(torch.int32 if x.dtype == torch.int32 else torch.int16)
+                    .cpu().numpy().view(np.uint32 if x.dtype == torch.int32 else np.uint16)
+                    for x in (t.packed, t.scales, t.biases)))
+            want = O.sdpa_unfused(from_torch(q, F16), trip[0], trip[1], scale, gs, bits, F16)
+            err_oracle = max_abs(from_torch(outs[-1], F16), want, F16)
+        same = all(torch.equal(outs[0], o) for o in outs[1:])
+        np.save(os.path.join(out_dir, f"ctx_{rank}.npy"),
+                np.array([max(errs), err_oracle, float(same)]))
+        del graph
+        torch.cuda.synchronize()
+        dist.barrier()
     finally:
+        if split is not None:
+            split.close()
         dist.destroy_process_group()
 
 
@@ -113,23 +139,28 @@ def _kv_head_shard_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def _spawn(fn, world, tmp_path):
+def _spawn(fn, world, tmp_path, *extra):
     import torch.multiprocessing as mp
-    mp.start_processes(fn, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(fn, args=(world, _free_port(), str(tmp_path)) + extra, nprocs=world,
+                       join=True, start_method="spawn")
 
 
-@pytest.mark.timeout(600)
-def test_context_split_nccl(tmp_path):
+@pytest.mark.timeout(900)
+@pytest.mark.parametrize("transport", ["peer", "collective"])
+def test_context_split_131072_keys(tmp_path, transport):
+    """Every rank's output equals the one-GPU decode over all keys (2e-3) in
+    eager steps and in graph replays, identically across steps; rank 0's
+    equals the oracle's."""
     import torch
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs two or more GPUs")
     world = min(world, 8)
-    _spawn(_context_split_worker, world, tmp_path)
+    _spawn(_context_split_worker, world, tmp_path, transport)
     for r in range(world):
-        err_full, err_oracle = np.load(tmp_path / f"ctx_{r}.npy")
+        err_full, err_oracle, same = np.load(tmp_path / f"ctx_{r}.npy")
         assert err_full <= TOL, (r, err_full)
+        assert same == 1.0, r
         if r == 0:
             assert err_oracle <= TOL, err_oracle
 

@@ -1,13 +1,18 @@
 """kvq_sdpa_decode_noalloc against kvq_sdpa_decode, through the C ABI.
 
-The no-allocation decode exists for callers that must not allocate device
-memory (work recorded inside an open CUDA stream capture, serving processes
-that own all device memory): its scratch is a fixed array inside libkvq.
-These tests call it twice in a row on different inputs — the second call
-finds the first call's leftovers in that shared scratch — and require each
-result to match kvq_sdpa_decode on the same inputs within the decode
-tolerance (2e-3 on fp16 outputs).  They also check that shapes needing more
-scratch than the array holds are refused with KVQ_ERR_WORKSPACE.
+The no-allocation decode exists for callers that cannot have device memory
+allocated on their behalf: serving processes whose own pool took all free
+device memory at start-up, and latency-bound decode loops that must never
+meet a cudaMalloc's implicit device synchronization.  Its scratch is a fixed
+array inside libkvq.  These tests call it twice in a row on different
+inputs — the second call finds the first call's leftovers in that shared
+scratch — and require each result to match kvq_sdpa_decode on the same
+inputs within the decode tolerance (2e-3 on fp16 outputs).  They also check
+that shapes needing more scratch than the array holds are refused with
+KVQ_ERR_WORKSPACE, that a query the balanced kernel cannot take (not 16-byte
+aligned) still fits by running without a key split, and that a raised device
+error flag in the scratch survives later calls until kvq_check_device
+reports it.
 
 This file is collected last, so a run that stops at the first failure has
 already run every other test; it also passes on its own in a fresh process.
@@ -73,3 +78,41 @@ def test_noalloc_refuses_shapes_beyond_its_scratch():
     assert "kvq_sdpa_decode_noalloc" in msg and "bytes" in msg
     torch.cuda.synchronize()
     assert not out.any()
+
+
+def test_noalloc_unaligned_query_runs_without_key_split():
+    """A q that is not 16-byte aligned takes the split kernel; at this shape
+    its split partials exceed the scratch, so the call runs unsplit."""
+    import torch
+    import kvq
+    from kvq import _lib
+    q0, K, V = _inputs(14, 1, 8, 4, 32768, 256, 64, 8)
+    buf = torch.zeros(q0.numel() + 8, dtype=q0.dtype, device=q0.device)
+    q = buf[1:1 + q0.numel()].view(q0.shape)  # 2 bytes past a 16-byte boundary
+    q.copy_(q0)
+    assert q.data_ptr() % 16 == 2
+    want = kvq.sdpa_decode(q, K, V, 0.0625)
+    for _ in range(2):
+        got = torch.empty_like(q0)
+        _lib.check(_noalloc(q, K, V, 0.0625, got))
+        torch.cuda.synchronize()
+        err = max_abs(from_torch(got, F16), from_torch(want, F16), F16)
+        assert err <= TOL, err
+
+
+def test_noalloc_error_flag_kept_until_reported():
+    """A raised error flag in the scratch is not cleared by the next call;
+    kvq_check_device(NULL) reports it once and clears it."""
+    import torch
+    from kvq import _lib
+    L = _lib.lib()
+    q, K, V = _inputs(15, 1, 16, 4, 1024, 128, 64, 8)
+    out = torch.empty_like(q)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(_noalloc(q, K, V, 0.088, out))  # looks the scratch address up
+    _lib.check(L.kvq_check_device(None, st))   # nothing raised so far
+    _lib.check(L.kvq_debug_raise_flag(None, st))
+    _lib.check(_noalloc(q, K, V, 0.088, out))  # must leave the flag raised
+    assert L.kvq_check_device(None, st) == _lib.ERR_CUDA
+    assert "error flag" in L.kvq_last_error().decode()
+    _lib.check(L.kvq_check_device(None, st))   # reported once, then clear
