@@ -1,33 +1,47 @@
 #!/usr/bin/env python
-"""Benchmark of the quantized-KV decode hot path (BASELINE config 2).
+"""Benchmark of the quantized-KV decode hot path.
 
-One step = one attention layer of batched kv4 decode: quantize-on-append of
-one new K/V row per sequence into the layer's cache, then flash-decoding SDPA
-of 32 query heads (8 kv heads, GQA 4) over the 8193-row cache, for B = 8
-sequences (D 128, group 64, fp16, keys with 4 outlier channels x8).  Steps
-cycle through NL distinct layer caches whose total size (NL x 75.5 MB)
-exceeds twice the 126 MB L2, so every step streams its K/V from HBM; after
-each step the layer is trimmed by one token (host bookkeeping only) so every
-step does identical work.
+The line the driver reads (default `--workload decode`), at N = 1, 2, 4, 8
+GPUs (one process per GPU, torchrun for N > 1):
 
-value      aggregate algorithmic HBM GB/s over all ranks (K/V packed codes +
-           scales + biases of 8193 rows, q, output, appended rows) for K steps
-           replayed from CUDA graphs, timed with CUDA events, max over ranks.
-e2e        the same metric through the public Python API per step, with the
-           step's q and new K/V rows copied from pinned host memory and the
-           output copied back inside the timed region.
-roofline   the decode kernel alone: algorithmic bytes per launch / its mean
-           CUDA-event duration inside the timed graphs, against the measured
-           HBM copy bandwidth.
+value      config 5, long-context serving: B = 64 sequences with ragged
+           lengths U[1024, 32768] (numpy seed 5), Hq 32, Hkv 8, D 128, kv4
+           group 64, decoded with per-sequence key counts (seq_lens).  The 8
+           kv heads are sharded over the N GPUs (8/N each, with their GQA
+           query heads): strong scaling, no collective on the data path.
+           One step = one decode of all 64 sequences on every rank; steps
+           cycle through NL distinct layer caches (more than 3x the 126 MB
+           L2 per GPU), replayed from one CUDA graph per layer, timed with
+           CUDA events over exactly K steps, max over ranks.  Aggregate
+           algorithmic HBM GB/s = K/V codes + scales + biases of every
+           sequence's keys, plus q and output, over all ranks.
+e2e        the same step through the public Python API (kvq.sdpa_decode with
+           seq_lens), with each step's q copied from pinned host memory and
+           the output copied back inside the timed region.
+roofline   the decode launch pair of one rank (attn_bal_kernel +
+           attn_bal_merge_kernel, the whole step): its algorithmic bytes per
+           launch / its CUDA-event time, against the measured HBM copy
+           bandwidth.
+config2    nested: batched kv4 decode with quantize-on-append (B 8, Hq 32,
+           Hkv 8, D 128, 8,193 keys, key outliers), one replica per GPU,
+           with its own decode roofline (a CUDA graph per pass over the
+           layers).
+context_split
+           nested: one 131,072-key sequence split along the context over the
+           N ranks, partials exchanged over peer memory and merged (a CUDA
+           graph per pass over the layers), us per step and the exchange's
+           share of it.
 cpu_baseline / --impl reference
-           the CPU oracle (C restatement of mlx-bun's unfused op graph, all
-           host threads) on a bounded sample of the same workload.
+           the CPU oracle (C restatement of mlx-bun's unfused op graph) with
+           every host core, on a bounded sample of config 5's (sequence, kv
+           head) pairs.
 
-Multi-GPU (torchrun): each rank owns its own shard of sequences (weak
-scaling, no communication on the data path).
+Other workloads print their own line: `--workload prefill` (config 4,
+tensor-core chunked prefill), `config1` and `config3`.
 """
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -40,28 +54,34 @@ for _p in (ROOT, PKG):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-CFG = dict(B=8, Hq=32, Hkv=8, D=128, N_prior=8192, bits=4, gs=64, outliers=4)
-METRIC = "quantized-KV decode SDPA achieved HBM GB/s (config 2: B8 Hq32 Hkv8 D128 N8193 kv4 gs64, append+decode per step)"
-UNIT = "GB/s"
-WORKLOAD = "config2-kv4-decode-append"
+L2_BYTES = 126e6
 FALLBACK_HBM = 6650.0
+UNIT = "GB/s"
+
+CFG5 = dict(B=64, Hq=32, Hkv=8, D=128, bits=4, gs=64, lo=1024, hi=32768, seed=5)
+METRIC = ("quantized-KV decode SDPA achieved HBM GB/s (config 5: B64 ragged lengths "
+          "U[1024, 32768], Hq32 Hkv8 D128 kv4 gs64, kv heads sharded over the GPUs)")
+WORKLOAD = "config5-kv4-ragged-decode-kvhead-shards"
+
+CFG2 = dict(B=8, Hq=32, Hkv=8, D=128, N_prior=8192, bits=4, gs=64, outliers=4)
 
 
 def kv_row_bytes(c):
+    """K and V bytes of one key row of one kv head: codes + scales + biases."""
     return 2 * (c["D"] * c["bits"] // 8 + 2 * (c["D"] // c["gs"]) * 2)
 
 
-def step_bytes(c):
-    N = c["N_prior"] + 1
-    kv = c["B"] * c["Hkv"] * N * kv_row_bytes(c)
-    q = c["B"] * c["Hq"] * c["D"] * 2
-    app = c["B"] * c["Hkv"] * c["D"] * 2 * 2
-    return kv + 2 * q + app
+def config5_lens():
+    import numpy as np
+    c = CFG5
+    return np.random.default_rng(c["seed"]).integers(c["lo"], c["hi"] + 1, size=c["B"])
 
 
-def decode_launch_bytes(c):
-    N = c["N_prior"] + 1
-    return c["B"] * c["Hkv"] * N * kv_row_bytes(c) + 2 * c["B"] * c["Hq"] * c["D"] * 2
+def config5_rank_bytes(lens, hk):
+    """Algorithmic bytes of one decode step on a rank owning `hk` kv heads."""
+    c = CFG5
+    nrep = c["Hq"] // c["Hkv"]
+    return int(lens.sum()) * hk * kv_row_bytes(c) + 2 * c["B"] * hk * nrep * c["D"] * 2
 
 
 def peaks():
@@ -73,14 +93,20 @@ def peaks():
         return FALLBACK_HBM, "fallback"
 
 
-def traffic_from_profiles():
-    """dram bytes of the decode's attention launch from the committed ncu summary
-    (the merge reads the partials from L2), or None."""
-    p = os.path.join(ROOT, "profiles", "attn_decode_config2.md")
+def host_cores():
     try:
-        for line in open(p):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                return int(line.split(":")[1].strip().split()[0])
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def traffic_ratio(name):
+    """DRAM bytes per algorithmic byte of a decode launch, from the committed
+    ncu summary profiles/<name> ("traffic_ratio:" line), or None."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", name)):
+            if line.strip().startswith("traffic_ratio:"):
+                return float(line.split(":")[1].split()[0])
     except Exception:
         pass
     return None
@@ -131,64 +157,253 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
+class Timed:
+    """Barrier + synchronize on both sides of a CUDA-event-timed region on
+    `stream`; `ms` is the maximum over ranks."""
+
+    def __init__(self, stream, world, device, clocks=None):
+        import torch
+        self.stream, self.world, self.device, self.clocks = stream, world, device, clocks
+        self.e0 = torch.cuda.Event(enable_timing=True)
+        self.e1 = torch.cuda.Event(enable_timing=True)
+        self.clk = None
+        self.ms = None
+
+    def __enter__(self):
+        import torch
+        import torch.distributed as dist
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        if self.clocks:
+            self.clocks.start()
+            time.sleep(0.1)
+        self.e0.record(self.stream)
+        return self
+
+    def __exit__(self, *exc):
+        import torch
+        import torch.distributed as dist
+        self.e1.record(self.stream)
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier()
+        if self.clocks:
+            self.clk = self.clocks.stop()
+        t = torch.tensor([self.e0.elapsed_time(self.e1)], device=self.device, dtype=torch.float64)
+        if self.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        self.ms = float(t.item())
+        return False
+
+
 # ------------------------------------------------------------ CPU oracle --
 
-def cpu_oracle_sample(K_steps, budget_s, seed=0):
-    """Time the C oracle on (sequence, kv-head) pairs of config 2.
-
-    Returns (GB/s, threads, description).  Each timed call covers `pairs`
-    of the 64 (b, kv-head) pairs of one step (N = 8193 rows, 4 query heads
-    each), sized so K_steps calls take about `budget_s` seconds."""
+def cpu_oracle_config5(max_calls, budget_s, threads, seed=0):
+    """Time the C oracle on (sequence, kv-head) pairs of config 5 with
+    `threads` OpenMP threads.  One call covers `threads` pairs (the first
+    `threads` sequences' lengths, one kv head and its 4 query heads each);
+    at most `max_calls` calls and about `budget_s` seconds are timed.
+    Returns (GB/s, description, calls, seconds)."""
     import numpy as np
     from oracle import oracle as O
-    c = CFG
-    N, D, nrep = c["N_prior"] + 1, c["D"], c["Hq"] // c["Hkv"]
+    c = CFG5
+    D, nrep = c["D"], c["Hq"] // c["Hkv"]
+    lens = config5_lens()
+    P = max(1, threads)
+    sl = np.array([int(lens[i % len(lens)]) for i in range(P)], np.int32)
+    Nmax = int(sl.max())
     rng = np.random.default_rng(seed)
-    k = rng.standard_normal((1, 1, N, D)).astype(np.float32)
-    k[..., :c["outliers"]] *= 8.0
-    kb = O.to_dtype_bits(k, O.F16)
-    vb = O.to_dtype_bits(rng.standard_normal((1, 1, N, D)).astype(np.float32), O.F16)
+    kb = O.to_dtype_bits(rng.standard_normal((1, 1, Nmax, D)).astype(np.float32), O.F16)
+    vb = O.to_dtype_bits(rng.standard_normal((1, 1, Nmax, D)).astype(np.float32), O.F16)
     kq = O.quantize(kb, c["gs"], c["bits"], O.F16)
     vq = O.quantize(vb, c["gs"], c["bits"], O.F16)
-    threads = O.max_threads()
-    # one pair per thread per call: [threads, 1, N, *] replicated pair data
-    P = max(1, threads)
     kqP = tuple(np.ascontiguousarray(np.broadcast_to(a, (P,) + a.shape[1:])) for a in kq)
     vqP = tuple(np.ascontiguousarray(np.broadcast_to(a, (P,) + a.shape[1:])) for a in vq)
     q = O.to_dtype_bits(rng.standard_normal((P, nrep, 1, D)).astype(np.float32), O.F16)
     scale = 1.0 / np.sqrt(D)
-    O.sdpa_unfused(q, kqP, vqP, scale, c["gs"], c["bits"], O.F16)  # warm
+
+    def call():
+        O.sdpa_unfused(q, kqP, vqP, scale, c["gs"], c["bits"], O.F16, seq_lens=sl,
+                       threads=threads)
+
+    call()  # warm
     t0 = time.perf_counter()
-    O.sdpa_unfused(q, kqP, vqP, scale, c["gs"], c["bits"], O.F16)
+    call()
     t_call = time.perf_counter() - t0
-    # time at most K_steps calls, and no more than budget_s of work
-    steps = max(1, min(K_steps, int(budget_s / max(t_call, 1e-6))))
+    calls = max(1, min(max_calls, int(budget_s / max(t_call, 1e-6))))
     t0 = time.perf_counter()
-    for _ in range(steps):
-        O.sdpa_unfused(q, kqP, vqP, scale, c["gs"], c["bits"], O.F16)
+    for _ in range(calls):
+        call()
     el = time.perf_counter() - t0
-    pairs = P * steps
-    by = pairs * (N * kv_row_bytes(c) + 2 * nrep * D * 2)
-    desc = (f"{pairs} (sequence, kv-head) pairs of config 2 (N=8193, 4 query heads each, "
-            f"{pairs / 64:.2f} layer-steps), C oracle of the unfused op graph, {threads} threads")
-    return by / el / 1e9, threads, desc, el
+    by = calls * (int(sl.sum()) * kv_row_bytes(c) + 2 * P * nrep * D * 2)
+    desc = (f"{calls} calls x {P} (sequence, kv-head) pairs of config 5 (the first {P} "
+            f"sequences' lengths, mean {sl.mean():.0f} keys, 4 query heads each), C oracle of "
+            f"the unfused op graph, {threads} threads")
+    return by / el / 1e9, desc, calls, el
 
 
-# ------------------------------------------------------------- GPU arm --
+# ------------------------------------------------------- config 5 (main) --
 
-def setup_layers(c, NL, device, seed):
+def _fill(cache, B, H, N, D, g, device, chunk):
+    """Append N seeded fp16 rows to `cache` in chunks; return the last views."""
+    import torch
+    views = None
+    for s0 in range(0, N, chunk):
+        S = min(chunk, N - s0)
+        k = torch.randn(B, H, S, D, generator=g, device=device).half()
+        v = torch.randn(B, H, S, D, generator=g, device=device).half()
+        views = cache.update_and_fetch_quantized(k, v)
+        del k, v
+    return views
+
+
+def run_config5(args, rank, world, local_rank):
+    import numpy as np
     import torch
     import kvq
+    c = CFG5
+    B, Hq, Hkv, D = c["B"], c["Hq"], c["Hkv"], c["D"]
+    if Hkv % world:
+        raise SystemExit("config 5 shards 8 kv heads: run on 1, 2, 4 or 8 GPUs")
+    device = torch.device("cuda", local_rank)
+    hk = Hkv // world
+    nrep = Hq // Hkv
+    scale = 1.0 / np.sqrt(D)
+    lens = config5_lens()
+    Nmax = int(lens.max())
+    rank_bytes = config5_rank_bytes(lens, hk)
+    total_bytes = config5_rank_bytes(lens, Hkv)
+    NL = min(16, max(2, math.ceil(3 * L2_BYTES / rank_bytes)))
     g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    B, Hq, Hkv, D, Np = c["B"], c["Hq"], c["Hkv"], c["D"], c["N_prior"]
-    reserve = (Np + 1 + 255) // 256 * 256
+    g.manual_seed(5000 + rank)
+    sl = torch.tensor(lens, dtype=torch.int32, device=device)
     layers = []
     for _ in range(NL):
-        cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=reserve)
-        k = torch.randn(B, Hkv, Np, D, generator=g, device=device, dtype=torch.float32)
+        cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=(Nmax + 255) // 256 * 256)
+        K, V = _fill(cache, B, hk, Nmax, D, g, device, 2048)
+        q = torch.randn(B, hk * nrep, 1, D, generator=g, device=device).half()
+        layers.append(dict(cache=cache, K=K, V=V, q=q, out=torch.empty_like(q)))
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(device)
+
+    def step(Ly):
+        kvq.sdpa_decode(Ly["q"], Ly["K"], Ly["V"], scale, seq_lens=sl, out=Ly["out"])
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(layers[i % NL])
+    stream.synchronize()
+    graphs = []
+    for Ly in layers:
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            step(Ly)
+        graphs.append(gr)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            graphs[i % NL].replay()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    with torch.cuda.stream(stream):
+        with Timed(stream, world, device, Clocks(local_rank) if rank == 0 else None) as tm:
+            for i in range(K):
+                graphs[i % NL].replay()
+    ms = tm.ms
+
+    # e2e through the public API, host buffers, copies inside the timed region
+    hq = [torch.empty_like(Ly["q"], device="cpu").pin_memory() for Ly in layers]
+    ho = [torch.empty_like(Ly["q"], device="cpu").pin_memory() for Ly in layers]
+    for j, Ly in enumerate(layers):
+        hq[j].copy_(Ly["q"])
+    K2 = min(K, 200)
+    with torch.cuda.stream(stream):
+        with Timed(stream, world, device) as te:
+            for i in range(K2):
+                j = i % NL
+                Ly = layers[j]
+                Ly["q"].copy_(hq[j], non_blocking=True)
+                step(Ly)
+                ho[j].copy_(Ly["out"], non_blocking=True)
+    e2e_ms = te.ms
+    if not torch.isfinite(layers[0]["out"].float()).all():
+        raise RuntimeError("non-finite decode output")
+    del graphs
+
+    value = total_bytes * K / (ms / 1e3) / 1e9
+    kern_s = ms / 1e3 / K
+    achieved = rank_bytes / kern_s / 1e9
+    peak, peak_kind = peaks()
+    ratio = traffic_ratio("attn_decode_config5.md")
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": K, "warmup": args.warmup, "ms_per_step": round(ms / K, 5),
+        "us_per_step": round(1e3 * ms / K, 3),
+        "tokens_per_s": round(B * K / (ms / 1e3), 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "u4 codes/f16",
+        "data": "synthetic (seeded torch.randn K/V/q; lengths numpy PCG64 seed 5)",
+        "config": {"workload": WORKLOAD, "batch": B, "Hq": Hq, "Hkv": Hkv, "head_dim": D,
+                   "bits": c["bits"], "group_size": c["gs"],
+                   "lengths": f"U[{c['lo']}, {c['hi']}] seed {c['seed']}, sum {int(lens.sum())}",
+                   "parallelism": f"kv-head shards: {hk} kv head(s) x 64 sequences per GPU, "
+                                  f"{world} GPU(s), no collective",
+                   "layers_cycled": NL,
+                   "l2": f"inputs larger than L2: {NL} distinct layer caches, "
+                         f"{NL * rank_bytes / 1e6:.0f} MB per GPU cycled",
+                   "timing": "one CUDA graph per layer, exactly K replays, CUDA events, "
+                             "barrier + synchronize on both sides, max over ranks"},
+        "bytes_per_step": total_bytes,
+        "e2e": {"value": round(total_bytes * K2 / (e2e_ms / 1e3) / 1e9, 1), "unit": UNIT,
+                "h2d_bytes_per_step": int(hq[0].numel() * 2) * world,
+                "d2h_bytes_per_step": int(ho[0].numel() * 2) * world,
+                "us_per_step": round(1e3 * e2e_ms / K2, 3), "steps": K2,
+                "path": "kvq.sdpa_decode per step (eager), q from pinned host memory, output "
+                        "back to pinned host memory, every rank"},
+        "gpu_launches": 2 * K,  # per step: attn_bal_kernel + attn_bal_merge_kernel
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "kernel": "decode = attn_bal_kernel<4,128,64,1> (seq_lens) + "
+                               "attn_bal_merge_kernel",
+                     "kernel_us": round(kern_s * 1e6, 3), "bytes_per_launch": rank_bytes,
+                     "traffic": int(ratio * rank_bytes) if ratio else None,
+                     "traffic_note": "ncu DRAM bytes per algorithmic byte of a 16-sequence "
+                                     "capture, scaled to this launch",
+                     "timing": "CUDA events over the K timed graph replays (the step is the "
+                               "decode launch pair), max over ranks"},
+        "clocks": tm.clk,
+    }
+    for Ly in layers:
+        Ly["cache"].dispose()
+    return res
+
+
+# -------------------------------------------------- config 2 (nested) --
+
+def run_config2(args, rank, world, local_rank):
+    """Batched kv4 decode with quantize-on-append, one replica per GPU."""
+    import numpy as np
+    import torch
+    import kvq
+    c = CFG2
+    device = torch.device("cuda", local_rank)
+    B, Hq, Hkv, D, Np = c["B"], c["Hq"], c["Hkv"], c["D"], c["N_prior"]
+    scale = 1.0 / np.sqrt(D)
+    N = Np + 1
+    layer_bytes = B * Hkv * N * kv_row_bytes(c)
+    step_bytes = layer_bytes + 2 * B * Hq * D * 2 + B * Hkv * D * 2 * 2
+    launch_bytes = layer_bytes + 2 * B * Hq * D * 2
+    NL = max(4, math.ceil(3 * L2_BYTES / layer_bytes))
+    g = torch.Generator(device=device)
+    g.manual_seed(1000 + rank)
+    layers = []
+    for _ in range(NL):
+        cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=(N + 255) // 256 * 256)
+        k = torch.randn(B, Hkv, Np, D, generator=g, device=device)
         k[..., :c["outliers"]] *= 8.0
-        v = torch.randn(B, Hkv, Np, D, generator=g, device=device, dtype=torch.float32)
+        v = torch.randn(B, Hkv, Np, D, generator=g, device=device)
         cache.update_and_fetch_quantized(k.half(), v.half())
         del k, v
         kn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
@@ -197,173 +412,169 @@ def setup_layers(c, NL, device, seed):
         q = torch.randn(B, Hq, 1, D, generator=g, device=device).half()
         layers.append(dict(cache=cache, kn=kn, vn=vn, q=q, out=torch.empty_like(q)))
     torch.cuda.synchronize()
-    return layers
+    stream = torch.cuda.Stream(device)
+
+    def step(L):
+        qk, qv = L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])
+        kvq.sdpa_decode(L["q"], qk, qv, scale, out=L["out"])
+        L["cache"].trim(1)  # host bookkeeping: every replay does the same work
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(layers[i % NL])
+    stream.synchronize()
+    # one graph per pass over the layers (a replay is NL steps), and a
+    # decode-only graph of the same layers (the roofline's kernel time)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for L in layers:
+            step(L)
+    views = []
+    for L in layers:
+        views.append(L["cache"].update_and_fetch_quantized(L["kn"], L["vn"]))
+    dec = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(dec, stream=stream):
+        for L, (qk, qv) in zip(layers, views):
+            kvq.sdpa_decode(L["q"], qk, qv, scale, out=L["out"])
+    for L in layers:
+        L["cache"].trim(1)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
+            dec.replay()
+    torch.cuda.synchronize()
+    reps = max(1, math.ceil(args.steps / NL))
+    K = reps * NL
+    with torch.cuda.stream(stream):
+        with Timed(stream, world, device) as t1:
+            for _ in range(reps):
+                graph.replay()
+        with Timed(stream, world, device) as t2:
+            for _ in range(reps):
+                dec.replay()
+    kern_s = t2.ms / 1e3 / K
+    achieved = launch_bytes / kern_s / 1e9
+    peak, peak_kind = peaks()
+    ratio = traffic_ratio("attn_decode_config2.md")
+    out = {
+        "workload": "config2-kv4-decode-append: B8 Hq32 Hkv8 D128, 8192 prior keys + 1 appended "
+                    "per step, kv4 gs64, key outliers; one replica per GPU (weak)",
+        "value": round(world * step_bytes * K / (t1.ms / 1e3) / 1e9, 1), "unit": UNIT,
+        "steps": K, "us_per_step": round(1e3 * t1.ms / K, 3), "bytes_per_step": step_bytes,
+        "layers_cycled": NL, "timing": "a CUDA graph per pass over the layers, CUDA events",
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "kernel": "decode = attn_bal_kernel<4,128,64,1> + attn_bal_merge_kernel",
+                     "kernel_us": round(kern_s * 1e6, 3), "bytes_per_launch": launch_bytes,
+                     "traffic": int(ratio * launch_bytes) if ratio else None,
+                     "timing": "decode-only graph replays of the same layers, CUDA events"},
+    }
+    del graph, dec
+    for L in layers:
+        L["cache"].dispose()
+    return out
 
 
-def gpu_step(L, scale):
-    import kvq
-    qk, qv = L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])
-    kvq.sdpa_decode(L["q"], qk, qv, scale, out=L["out"])
-    L["cache"].trim(1)
+# ------------------------------------------- context split (nested) --
 
-
-def run_gpu(args, rank, world, local_rank):
+def run_context_split(args, rank, world, local_rank):
+    """Config 5's single 131,072-key sequence split along the context."""
     import numpy as np
     import torch
     import torch.distributed as dist
     import kvq
-
+    from kvq.parallel import ContextSplitDecode, context_ranges
+    Hq, Hkv, D, bits, gs, N = 32, 8, 128, 4, 64, 131072
+    c = dict(D=D, bits=bits, gs=gs)
     device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    c = CFG
-    scale = 1.0 / np.sqrt(c["D"])
-    layer_bytes = c["B"] * c["Hkv"] * (c["N_prior"] + 1) * kv_row_bytes(c)
-    NL = max(4, int(np.ceil(2 * 126e6 * 1.5 / layer_bytes)))
-    layers = setup_layers(c, NL, device, seed=1000 + rank)
+    scale = 1.0 / np.sqrt(D)
+    a, b = context_ranges(N, world)[rank]
+    rank_bytes = (b - a) * Hkv * kv_row_bytes(c) + 2 * Hq * D * 2
+    NL = min(32, max(2, math.ceil(3 * L2_BYTES / rank_bytes)))
+    g = torch.Generator(device=device)
+    g.manual_seed(7000 + rank)
+    gq = torch.Generator(device=device)
+    gq.manual_seed(77)  # the same queries on every rank
+    layers = []
+    for _ in range(NL):
+        cache = kvq.QuantizedKVCache(gs, bits, reserve_rows=(b - a + 255) // 256 * 256)
+        K, V = _fill(cache, 1, Hkv, b - a, D, g, device, 8192)
+        q = torch.randn(1, Hq, 1, D, generator=gq, device=device).half()
+        layers.append(dict(cache=cache, K=K, V=V, q=q, out=torch.empty_like(q)))
+    torch.cuda.synchronize()
     stream = torch.cuda.Stream(device)
-    # warm-up (also sizes the library-managed workspace before capture)
+    split = ContextSplitDecode(transport="peer") if world > 1 else None
+    R = Hq
+    packed = torch.empty(R * (D + 2), dtype=torch.float32, device=device)
+
+    def step(Ly):
+        if split is None:
+            kvq.sdpa_decode(Ly["q"], Ly["K"], Ly["V"], scale, out=Ly["out"])
+        else:
+            Ly["out"].copy_(split.step(Ly["q"], Ly["K"], Ly["V"], scale))
+
+    def partial_only(Ly):
+        kvq.sdpa_decode_partial(Ly["q"], Ly["K"], Ly["V"], scale, packed_out=packed)
+
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
-            gpu_step(layers[i % NL], scale)
+            step(layers[i % NL])
     stream.synchronize()
-
-    # ---- graphs: one replay = NL steps (one pass over the layers)
-    per_graph = NL
+    # one graph per pass over the layers (a replay is NL steps); the same
+    # pass with the partial decode alone, for the exchange's share
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for j in range(per_graph):
-            gpu_step(layers[j], scale)
-    # decode-only graph over the same layers (kernel timing for the roofline)
-    views = []
-    for L in layers:
-        L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])  # leave row 8192 written
-        views.append(L["cache"].fetch())
-    g_dec = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_dec, stream=stream):
-        for j in range(per_graph):
-            kvq.sdpa_decode(layers[j]["q"], views[j][0], views[j][1], scale, out=layers[j]["out"])
-    for L in layers:
-        L["cache"].trim(1)
-    for _ in range(3):
-        graph.replay()
-        g_dec.replay()
-    torch.cuda.synchronize()
-
-    K = args.steps
-    reps = max(1, (K + per_graph - 1) // per_graph)
-    K = reps * per_graph
-    clocks = Clocks(local_rank) if rank == 0 else None
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    if clocks:
-        clocks.start()
-        time.sleep(0.1)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for Ly in layers:
+            step(Ly)
+    pgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(pgraph, stream=stream):
+        for Ly in layers:
+            partial_only(Ly)
     with torch.cuda.stream(stream):
-        e0.record()
-        for r in range(reps):
+        for _ in range(3):
             graph.replay()
-        e1.record()
-        # the decode kernel alone, same layers, same stream, right after
-        e2.record()
-        for r in range(reps):
-            g_dec.replay()
-        e3.record()
+            pgraph.replay()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop() if clocks else None
-    ms = e0.elapsed_time(e1)
-    kern_ms = [e2.elapsed_time(e3) / (reps * per_graph)]
-    t = torch.tensor([ms], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-
-    # ---- e2e through the public API with host buffers
-    import kvq as _k  # noqa: F401
-    hq = [torch.empty_like(L["q"], device="cpu").pin_memory() for L in layers]
-    hk = [torch.empty_like(L["kn"], device="cpu").pin_memory() for L in layers]
-    hv = [torch.empty_like(L["vn"], device="cpu").pin_memory() for L in layers]
-    ho = [torch.empty_like(L["q"], device="cpu").pin_memory() for L in layers]
-    for j, L in enumerate(layers):
-        hq[j].copy_(L["q"])
-        hk[j].copy_(L["kn"])
-        hv[j].copy_(L["vn"])
-    K2 = min(K, max(200, NL * 50))
-    K2 = (K2 + NL - 1) // NL * NL
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, math.ceil(args.steps / NL))
+    K = reps * NL
     with torch.cuda.stream(stream):
-        f0.record()
-        for i in range(K2):
-            j = i % NL
-            L = layers[j]
-            L["q"].copy_(hq[j], non_blocking=True)
-            L["kn"].copy_(hk[j], non_blocking=True)
-            L["vn"].copy_(hv[j], non_blocking=True)
-            qk, qv = L["cache"].update_and_fetch_quantized(L["kn"], L["vn"])
-            kvq.sdpa_decode(L["q"], qk, qv, scale, out=L["out"])
-            L["cache"].trim(1)
-            ho[j].copy_(L["out"], non_blocking=True)
-        f1.record()
-    torch.cuda.synchronize()
-    e2e_ms = f0.elapsed_time(f1)
-    t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t.item())
-
-    # sanity: the benchmarked output is finite
+        with Timed(stream, world, device) as t1:
+            for _ in range(reps):
+                graph.replay()
+        with Timed(stream, world, device) as t2:
+            for _ in range(reps):
+                pgraph.replay()
+    if split is not None:
+        split.check(stream)
     if not torch.isfinite(layers[0]["out"].float()).all():
-        raise RuntimeError("non-finite decode output")
+        raise RuntimeError("non-finite context-split output")
+    del graph, pgraph
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # every rank's last exchange is done before the buffers go
+    if split is not None:
+        split.close()
+    for Ly in layers:
+        Ly["cache"].dispose()
+    total = N * Hkv * kv_row_bytes(c) + 2 * Hq * D * 2 * world
+    us = 1e3 * t1.ms / K
+    out = {
+        "workload": "one 131072-key sequence, Hq32 Hkv8 D128 kv4 gs64, split along the context "
+                    f"over {world} GPU(s); partials exchanged over peer memory (CUDA IPC, "
+                    "plain stores + flags) and merged in one kernel; a CUDA graph per pass "
+                    "over the layers",
+        "us_per_step": round(us, 3), "value": round(total * K / (t1.ms / 1e3) / 1e9, 1),
+        "unit": UNIT, "steps": K, "layers_cycled": NL,
+        "partial_us_per_step": round(1e3 * t2.ms / K, 3),
+    }
+    if world > 1:
+        out["exchange_share"] = round(max(0.0, 1.0 - t2.ms / t1.ms), 4)
+        out["exchange_note"] = ("share of the step not spent in the partial decode: the "
+                                "exchange-and-merge kernel and its wait for the slowest rank")
+    return out
 
-    sb = step_bytes(c)
-    value = world * sb * K / (ms_max / 1e3) / 1e9
-    e2e_value = world * sb * K2 / (e2e_ms / 1e3) / 1e9
-    kmean = sum(kern_ms) / len(kern_ms)
-    achieved = decode_launch_bytes(c) / (kmean / 1e3) / 1e9
-    peak, peak_kind = peaks()
-    res = None
-    if rank == 0:
-        res = {
-            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
-            "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5),
-            "us_per_step": round(1e3 * ms_max / K, 3),
-            "tokens_per_s": round(world * c["B"] * K / (ms_max / 1e3), 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes/f16",
-            "data": "synthetic (seeded torch.randn; keys with 4 outlier channels x8)",
-            "config": {"workload": WORKLOAD, "B_per_gpu": c["B"], "Hq": c["Hq"], "Hkv": c["Hkv"],
-                       "head_dim": c["D"], "context": c["N_prior"] + 1, "bits": c["bits"],
-                       "group_size": c["gs"], "layers_cycled": NL,
-                       "l2": f"inputs larger than L2: {NL} distinct layer caches, "
-                             f"{NL * layer_bytes / 1e6:.0f} MB cycled",
-                       "parallelism": f"shard by sequence, {world} GPU(s), no collective",
-                       "timing": "CUDA graphs of NL steps, CUDA events, max over ranks"},
-            "bytes_per_step": sb,
-            "e2e": {"value": round(e2e_value, 1), "unit": UNIT,
-                    "h2d_bytes_per_step": int(hq[0].numel() * 2 + hk[0].numel() * 2 + hv[0].numel() * 2),
-                    "d2h_bytes_per_step": int(ho[0].numel() * 2),
-                    "us_per_step": round(1e3 * e2e_ms / K2, 3), "steps": K2,
-                    "path": "kvq Python API per step (eager), pinned host buffers"},
-            "gpu_launches": 3 * K,  # per step: fused K/V append, attention, merge of partials
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind,
-                         "kernel": "decode = attn_bal_kernel<4,128,64,1> + attn_bal_merge_kernel",
-                         "kernel_us": round(kmean * 1e3, 3),
-                         "bytes_per_launch": decode_launch_bytes(c),
-                         "traffic": traffic_from_profiles(),
-                         "timing": "CUDA events around decode-only graph replays of the same "
-                                   "layers, right after the timed steps, same stream"},
-            "clocks": clk,
-        }
-    return res
 
+# ----------------------------------------------------- other workloads --
 
 CFG4 = dict(B=1, Hq=32, Hkv=8, D=128, N_prior=16384, L=512, bits=8, gs=64, outliers=4)
 
@@ -405,7 +616,6 @@ def run_prefill(args):
                            q=torch.randn(B, Hq, L, D, generator=g, device=device).half()))
     torch.cuda.synchronize()
     stream = torch.cuda.Stream()
-    mask = None
 
     def step(Ly):
         qk, qv = Ly["cache"].update_and_fetch_quantized(Ly["kn"], Ly["vn"])
@@ -435,18 +645,16 @@ def run_prefill(args):
             g_step.replay()
             g_att.replay()
         torch.cuda.synchronize()
-        reps = max(1, args.steps // NL)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        ev[0].record(stream)
-        for _ in range(reps):
-            g_step.replay()
-        ev[1].record(stream)
-        for _ in range(reps):
-            g_att.replay()
-        ev[2].record(stream)
-        ev[2].synchronize()
-    step_ms = ev[0].elapsed_time(ev[1]) / (reps * NL)
-    att_ms = ev[1].elapsed_time(ev[2]) / (reps * NL)
+    reps = max(1, args.steps // NL)
+    with torch.cuda.stream(stream):
+        with Timed(stream, 1, device, Clocks(0)) as t1:
+            for _ in range(reps):
+                g_step.replay()
+        with Timed(stream, 1, device) as t2:
+            for _ in range(reps):
+                g_att.replay()
+    step_ms = t1.ms / (reps * NL)
+    att_ms = t2.ms / (reps * NL)
     fl = prefill_flops(c)
     try:
         peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
@@ -455,7 +663,8 @@ def run_prefill(args):
         peak, pk = 1590.0, "fallback"
     att_tf = fl / (att_ms / 1e3) / 1e12
     print(json.dumps({
-        "metric": "quantized-KV chunked prefill TFLOP/s (config 4: B1 Hq32 Hkv8 D128, 16384 prior + 512-row causal chunk, kv8 gs64)",
+        "metric": "quantized-KV chunked prefill TFLOP/s (config 4: B1 Hq32 Hkv8 D128, 16384 "
+                  "prior + 512-row causal chunk, kv8 gs64)",
         "value": round(fl / (step_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": 1,
         "steps": reps * NL, "warmup": args.warmup, "ms_per_step": round(step_ms, 5),
         "higher_is_better": True, "dtype": "u8 codes/f16", "data": "synthetic (seeded torch.randn)",
@@ -463,86 +672,54 @@ def run_prefill(args):
                    "layers_cycled": NL, "l2": "4 distinct layers (147 MB of K/V) per replay"},
         "roofline": {"bound": "tensor", "achieved": round(att_tf, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(att_tf / peak, 4), "peak_kind": pk,
-                     "kernel": "prefill_tc_kernel (tcgen05 UMMA, TMEM accumulators) + prefill_tc_merge_kernel",
+                     "kernel": "prefill_tc_kernel (tcgen05 UMMA, TMEM accumulators) + "
+                               "prefill_tc_merge_kernel",
                      "kernel_us": round(att_ms * 1e3, 3)},
-        "gpu_launches": 3 * reps * NL}))
+        "gpu_launches": 3 * reps * NL, "clocks": t1.clk}))
 
-
-# ------------------------------------------------------ other configs --
-#
-# Secondary measurement lines for the other BASELINE configs (one JSON line
-# each, not read by the driver): config 1 (one small decode step, many
-# distinct layers so the working set exceeds L2), config 3 (Gemma-style
-# rotating window: 5 window layers + 1 global layer per step, append and
-# decode), config 5 (ragged batch of 64 sequences decoded with seq_lens, kv
-# heads sharded over ranks with no communication) and config 5's single
-# 131,072-token sequence split along the context (partials all-gathered over
-# NCCL and merged).  Synthetic seeded data of the named shapes.
 
 CONFIG_DESC = {
     "config1": "single decode step: B1 Hq16 Hkv4 D128 N2048 kv8 gs64, 64 distinct layers cycled",
     "config3": "Gemma-style window: B4 Hq8 Hkv4 D256 kv8 gs64; per step 5 rotating layers (window "
                "1024, 4096 tokens written) + 1 global layer (4096), append + decode each",
-    "config5": "ragged serving: B64 lengths U[1024, 32768] (seed 5), Hq32 Hkv8 D128 kv4 gs64, "
-               "decode with seq_lens; kv heads sharded over ranks, no collective",
-    "config5-ctx": "one 131072-token sequence, Hq32 Hkv8 D128 kv4 gs64, context split over ranks; "
-                   "(m, l, o) partials all-gathered over NCCL and merged",
 }
 
 
-def _fill_cache(cache, B, H, N, D, g, device, chunk):
-    """Append N seeded rows (fp16) to `cache` in chunks; returns the last views."""
-    import torch
-    views = None
-    for s0 in range(0, N, chunk):
-        S = min(chunk, N - s0)
-        k = torch.randn(B, H, S, D, generator=g, device=device).half()
-        v = torch.randn(B, H, S, D, generator=g, device=device).half()
-        views = cache.update_and_fetch_quantized(k, v)
-        del k, v
-    return views
-
-
-def run_config(args, rank, world, local_rank):
+def run_config(args):
+    """Secondary lines for configs 1 and 3 on one GPU (graph of one pass)."""
     import numpy as np
     import torch
-    import torch.distributed as dist
     import kvq
-    from kvq.parallel import ContextSplitDecode, context_ranges
-
     w = args.workload
-    device = torch.device("cuda", local_rank)
+    device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     g = torch.Generator(device=device)
-    g.manual_seed(3000 + rank)
+    g.manual_seed(3000)
     steps, keep = [], []
-    nbytes = 0  # algorithmic bytes of this rank per pass over `steps`
-    dt = "u8 codes/f16"
-    scaling = "weak"
-    graph_ok = True
+    nbytes = 0
     if w == "config1":
         B, Hq, Hkv, D, N, bits, gs = 1, 16, 4, 128, 2048, 8, 64
-        rb = 2 * (D * bits // 8 + 2 * (D // gs) * 2)
+        rb = kv_row_bytes(dict(D=D, bits=bits, gs=gs))
         scale = 1.0 / np.sqrt(D)
         for _ in range(64):
             cache = kvq.QuantizedKVCache(gs, bits)
-            kq, vq = _fill_cache(cache, B, Hkv, N, D, g, device, N)
+            kq, vq = _fill(cache, B, Hkv, N, D, g, device, N)
             q = torch.randn(B, Hq, 1, D, generator=g, device=device).half()
             out = torch.empty_like(q)
             keep.append((cache, kq, vq, q, out))
             steps.append(lambda kq=kq, vq=vq, q=q, out=out:
                          kvq.sdpa_decode(q, kq, vq, scale, out=out))
             nbytes += B * Hkv * N * rb + 2 * B * Hq * D * 2
-    elif w == "config3":
+    else:
         B, Hq, Hkv, D, bits, gs, win = 4, 8, 4, 256, 8, 64, 1024
-        rb = 2 * (D * bits // 8 + 2 * (D // gs) * 2)
+        rb = kv_row_bytes(dict(D=D, bits=bits, gs=gs))
         scale = 1.0 / 16.0
         for _ in range(3):  # 3 x (5 + 1) layers: 241 MB cycled, above L2
             for li in range(6):
                 local = li < 5
                 cache = kvq.RotatingQuantizedKVCache(win, gs, bits) if local else \
                     kvq.QuantizedKVCache(gs, bits, reserve_rows=4352)
-                _fill_cache(cache, B, Hkv, 4096, D, g, device, win)
+                _fill(cache, B, Hkv, 4096, D, g, device, win)
                 kn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
                 vn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
                 q = torch.randn(B, Hq, 1, D, generator=g, device=device).half()
@@ -560,128 +737,85 @@ def run_config(args, rank, world, local_rank):
                         cache.trim(1)  # host bookkeeping: every replay the same work
                 steps.append(st)
                 nbytes += B * Hkv * n * rb + 2 * B * Hq * D * 2 + B * Hkv * D * 2 * 2
-    elif w == "config5":
-        B, Hq, Hkv, D, bits, gs = 64, 32, 8, 128, 4, 64
-        if Hkv % world:
-            raise SystemExit("config5 shards 8 kv heads: use 1, 2, 4 or 8 GPUs")
-        rb = 2 * (D * bits // 8 + 2 * (D // gs) * 2)
-        scale = 1.0 / np.sqrt(D)
-        lens = np.random.default_rng(5).integers(1024, 32769, size=B)
-        hk = Hkv // world
-        Nmax = int(lens.max())
-        cache = kvq.QuantizedKVCache(gs, bits, reserve_rows=(Nmax + 255) // 256 * 256)
-        kq, vq = _fill_cache(cache, B, hk, Nmax, D, g, device, 1024)
-        q = torch.randn(B, hk * (Hq // Hkv), 1, D, generator=g, device=device).half()
-        out = torch.empty_like(q)
-        sl = torch.tensor(lens, dtype=torch.int32, device=device)
-        keep.append((cache, kq, vq, q, out, sl))
-        steps.append(lambda: kvq.sdpa_decode(q, kq, vq, scale, seq_lens=sl, out=out))
-        nbytes = int(lens.sum()) * hk * rb + 2 * B * hk * (Hq // Hkv) * D * 2
-        dt = "u4 codes/f16"
-        scaling = "strong"
-    elif w == "config5-ctx":
-        Hq, Hkv, D, bits, gs, N = 32, 8, 128, 4, 64, 131072
-        rb = 2 * (D * bits // 8 + 2 * (D // gs) * 2)
-        scale = 1.0 / np.sqrt(D)
-        a, b = context_ranges(N, world)[rank]
-        cache = kvq.QuantizedKVCache(gs, bits, reserve_rows=(b - a + 255) // 256 * 256)
-        kq, vq = _fill_cache(cache, 1, Hkv, b - a, D, g, device, 4096)
-        gq = torch.Generator(device=device)
-        gq.manual_seed(77)  # the same query on every rank
-        q = torch.randn(1, Hq, 1, D, generator=gq, device=device).half()
-        out = torch.empty_like(q)
-        keep.append((cache, kq, vq, q, out))
-        if world > 1:
-            split = ContextSplitDecode()
-            steps.append(lambda: out.copy_(split.step(q, kq, vq, scale)))
-            graph_ok = False  # the all-gather runs eagerly
-        else:
-            steps.append(lambda: kvq.sdpa_decode(q, kq, vq, scale, out=out))
-        nbytes = (b - a) * Hkv * rb + 2 * Hq * D * 2
-        dt = "u4 codes/f16"
-        scaling = "strong"
     torch.cuda.synchronize()
-
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
             for s in steps:
                 s()
     stream.synchronize()
-    graph = None
-    if graph_ok:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for s in steps:
-                s()
-        for _ in range(3):
-            graph.replay()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for s in steps:
+            s()
+    for _ in range(3):
+        graph.replay()
     torch.cuda.synchronize()
     reps = max(1, (args.steps + len(steps) - 1) // len(steps))
-    clocks = Clocks(local_rank) if rank == 0 else None
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    if clocks:
-        clocks.start()
-        time.sleep(0.1)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        e0.record()
-        for _ in range(reps):
-            if graph is not None:
+        with Timed(stream, 1, device, Clocks(0)) as tm:
+            for _ in range(reps):
                 graph.replay()
-            else:
-                for s in steps:
-                    s()
-        e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop() if clocks else None
-    t = torch.tensor([e0.elapsed_time(e1), float(nbytes)], device=device, dtype=torch.float64)
-    if world > 1:
-        tt = t.clone()
-        dist.all_reduce(t[0:1], op=dist.ReduceOp.MAX)
-        dist.all_reduce(tt[1:2], op=dist.ReduceOp.SUM)
-        t[1] = tt[1]
-    ms, total_bytes = float(t[0].item()), float(t[1].item())
-    if not torch.isfinite(keep[0][-2 if w == "config5" else -1].float()).all():
-        raise RuntimeError("non-finite decode output")
-    if rank != 0:
-        return None
     K = reps * len(steps)
-    gbs = total_bytes * reps / (ms / 1e3) / 1e9
-    per_gpu = gbs / world
+    gbs = nbytes * reps / (tm.ms / 1e3) / 1e9
     peak, peak_kind = peaks()
-    return {
+    print(json.dumps({
         "metric": f"quantized-KV decode SDPA achieved HBM GB/s ({w})", "value": round(gbs, 1),
-        "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
-        "ms_per_step": round(ms / K, 5), "us_per_step": round(1e3 * ms / K, 3),
-        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": dt,
-        "data": "synthetic (seeded torch.randn / numpy lengths)",
-        "config": {"workload": w, "description": CONFIG_DESC[w],
-                   "bytes_per_pass_all_ranks": int(total_bytes), "steps_per_pass": len(steps),
-                   "timing": ("CUDA graph of one pass" if graph is not None else
-                              "eager steps (NCCL all-gather inside)") +
-                             ", CUDA events, max over ranks"},
-        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
-                     "note": "whole step per GPU (append included where the config appends)"},
-        "clocks": clk,
-    }
+        "unit": UNIT, "n_gpus": 1, "steps": K, "warmup": args.warmup,
+        "ms_per_step": round(tm.ms / K, 5), "us_per_step": round(1e3 * tm.ms / K, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes/f16",
+        "data": "synthetic (seeded torch.randn)",
+        "config": {"workload": w, "description": CONFIG_DESC[w], "bytes_per_pass": int(nbytes),
+                   "steps_per_pass": len(steps),
+                   "timing": "CUDA graph of one pass, CUDA events"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": UNIT,
+                     "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
+                     "note": "whole step (append included where the config appends)"},
+        "clocks": tm.clk}))
 
 
 def profile_run(args):
-    """Fixed small workload for ncu: 3 config-2 layers (227 MB, above L2),
-    `--steps` launches of one kernel, cycling layers."""
+    """Fixed small workloads for ncu (no timing): `--steps` launches of one
+    kernel.  decode / append: 3 config-2 layers (227 MB, above L2), cycled;
+    config5: the first 16 sequences of config 5, all 8 kv heads (315 MB)."""
     import numpy as np
     import torch
     import kvq
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    layers = setup_layers(CFG, 3, device, seed=7)
-    scale = 1.0 / np.sqrt(CFG["D"])
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    if args.profile == "config5":
+        c = CFG5
+        lens = config5_lens()[:16]
+        Nmax = int(lens.max())
+        cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=(Nmax + 255) // 256 * 256)
+        K, V = _fill(cache, 16, c["Hkv"], Nmax, c["D"], g, device, 2048)
+        q = torch.randn(16, c["Hq"], 1, c["D"], generator=g, device=device).half()
+        sl = torch.tensor(lens, dtype=torch.int32, device=device)
+        for _ in range(args.steps):
+            out = kvq.sdpa_decode(q, K, V, 1.0 / np.sqrt(c["D"]), seq_lens=sl)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": "config5", "launches": args.steps,
+                          "algorithmic_bytes_per_launch":
+                              int(lens.sum()) * c["Hkv"] * kv_row_bytes(c) + 2 * 16 * c["Hq"] *
+                              c["D"] * 2,
+                          "out_mean_abs": float(out.float().abs().mean())}))
+        return
+    c = CFG2
+    B, Hq, Hkv, D, Np = c["B"], c["Hq"], c["Hkv"], c["D"], c["N_prior"]
+    layers = []
+    for _ in range(3):
+        cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=(Np + 256) // 256 * 256)
+        k = torch.randn(B, Hkv, Np, D, generator=g, device=device)
+        k[..., :c["outliers"]] *= 8.0
+        cache.update_and_fetch_quantized(k.half(), torch.randn(B, Hkv, Np, D, generator=g,
+                                                               device=device).half())
+        kn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
+        vn = torch.randn(B, Hkv, 1, D, generator=g, device=device).half()
+        q = torch.randn(B, Hq, 1, D, generator=g, device=device).half()
+        layers.append(dict(cache=cache, kn=kn, vn=vn, q=q, out=torch.empty_like(q)))
+    scale = 1.0 / np.sqrt(D)
     views = []
     for L in layers:
         views.append(L["cache"].update_and_fetch_quantized(L["kn"], L["vn"]))
@@ -698,71 +832,80 @@ def profile_run(args):
                       "out_mean_abs": float(layers[0]["out"].float().abs().mean())}))
 
 
+# ----------------------------------------------------------------- main --
+
+def reference_arm(args, rank):
+    """mlx-bun's own CPU path cannot run here (Bun + MLX, macOS arm64 only);
+    its op graph restated in C is timed on every host core, rank 0 only."""
+    if rank != 0:
+        return
+    threads = host_cores()
+    K = max(1, args.steps)
+    gbs, desc, calls, el = cpu_oracle_config5(K, 60.0, threads)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": calls, "steps_requested": K, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "u4 codes/f16", "data": "synthetic (seeded numpy)",
+        "config": {"workload": WORKLOAD},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(gbs, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "mlx-bun's own CPU path (MLX CPU stream under Bun) cannot run on this box; the C "
+                "restatement of its op graph is timed with an explicit thread count of every "
+                "host core (torchrun's OMP_NUM_THREADS=1 does not apply); each step is one "
+                "oracle call, at most ~60 s of them"}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="kvq", choices=["kvq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "prefill", "config1", "config3", "config5",
-                                           "config5-ctx"], default="decode",
-                    help="decode: the config-2 step the driver reads (default); prefill: "
-                         "config 4 chunked prefill; config1/3/5/5-ctx: the other BASELINE "
-                         "configs (separate JSON lines)")
-    ap.add_argument("--profile", choices=["decode", "append"], default=None,
-                    help="run only the named kernel over 3 config-2 layers, `--steps` "
-                         "launches, no timing (a small, fixed workload for ncu captures)")
+    ap.add_argument("--no-nested", action="store_true",
+                    help="skip the nested config-2 and context-split measurements")
+    ap.add_argument("--workload", choices=["decode", "prefill", "config1", "config3"],
+                    default="decode",
+                    help="decode: the config-5 line the driver reads (default); prefill: "
+                         "config 4 chunked prefill; config1 / config3: their own lines")
+    ap.add_argument("--profile", choices=["decode", "append", "config5"], default=None,
+                    help="run only the named kernel on a small fixed workload, `--steps` "
+                         "launches, no timing (for ncu captures)")
     args = ap.parse_args()
     if args.profile:
         return profile_run(args)
-    if args.workload == "prefill":
-        return run_prefill(args)
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-
     if args.impl == "reference":
-        if rank != 0:
-            return
-        K = max(1, args.steps)
-        budget = 60.0
-        gbs, threads, desc, el = cpu_oracle_sample(K, budget)
-        line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": UNIT,
-                "n_gpus": args.gpus, "steps": K, "warmup": args.warmup,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "u4 codes/f16", "data": "synthetic (seeded numpy)",
-                "config": {"workload": WORKLOAD},
-                "cpu_baseline": {"value": round(gbs, 4), "unit": UNIT, "cores": threads,
-                                 "kind": "port", "sample": desc},
-                "e2e": {"value": round(gbs, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0},
-                "note": "mlx-bun's own CPU path (MLX CPU stream under Bun) cannot run on "
-                        "this box; the C restatement of its op graph is timed instead"}
-        print(json.dumps(line))
-        return
+        return reference_arm(args, rank)
+    if args.workload == "prefill":
+        return run_prefill(args)
+    if args.workload in CONFIG_DESC:
+        return run_config(args)
 
     import torch
     import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    if args.workload in CONFIG_DESC:
-        try:
-            res = run_config(args, rank, world, local_rank)
-            if rank == 0:
-                print(json.dumps(res))
-        finally:
-            if world > 1:
-                dist.destroy_process_group()
-        return
     try:
-        res = run_gpu(args, rank, world, local_rank)
+        res = run_config5(args, rank, world, local_rank)
+        if not args.no_nested:
+            c2 = run_config2(args, rank, world, local_rank)
+            ctx = run_context_split(args, rank, world, local_rank)
+            if res is not None:
+                res["config2"] = c2
+                res["context_split"] = ctx
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
-                gbs, threads, desc, el = cpu_oracle_sample(4, 12.0)
+                threads = host_cores()
+                gbs, desc, _, _ = cpu_oracle_config5(10 ** 6, 15.0, threads)
                 res["cpu_baseline"] = {"value": round(gbs, 4), "unit": UNIT, "cores": threads,
                                        "kind": "port", "sample": desc}
             print(json.dumps(res))
