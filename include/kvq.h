@@ -133,7 +133,68 @@ int32_t kvq_cache_trim(kvq_cache* cache, int32_t n, int32_t bypass);
 int32_t kvq_cache_make_mask(const kvq_cache* cache, int32_t N, int32_t window_size,
                             int32_t* mask_mode, int32_t* mask_window);
 
-/* ---- conversion --------------------------------------------------------- */
+/* ---- batched serving: per-sequence positions on the device -------------- */
+
+/* Ragged append for a batch whose sequences sit at different lengths (the
+ * quantized-KV unlock of mlx-bun's batch scheduler, which is bf16-only,
+ * src/serve/generation-gateway.ts:83-84, :156; and the dynamic-offset
+ * writes of the compiled-decode adapters, src/model/compiled-decode.ts:99-190
+ * with slice_update_dynamic, src/mlx/ops.ts:513-525).  Batch entry b
+ * quantizes its first counts[b] rows of k / v ([B, H, S, D], strides as
+ * kvq_append; counts NULL: all S) into rows [seq_lens[b], seq_lens[b] +
+ * counts[b]) of its own (b, h) rows, then seq_lens[b] += counts[b].
+ * seq_lens and counts are DEVICE int32[B]: positions are read and advanced
+ * on the GPU, so a CUDA graph of append + decode appends at the next row on
+ * every replay.  Growing caches only, created with reserve_rows > 0 (the
+ * capacity); an entry whose rows would pass it is skipped (its length stays)
+ * and the cache's error flag is raised — see kvq_cache_check.  The host
+ * offset is not used or changed: do not mix with kvq_append on one cache.
+ * Decode over it with kvq_cache_fetch_all views and the same seq_lens. */
+int32_t kvq_append_ragged(kvq_cache* cache, const void* k, const void* v, int32_t S,
+                          const int64_t* k_strides, const int64_t* v_strides, int32_t* seq_lens,
+                          const int32_t* counts, void* stream);
+
+/* Views of the cache's whole physical capacity (len = capacity rows), for
+ * kvq_sdpa_decode with per-sequence seq_lens after ragged appends. */
+int32_t kvq_cache_fetch_all(const kvq_cache* cache, kvq_qtensor* keys, kvq_qtensor* values);
+
+/* Synchronize `stream`, report (then clear) the cache's error flag: a
+ * ragged append skipped an entry that would have passed the capacity. */
+int32_t kvq_cache_check(kvq_cache* cache, void* stream);
+
+/* ---- conversion and persistence ----------------------------------------- */
+
+/* Quantized cache from a dense fp16 / bf16 K/V buffer with its state
+ * (KVCache.toQuantized, src/model/gemma4-base.ts:395-404, and
+ * RotatingKVCache.toQuantized, :892-902 — the per-layer step of
+ * maybeQuantizeKv, src/generate.ts:101-129).  Every one of the `rows` rows
+ * per (batch, head) is quantized as laid out: the padding of a growing
+ * buffer and the ring order of a rotating one are kept, and offset and
+ * ring_idx are adopted (ring_idx is ignored for growing caches), so the
+ * cache continues exactly where the dense one stood.  k, v: device [B, H,
+ * rows, D] with element strides (d stride 1).  desc->max_size picks growing
+ * (0) or rotating.  Stream-ordered; the dense buffers may be released once
+ * the stream has passed this call. */
+int32_t kvq_cache_from_dense(const kvq_desc* desc, const void* k, const void* v, int32_t rows,
+                             const int64_t* k_strides, const int64_t* v_strides, int64_t offset,
+                             int64_t ring_idx, void* stream, kvq_cache** out);
+
+/* Copy rows [0, rows) of every (batch, head) of the six components to host
+ * memory, contiguous [B, H, rows, *] each, in the order K packed, K scales,
+ * K biases, V packed, V scales, V biases — the tensors of a saved cache
+ * (saveKvCache, src/kv-store.ts:54-123, which keeps the live [0:offset]
+ * rows of a growing cache and the whole buffer of a ring).  Synchronizes
+ * `stream`. */
+int32_t kvq_cache_export(const kvq_cache* cache, int64_t rows, void* const* host, void* stream);
+
+/* A cache holding `rows` rows per (batch, head) read from six host buffers
+ * laid out as kvq_cache_export writes them, with the given offset and ring
+ * index (loadKvCache + restoreState, src/kv-store.ts:147-175,
+ * src/model/gemma4-base.ts:385-391, :880-886).  Synchronizes `stream`. */
+int32_t kvq_cache_import(const kvq_desc* desc, const void* const* host, int32_t rows,
+                         int64_t offset, int64_t ring_idx, void* stream, kvq_cache** out);
+
+/* ---- quantize ------------------------------------------------------------ */
 
 /* Affine group quantize of `rows` contiguous rows of D dtype values into
  * contiguous packed / scales / biases (mlx_quantize as called by

@@ -1592,6 +1592,11 @@ __global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int g
     U = (int64_t)u * p.Tu;
     RT = (int64_t)p.B * Hkv * p.Tu;
   } else {  // tiles of the entries before b and of all entries
+    // The lengths live in memory that an earlier kernel of the stream may
+    // have just written (a ragged append advances them): wait before
+    // reading.  The attention grid signals its dependents at its start, so
+    // without this wait the merge could run ahead of the append.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     int64_t before = 0, all = 0;
     for (int bb = tid; bb < p.B; bb += D) {
       const int n = min(max(p.seq_lens[bb], 0), p.N);

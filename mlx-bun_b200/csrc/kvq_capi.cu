@@ -151,6 +151,7 @@ struct kvq_cache {
   void* base = nullptr; // one allocation holding the six components
   size_t bytes = 0;
   TripleView k{}, v{};
+  int* status = nullptr;  // device error flag (ragged append past the capacity)
 
   int64_t words() const { return (int64_t)d.head_dim * d.bits / 32; }
   int64_t groups() const { return (int64_t)d.head_dim / d.group_size; }
@@ -162,6 +163,7 @@ namespace {
 
 struct Layout {
   size_t off[6];
+  size_t status;  // 256-byte block after the six components: the cache's error flag
   size_t total;
 };
 
@@ -177,7 +179,8 @@ Layout layout_for(const kvq_cache* c, int64_t cap) {
     L.off[i] = o;
     o += align256(sz[i]);
   }
-  L.total = o;
+  L.status = o;
+  L.total = o + 256;
   return L;
 }
 
@@ -185,6 +188,7 @@ void bind_views(kvq_cache* c, void* base, int64_t cap) {
   const Layout L = layout_for(c, cap);
   uint8_t* p = static_cast<uint8_t*>(base);
   const int64_t hs = cap, bs = cap * c->d.kv_heads;
+  c->status = reinterpret_cast<int*>(p + L.status);
   c->k = TripleView{reinterpret_cast<uint32_t*>(p + L.off[0]),
                     reinterpret_cast<uint16_t*>(p + L.off[1]),
                     reinterpret_cast<uint16_t*>(p + L.off[2]), bs, hs};
@@ -346,6 +350,40 @@ int32_t make_attn_args(const kvq_qtensor* k, const kvq_qtensor* v, const void* q
 }
 
 }  // namespace kvq
+
+namespace {
+
+// A cache of `rows` rows per (batch, head) holding the given state: zeroed
+// storage of at least `rows` rows, offset / ring index / buffer length set.
+int32_t adopt_state(const kvq_desc* desc, int32_t rows, int64_t offset, int64_t ring_idx,
+                    cudaStream_t st, kvq_cache** out) {
+  int32_t rc = check_desc(desc);
+  if (rc) return rc;
+  if (rows < 0 || offset < 0) return fail(KVQ_ERR_ARG, "rows and offset must be >= 0");
+  if (desc->max_size == 0 && offset > rows)
+    return fail(KVQ_ERR_ARG, "growing cache: offset exceeds the buffer rows");
+  if (desc->max_size > 0 && (ring_idx < 0 || ring_idx > rows))
+    return fail(KVQ_ERR_ARG, "rotating cache: ring_idx must lie in [0, rows]");
+  kvq_cache* c = new kvq_cache();
+  c->d = *desc;
+  if (rows > 0) {
+    int64_t cap = std::max<int64_t>({(int64_t)rows, desc->reserve_rows,
+                                     c->ring() ? (int64_t)desc->max_size : 0});
+    cap = round_up(cap, c->ring() ? 16 : 256);
+    if ((rc = relayout(c, cap, {}, st))) {
+      delete c;
+      return rc;
+    }
+    c->allocated = true;
+    c->seq_len = rows;
+  }
+  c->offset = offset;
+  c->ring_idx = c->ring() ? ring_idx : offset;
+  *out = c;
+  return KVQ_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -569,6 +607,141 @@ int32_t kvq_cache_make_mask(const kvq_cache* c, int32_t N, int32_t window_size, 
   const int64_t off = std::min<int64_t>(c->d.max_size - 1, c->offset);
   *mask_mode = KVQ_MASK_CAUSAL;
   *mask_window = (off + N > w) ? (int32_t)w : 0;
+  return KVQ_OK;
+}
+
+int32_t kvq_append_ragged(kvq_cache* c, const void* k, const void* v, int32_t S,
+                          const int64_t* k_strides, const int64_t* v_strides, int32_t* seq_lens,
+                          const int32_t* counts, void* stream) {
+  if (!c) return fail(KVQ_ERR_ARG, "cache is NULL");
+  if (!k || !v || !k_strides || !v_strides || !seq_lens)
+    return fail(KVQ_ERR_ARG, "NULL k / v / strides / seq_lens");
+  if (S <= 0) return fail(KVQ_ERR_ARG, "S must be positive");
+  if (k_strides[3] != 1 || v_strides[3] != 1) return fail(KVQ_ERR_ARG, "the d stride of k and v must be 1");
+  if (c->ring()) return fail(KVQ_ERR_STATE, "ragged appends take growing caches (max_size 0)");
+  if (!c->base)
+    return fail(KVQ_ERR_STATE, "ragged appends need the rows reserved at creation (reserve_rows > 0)");
+  DeviceGuard guard(c->d.device);
+  if (!guard.ok) return fail(KVQ_ERR_CUDA, "cannot select the cache's device");
+  RowGeom g{c->d.head_dim, c->d.bits, c->d.group_size};
+  return launch_append_ragged(k, k_strides, v, v_strides, c->d.batch, c->d.kv_heads, S, g,
+                              c->d.dtype, c->k, c->v, c->cap, seq_lens, counts, c->status,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int32_t kvq_cache_fetch_all(const kvq_cache* c, kvq_qtensor* keys, kvq_qtensor* values) {
+  if (!c || !keys || !values) return fail(KVQ_ERR_ARG, "NULL argument");
+  if (!c->base) return fail(KVQ_ERR_STATE, "cache has no device storage yet");
+  const TripleView* tv[2] = {&c->k, &c->v};
+  kvq_qtensor* out[2] = {keys, values};
+  for (int i = 0; i < 2; i++) {
+    kvq_qtensor& t = *out[i];
+    t.packed = tv[i]->packed;
+    t.scales = tv[i]->scales;
+    t.biases = tv[i]->biases;
+    t.batch_stride = tv[i]->batch_stride;
+    t.head_stride = tv[i]->head_stride;
+    t.batch = c->d.batch;
+    t.heads = c->d.kv_heads;
+    t.len = (int32_t)c->cap;
+    t.head_dim = c->d.head_dim;
+    t.bits = c->d.bits;
+    t.group_size = c->d.group_size;
+    t.dtype = c->d.dtype;
+  }
+  return KVQ_OK;
+}
+
+int32_t kvq_cache_check(kvq_cache* c, void* stream) {
+  if (!c) return fail(KVQ_ERR_ARG, "cache is NULL");
+  if (!c->base) return KVQ_OK;
+  DeviceGuard guard(c->d.device);
+  KVQ_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int flag = 0;
+  KVQ_CUDA_TRY(cudaMemcpy(&flag, c->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (flag) {
+    const int zero = 0;
+    KVQ_CUDA_TRY(cudaMemcpy(c->status, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    return fail(KVQ_ERR_STATE, "a ragged append would have passed the cache's capacity (rows skipped)");
+  }
+  return KVQ_OK;
+}
+
+int32_t kvq_cache_from_dense(const kvq_desc* desc, const void* k, const void* v, int32_t rows,
+                             const int64_t* k_strides, const int64_t* v_strides, int64_t offset,
+                             int64_t ring_idx, void* stream, kvq_cache** out) {
+  if (!out) return fail(KVQ_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  if (!desc) return fail(KVQ_ERR_ARG, "desc is NULL");
+  if (rows > 0 && (!k || !v || !k_strides || !v_strides))
+    return fail(KVQ_ERR_ARG, "NULL k / v / strides");
+  if (rows > 0 && (k_strides[3] != 1 || v_strides[3] != 1))
+    return fail(KVQ_ERR_ARG, "the d stride of k and v must be 1");
+  DeviceGuard guard(desc->device);
+  if (!guard.ok) return fail(KVQ_ERR_CUDA, "cannot select the cache's device");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  kvq_cache* c = nullptr;
+  int32_t rc = adopt_state(desc, rows, offset, ring_idx, st, &c);
+  if (rc) return rc;
+  if (rows > 0 && (rc = quantize_into(c, k, v, rows, k_strides, v_strides, 0, st))) {
+    kvq_cache_free(c);
+    return rc;
+  }
+  *out = c;
+  return KVQ_OK;
+}
+
+int32_t kvq_cache_export(const kvq_cache* c, int64_t rows, void* const* host, void* stream) {
+  if (!c || !host) return fail(KVQ_ERR_ARG, "NULL argument");
+  if (rows < 0 || (rows > 0 && (!c->base || rows > c->cap)))
+    return fail(KVQ_ERR_ARG, "rows must lie in [0, capacity]");
+  for (int i = 0; i < 6; i++)
+    if (rows > 0 && !host[i]) return fail(KVQ_ERR_ARG, "NULL host buffer");
+  if (rows == 0) return KVQ_OK;
+  DeviceGuard guard(c->d.device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  size_t rb[6];
+  row_bytes(c, rb);
+  for (int i = 0; i < 6; i++)
+    KVQ_CUDA_TRY(cudaMemcpy2DAsync(host[i], rows * rb[i], comp_ptr(c, i), c->cap * rb[i],
+                                   rows * rb[i], (size_t)c->bh(), cudaMemcpyDeviceToHost, st));
+  KVQ_CUDA_TRY(cudaStreamSynchronize(st));
+  return KVQ_OK;
+}
+
+int32_t kvq_cache_import(const kvq_desc* desc, const void* const* host, int32_t rows,
+                         int64_t offset, int64_t ring_idx, void* stream, kvq_cache** out) {
+  if (!out) return fail(KVQ_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  if (!desc) return fail(KVQ_ERR_ARG, "desc is NULL");
+  if (rows > 0 && !host) return fail(KVQ_ERR_ARG, "NULL host buffers");
+  for (int i = 0; rows > 0 && i < 6; i++)
+    if (!host[i]) return fail(KVQ_ERR_ARG, "NULL host buffer");
+  DeviceGuard guard(desc->device);
+  if (!guard.ok) return fail(KVQ_ERR_CUDA, "cannot select the cache's device");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  kvq_cache* c = nullptr;
+  int32_t rc = adopt_state(desc, rows, offset, ring_idx, st, &c);
+  if (rc) return rc;
+  if (rows > 0) {
+    size_t rb[6];
+    row_bytes(c, rb);
+    for (int i = 0; i < 6; i++) {
+      const cudaError_t e = cudaMemcpy2DAsync(comp_ptr(c, i), c->cap * rb[i], host[i],
+                                              rows * rb[i], rows * rb[i], (size_t)c->bh(),
+                                              cudaMemcpyHostToDevice, st);
+      if (e != cudaSuccess) {
+        kvq_cache_free(c);
+        return cuda_fail(e, "cudaMemcpy2DAsync(import)");
+      }
+    }
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+      kvq_cache_free(c);
+      return cuda_fail(e, "cudaStreamSynchronize(import)");
+    }
+  }
+  *out = c;
   return KVQ_OK;
 }
 

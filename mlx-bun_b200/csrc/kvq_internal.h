@@ -45,6 +45,13 @@ struct TripleView {
 int32_t launch_append_kv(const void* k, const int64_t* k_strides, const void* v,
                          const int64_t* v_strides, int B, int H, int S, RowGeom g, int dtype,
                          TripleView dk, TripleView dv, int64_t dst_row0, cudaStream_t st);
+// Ragged: entry b writes its first counts[b] (nullable: S) rows at rows
+// lens[b] + s (device arrays), then a second launch advances lens[b] by
+// that count; entries that would pass `cap` rows are skipped and raise *err.
+int32_t launch_append_ragged(const void* k, const int64_t* k_strides, const void* v,
+                             const int64_t* v_strides, int B, int H, int S, RowGeom g, int dtype,
+                             TripleView dk, TripleView dv, int64_t cap, int32_t* lens,
+                             const int32_t* counts, int* err, cudaStream_t st);
 // Contiguous rows -> contiguous triple.
 int32_t launch_quantize_rows(const void* x, int64_t rows, RowGeom g, int dtype, uint32_t* packed,
                              uint16_t* scales, uint16_t* biases, cudaStream_t st);

@@ -11,7 +11,15 @@
 //
 // One launch carries up to two jobs (the K and the V rows of an append,
 // selected by blockIdx.y): on the decode path the work is a few rows and the
-// launch itself is the cost.  For whole-cache conversion the kernel is
+// launch itself is the cost.
+//
+// Ragged appends (RAG): batch entry b writes its first counts[b] rows at
+// rows lens[b] + s of its (b, h) rows, where lens and counts are device
+// arrays — the positions live on the GPU, so a captured CUDA graph appends
+// at a new position on every replay.  A separate launch
+// (ragged_advance_kernel) then adds counts[b] to lens[b].  An entry whose
+// rows would pass the capacity is skipped by both launches and raises the
+// cache's error flag.  For whole-cache conversion the kernel is
 // HBM-bound: 2 B read and bits/8 + 4/gs B written per element, with 16-byte
 // loads when the input rows are 16-byte aligned.
 #include <cuda_bf16.h>
@@ -37,6 +45,10 @@ struct Jobs {
   Job j[2];
   int H, S, words;
   int64_t total_rows;
+  const int32_t* lens;    // ragged: device [B] first destination row per entry
+  const int32_t* counts;  // ragged: device [B] rows to write per entry (nullable: S)
+  int64_t cap;            // ragged: rows per (b, h)
+  int* err;               // ragged: cache error flag
 };
 
 template <bool BF16>
@@ -60,7 +72,8 @@ __device__ __forceinline__ float word_to_f(uint32_t w, int half) {
 }
 
 // BITS: 4 or 8.  TPG: threads per group (gs * BITS / 32).  VEC: 16-B loads.
-template <int BITS, int TPG, bool BF16, bool VEC>
+// RAG: ragged destination rows (lens / counts).
+template <int BITS, int TPG, bool BF16, bool VEC, bool RAG = false>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const Jobs jobs) {
   // launched as a programmatic dependent (launch_pdl): let the next kernel be
   // scheduled, then wait for the previous one before reading anything
@@ -134,8 +147,19 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const Jobs jobs) {
     c = fminf(fmaxf(c, 0.0f), NB);
     out |= (uint32_t)c << (BITS * i);
   }
+  int64_t row0 = J.dst_row0;
+  if (RAG) {
+    const int64_t l0 = jobs.lens[b];
+    const int64_t cnt = jobs.counts ? jobs.counts[b] : jobs.S;
+    if (cnt < 0 || l0 < 0 || l0 + cnt > jobs.cap) {
+      if (valid && s == 0 && word == 0) atomicExch(jobs.err, 1);
+      return;
+    }
+    if (s >= cnt) return;
+    row0 += l0;
+  }
   if (!valid) return;
-  const int64_t drow = b * J.dst_bstride + h * J.dst_hstride + J.dst_row0 + s;
+  const int64_t drow = b * J.dst_bstride + h * J.dst_hstride + row0 + s;
   J.packed[drow * words + word] = out;
   if ((word % TPG) == 0) {
     const int groups = words / TPG;
@@ -145,8 +169,28 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const Jobs jobs) {
   }
 }
 
+// lens[b] += counts[b] (or S) after the ragged quantize launch has read
+// them; entries the quantize launch skipped (past the capacity) stay put.
+__global__ void ragged_advance_kernel(int32_t* __restrict__ lens, const int32_t* __restrict__ counts,
+                                      int S, int B, int64_t cap) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int64_t l0 = lens[b];
+  const int64_t cnt = counts ? counts[b] : S;
+  if (cnt >= 0 && l0 >= 0 && l0 + cnt <= cap) lens[b] = (int32_t)(l0 + cnt);
+}
+
 template <int BITS, int TPG, bool BF16>
 int32_t dispatch_vec(bool vec, dim3 grid, cudaStream_t st, const Jobs& jobs) {
+  if (jobs.lens) {
+    if (vec)
+      KVQ_CUDA_TRY(launch_pdl(quantize_rows_kernel<BITS, TPG, BF16, true, true>, grid, dim3(256), 0, st, jobs));
+    else
+      KVQ_CUDA_TRY(launch_pdl(quantize_rows_kernel<BITS, TPG, BF16, false, true>, grid, dim3(256), 0, st, jobs));
+    return KVQ_OK;
+  }
   if (vec)
     KVQ_CUDA_TRY(launch_pdl(quantize_rows_kernel<BITS, TPG, BF16, true>, grid, dim3(256), 0, st, jobs));
   else
@@ -214,6 +258,26 @@ int32_t launch_append_kv(const void* k, const int64_t* k_strides, const void* v,
   jobs.H = H;
   jobs.S = S;
   return launch_jobs(jobs, 2, B, g, dtype, st);
+}
+
+int32_t launch_append_ragged(const void* k, const int64_t* k_strides, const void* v,
+                             const int64_t* v_strides, int B, int H, int S, RowGeom g, int dtype,
+                             TripleView dk, TripleView dv, int64_t cap, int32_t* lens,
+                             const int32_t* counts, int* err, cudaStream_t st) {
+  Jobs jobs{};
+  jobs.j[0] = job_for(k, k_strides, dk, 0);
+  jobs.j[1] = job_for(v, v_strides, dv, 0);
+  jobs.H = H;
+  jobs.S = S;
+  jobs.lens = lens;
+  jobs.counts = counts;
+  jobs.cap = cap;
+  jobs.err = err;
+  int32_t rc = launch_jobs(jobs, 2, B, g, dtype, st);
+  if (rc) return rc;
+  KVQ_CUDA_TRY(launch_pdl(ragged_advance_kernel, dim3((unsigned)((B + 127) / 128)), dim3(128), 0,
+                          st, lens, counts, S, B, cap));
+  return KVQ_OK;
 }
 
 int32_t launch_quantize_rows(const void* x, int64_t rows, RowGeom g, int dtype, uint32_t* packed,

@@ -28,7 +28,8 @@ EXPORTS = (
     "kvq_sdpa_merge", "kvq_sdpa_prefill", "kvq_debug_scores", "kvq_check_device",
     "kvq_sdpa_decode_noalloc", "kvq_debug_raise_flag", "kvq_peer_group_create",
     "kvq_peer_group_connect", "kvq_peer_exchange_merge", "kvq_peer_group_check",
-    "kvq_peer_group_free",
+    "kvq_peer_group_free", "kvq_append_ragged", "kvq_cache_fetch_all", "kvq_cache_check",
+    "kvq_cache_from_dense", "kvq_cache_export", "kvq_cache_import",
 )
 
 
@@ -94,6 +95,13 @@ def lib():
         "kvq_peer_exchange_merge": (i32, [vp, vp, i32, vp, vp]),
         "kvq_peer_group_check": (i32, [vp, vp]),
         "kvq_peer_group_free": (i32, [vp]),
+        "kvq_append_ragged": (i32, [vp, vp, vp, i32, P(i64), P(i64), vp, vp, vp]),
+        "kvq_cache_fetch_all": (i32, [vp, P(QTensor), P(QTensor)]),
+        "kvq_cache_check": (i32, [vp, vp]),
+        "kvq_cache_from_dense": (i32, [P(Desc), vp, vp, i32, P(i64), P(i64), i64, i64, vp,
+                                       P(vp)]),
+        "kvq_cache_export": (i32, [vp, i64, P(vp), vp]),
+        "kvq_cache_import": (i32, [P(Desc), P(vp), i32, i64, i64, vp, P(vp)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -186,6 +186,114 @@ class _CacheBase:
         dev = self._shape[4]
         return QuantizedTensor(kq, dev, self), QuantizedTensor(vq, dev, self)
 
+    # ---- batched serving: per-sequence positions on the device ----
+
+    def append_ragged(self, k: torch.Tensor, v: torch.Tensor, seq_lens: torch.Tensor,
+                      counts: torch.Tensor | None = None, stream=None):
+        """Entry b writes its first counts[b] (all S when None) rows of k / v
+        [B, H, S, D] at rows seq_lens[b]..., then seq_lens[b] += counts[b] —
+        on the device (kvq_append_ragged).  The cache must be a growing one
+        created with reserve_rows (its capacity).  Returns fetch_all()."""
+        if k.shape != v.shape or not k.is_cuda or not v.is_cuda:
+            raise ValueError("k and v must be CUDA tensors of one shape")
+        for t in (seq_lens,) + ((counts,) if counts is not None else ()):
+            if t.dtype != torch.int32 or not t.is_cuda or t.numel() != k.shape[0] or \
+                    not t.is_contiguous():
+                raise ValueError("seq_lens / counts must be contiguous CUDA int32 [B]")
+        if not self.reserve_rows:
+            raise ValueError("ragged appends need reserve_rows (the capacity) at creation")
+        self._ensure(k)
+        st = torch.cuda.current_stream(k.device).cuda_stream if stream is None else stream
+        check(lib().kvq_append_ragged(self._h, k.data_ptr(), v.data_ptr(), k.shape[2],
+                                      _strides4(k), _strides4(v), seq_lens.data_ptr(),
+                                      counts.data_ptr() if counts is not None else None, st))
+        return self.fetch_all()
+
+    def fetch_all(self):
+        """Views over the whole capacity, for decode with per-sequence seq_lens."""
+        kq, vq = QTensor(), QTensor()
+        check(lib().kvq_cache_fetch_all(self._h, ctypes.byref(kq), ctypes.byref(vq)))
+        dev = self._shape[4]
+        return QuantizedTensor(kq, dev, self), QuantizedTensor(vq, dev, self)
+
+    def check(self, stream=None):
+        """Raise if a ragged append skipped an entry past the capacity."""
+        if self._h.value is not None:
+            check(lib().kvq_cache_check(self._h, stream))
+
+    # ---- conversion and persistence ----
+
+    @classmethod
+    def _adopt(cls, h, shape, max_size, group_size, bits, reserve_rows=0):
+        obj = cls.__new__(cls)
+        _CacheBase.__init__(obj, max_size, group_size, bits, reserve_rows)
+        obj._h = h
+        obj._shape = shape
+        return obj
+
+    @classmethod
+    def _from_dense(cls, keys, values, offset, ring_idx, max_size, group_size, bits,
+                    reserve_rows=0, stream=None):
+        if keys.shape[:3] != values.shape[:3] or keys.shape[3] != values.shape[3]:
+            raise ValueError("keys and values must have one shape [B, H, rows, D]")
+        if not keys.is_cuda or not values.is_cuda or keys.dtype != values.dtype:
+            raise ValueError("keys and values must be CUDA tensors of one dtype")
+        B, H, rows, D = keys.shape
+        dev = keys.device.index
+        d = _lib.Desc(B, H, D, bits, group_size, dtype_code(keys.dtype), max_size, reserve_rows,
+                      dev)
+        st = torch.cuda.current_stream(keys.device).cuda_stream if stream is None else stream
+        h = ctypes.c_void_p()
+        check(lib().kvq_cache_from_dense(ctypes.byref(d), keys.data_ptr(), values.data_ptr(),
+                                         rows, _strides4(keys), _strides4(values), int(offset),
+                                         int(ring_idx), st, ctypes.byref(h)))
+        return cls._adopt(h, (B, H, D, keys.dtype, dev), max_size, group_size, bits, reserve_rows)
+
+    def export(self):
+        """Host copy of the saved region and the state, as mlx-bun persists a
+        cache (src/kv-store.ts:54-123): a growing cache keeps its live
+        [0:offset] rows, a ring its whole buffer and ring index.  Returns
+        dict(kind, offset, idx, max_size, bits, group_size, dtype, shape,
+        tensors = [k packed, k scales, k biases, v packed, v scales,
+        v biases] as numpy arrays)."""
+        import numpy as np
+        if self._h.value is None:
+            raise ValueError("cannot persist an empty cache")
+        B, H, D, dt, dev = self._shape
+        offset, ring_idx, seq_len, _ = self._state()
+        rows = seq_len if self.max_size else offset
+        G, W = D // self.group_size, D * self.bits // 32
+        arrs = [np.empty((B, H, rows, W), np.uint32), np.empty((B, H, rows, G), np.uint16),
+                np.empty((B, H, rows, G), np.uint16), np.empty((B, H, rows, W), np.uint32),
+                np.empty((B, H, rows, G), np.uint16), np.empty((B, H, rows, G), np.uint16)]
+        ptrs = (ctypes.c_void_p * 6)(*[a.ctypes.data for a in arrs])
+        with torch.cuda.device(dev):
+            torch.cuda.synchronize()
+            check(lib().kvq_cache_export(self._h, rows, ptrs, None))
+        return dict(kind="rotating-kvq" if self.max_size else "kvq", offset=offset,
+                    idx=ring_idx if self.max_size else None,
+                    max_size=self.max_size or None, bits=self.bits, group_size=self.group_size,
+                    dtype=dtype_code(dt), shape=[B, H, rows, D], tensors=arrs)
+
+    @staticmethod
+    def from_export(state, device: int = 0, reserve_rows: int = 0):
+        """The cache `export` described, on `device` (loadKvCache +
+        restoreState, src/kv-store.ts:147-175)."""
+        import numpy as np
+        B, H, rows, D = state["shape"]
+        max_size = state.get("max_size") or 0
+        d = _lib.Desc(B, H, D, state["bits"], state["group_size"], state["dtype"], max_size,
+                      reserve_rows, device)
+        arrs = [np.ascontiguousarray(a) for a in state["tensors"]]
+        ptrs = (ctypes.c_void_p * 6)(*[a.ctypes.data for a in arrs])
+        h = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            check(lib().kvq_cache_import(ctypes.byref(d), ptrs, rows, int(state["offset"]),
+                                         int(state.get("idx") or 0), None, ctypes.byref(h)))
+        cls = RotatingQuantizedKVCache if max_size else QuantizedKVCache
+        return cls._adopt(h, (B, H, D, torch_dtype(state["dtype"]), device), max_size,
+                          state["group_size"], state["bits"], reserve_rows)
+
     def _state(self):
         vals = [ctypes.c_int64() for _ in range(4)]
         if self._h.value is None:
@@ -254,6 +362,13 @@ class QuantizedKVCache(_CacheBase):
     def __init__(self, group_size: int = 64, bits: int = 8, reserve_rows: int = 0):
         super().__init__(0, group_size, bits, reserve_rows)
 
+    @classmethod
+    def from_dense(cls, keys: torch.Tensor, values: torch.Tensor, offset: int,
+                   group_size: int = 64, bits: int = 8, reserve_rows: int = 0, stream=None):
+        """KVCache.toQuantized (gemma4-base.ts:395-404): quantize the whole
+        dense buffer [B, H, rows, D] (padding included) and adopt offset."""
+        return cls._from_dense(keys, values, offset, 0, 0, group_size, bits, reserve_rows, stream)
+
     def is_trimmable(self) -> bool:
         return True
 
@@ -271,6 +386,18 @@ class RotatingQuantizedKVCache(_CacheBase):
     @property
     def ring_idx(self) -> int:
         return self._state()[1]
+
+    @classmethod
+    def from_dense(cls, keys: torch.Tensor, values: torch.Tensor, offset: int, ring_idx: int,
+                   max_size: int, group_size: int = 64, bits: int = 8, reserve_rows: int = 0,
+                   stream=None):
+        """RotatingKVCache.toQuantized (gemma4-base.ts:892-902): quantize the
+        ring as laid out (ring order, not temporal) and adopt offset and
+        ring index."""
+        if max_size <= 0:
+            raise ValueError("max_size must be positive")
+        return cls._from_dense(keys, values, offset, ring_idx, max_size, group_size, bits,
+                               reserve_rows, stream)
 
     def is_trimmable(self) -> bool:
         return self.offset < self.max_size

@@ -12,6 +12,13 @@ Two parts:
   line by line from ``src/model/gemma4-base.ts``:
     - ``QuantizedKVCache``        (:419-598)   growing, 256-row steps
     - ``RotatingQuantizedKVCache`` (:932-1261) sliding-window ring, keep=0
+  and of their dense (bf16 / fp16) originals, whose mechanics the quantized
+  classes port step for step, with ``to_quantized``:
+    - ``KVCache``        (:255-404, toQuantized :395-404)
+    - ``RotatingKVCache`` (:604-902, toQuantized :892-902)
+* ``save_kv`` / ``load_kv``: the MLXBUNKV1 file layout of ``src/kv-store.ts``
+  (magic, u32 header length, u32 data start, JSON header, 16 KiB-aligned
+  tensors) over numpy arrays, for checking the product's writer and reader.
 
 The oracle's quantize rule is pinned bit-exactly by
 ``tests/golden/rotating_kvq_mechanics.npz`` (bf16, gs 32, 8 bit), which was
@@ -179,6 +186,14 @@ class QuantizedKVCache:
         self.values = None
         self.offset = 0
 
+    # the stored form of new rows and of appended zeros (a triple here, the
+    # raw dtype bits in the dense subclasses)
+    def _enc(self, x_bits):
+        return list(quantize(x_bits, self.group_size, self.bits, self.dtype))
+
+    def _blank(self, B, H, T, D):
+        return _triple_zeros(B, H, T, D, self.group_size, self.bits)
+
     def update_and_fetch(self, k_bits: np.ndarray, v_bits: np.ndarray):
         """updateAndFetchQuantized (:452-507); k/v [B, H, L, D] uint16 bits."""
         B, H, L, kD = k_bits.shape
@@ -189,16 +204,16 @@ class QuantizedKVCache:
             if self.keys is not None and prev % STEP != 0:
                 self.keys = [a[:, :, :prev] for a in self.keys]
                 self.values = [a[:, :, :prev] for a in self.values]
-            nk = _triple_zeros(B, H, new_steps, kD, self.group_size, self.bits)
-            nv = _triple_zeros(B, H, new_steps, vD, self.group_size, self.bits)
+            nk = self._blank(B, H, new_steps, kD)
+            nv = self._blank(B, H, new_steps, vD)
             if self.keys is None:
                 self.keys, self.values = nk, nv
             else:
                 self.keys = [_cat(a, z) for a, z in zip(self.keys, nk)]
                 self.values = [_cat(a, z) for a, z in zip(self.values, nv)]
         self.offset += L
-        kq = quantize(k_bits, self.group_size, self.bits, self.dtype)
-        vq = quantize(v_bits, self.group_size, self.bits, self.dtype)
+        kq = self._enc(k_bits)
+        vq = self._enc(v_bits)
         for dst, src in ((self.keys, kq), (self.values, vq)):
             for a, s in zip(dst, src):
                 a[:, :, prev:self.offset] = s
@@ -227,6 +242,12 @@ class RotatingQuantizedKVCache:
         self.offset = 0
         self.ring_idx = 0
 
+    def _enc(self, x_bits):
+        return list(quantize(x_bits, self.group_size, self.bits, self.dtype))
+
+    def _blank(self, B, H, T, D):
+        return _triple_zeros(B, H, T, D, self.group_size, self.bits)
+
     @property
     def seq_len(self):
         return 0 if self.keys is None else self.keys[0].shape[2]
@@ -248,8 +269,8 @@ class RotatingQuantizedKVCache:
 
     def _update_concat(self, k, v):  # :1003-1024
         S = k.shape[2]
-        kq = list(quantize(k, self.group_size, self.bits, self.dtype))
-        vq = list(quantize(v, self.group_size, self.bits, self.dtype))
+        kq = self._enc(k)
+        vq = self._enc(v)
         if self.keys is None:
             self.keys, self.values = kq, vq
         else:
@@ -271,8 +292,8 @@ class RotatingQuantizedKVCache:
             new_size = min(STEP, self.max_size - prev)
             if new_size <= 0:
                 raise ValueError("rotating cache: non-positive growth")
-            nk = _triple_zeros(B, H, new_size, D, self.group_size, self.bits)
-            nv = _triple_zeros(B, H, new_size, vD, self.group_size, self.bits)
+            nk = self._blank(B, H, new_size, D)
+            nv = self._blank(B, H, new_size, vD)
             if self.keys is None:
                 self.keys, self.values = nk, nv
             else:
@@ -286,8 +307,8 @@ class RotatingQuantizedKVCache:
             self.ring_idx = self.max_size
         if self.ring_idx == self.max_size:
             self.ring_idx = 0
-        kq = quantize(k, self.group_size, self.bits, self.dtype)
-        vq = quantize(v, self.group_size, self.bits, self.dtype)
+        kq = self._enc(k)
+        vq = self._enc(v)
         self.keys = [a.copy() for a in self.keys]
         self.values = [a.copy() for a in self.values]
         for dst, src in ((self.keys, kq), (self.values, vq)):
@@ -323,6 +344,105 @@ class RotatingQuantizedKVCache:
             self.ring_idx = self.seq_len
         else:
             self.ring_idx -= k
+
+
+class KVCache(QuantizedKVCache):
+    """Dense growing cache (gemma4-base.ts:255-404): the same mechanics with
+    raw dtype rows; keys / values are one-element lists [B, H, T, D]."""
+
+    def __init__(self, dtype: int):
+        super().__init__(64, 8, dtype)
+
+    def _enc(self, x_bits):
+        return [np.ascontiguousarray(x_bits, dtype=np.uint16)]
+
+    def _blank(self, B, H, T, D):
+        return [_zeros(B, H, T, D, np.uint16)]
+
+    def to_quantized(self, group_size: int, bits: int):
+        """toQuantized (:395-404): the whole buffer, padding included."""
+        q = QuantizedKVCache(group_size, bits, self.dtype)
+        q.offset = self.offset
+        if self.keys is not None:
+            q.keys = list(quantize(self.keys[0], group_size, bits, self.dtype))
+            q.values = list(quantize(self.values[0], group_size, bits, self.dtype))
+        return q
+
+
+class RotatingKVCache(RotatingQuantizedKVCache):
+    """Dense sliding-window ring (gemma4-base.ts:604-902), keep = 0."""
+
+    def __init__(self, max_size: int, dtype: int):
+        super().__init__(max_size, 64, 8, dtype)
+
+    def _enc(self, x_bits):
+        return [np.ascontiguousarray(x_bits, dtype=np.uint16)]
+
+    def _blank(self, B, H, T, D):
+        return [_zeros(B, H, T, D, np.uint16)]
+
+    def to_quantized(self, group_size: int, bits: int):
+        """toQuantized (:892-902): the ring as laid out, state carried over."""
+        q = RotatingQuantizedKVCache(self.max_size, group_size, bits, self.dtype)
+        if self.keys is not None:
+            q.keys = list(quantize(self.keys[0], group_size, bits, self.dtype))
+            q.values = list(quantize(self.values[0], group_size, bits, self.dtype))
+        q.offset = self.offset
+        q.ring_idx = self.ring_idx
+        return q
+
+
+# ------------------------------------------------------- MLXBUNKV1 files ---
+
+KV_MAGIC = b"MLXBUNKV1\n"
+KV_ALIGN = 16384
+
+
+def _align_up(n):
+    return (n + KV_ALIGN - 1) // KV_ALIGN * KV_ALIGN
+
+
+def save_kv(path, tokens, entries):
+    """Write the MLXBUNKV1 layout of src/kv-store.ts:54-123: magic, u32 LE
+    header length, u32 LE data start, JSON header, then each tensor at a
+    16 KiB-aligned offset relative to the data start.  `entries`: list of
+    (header dict without tensor offsets, list of (name, numpy array)); the
+    writer adds {name}Offset / {name}Bytes keys per tensor."""
+    import json
+    hdr_entries, blobs, off = [], [], 0
+    for meta, tensors in entries:
+        e = dict(meta)
+        for name, a in tensors:
+            b = np.ascontiguousarray(a).tobytes()
+            o = _align_up(off)
+            e[name + "Offset"], e[name + "Bytes"] = o, len(b)
+            blobs.append((o, b))
+            off = o + len(b)
+        hdr_entries.append(e)
+    hj = json.dumps({"tokens": list(tokens), "caches": hdr_entries}).encode()
+    start = _align_up(len(KV_MAGIC) + 8 + len(hj))
+    with open(path, "wb") as f:
+        pre = bytearray(start)
+        pre[:len(KV_MAGIC)] = KV_MAGIC
+        pre[len(KV_MAGIC):len(KV_MAGIC) + 4] = len(hj).to_bytes(4, "little")
+        pre[len(KV_MAGIC) + 4:len(KV_MAGIC) + 8] = start.to_bytes(4, "little")
+        pre[len(KV_MAGIC) + 8:len(KV_MAGIC) + 8 + len(hj)] = hj
+        f.write(pre)
+        for o, b in blobs:
+            f.seek(start + o)
+            f.write(b)
+
+
+def load_kv(path):
+    """Read an MLXBUNKV1 file: (header dict, data start, raw bytes)."""
+    import json
+    raw = open(path, "rb").read()
+    if raw[:len(KV_MAGIC)] != KV_MAGIC:
+        raise ValueError("not an mlx-bun KV cache file")
+    n = int.from_bytes(raw[len(KV_MAGIC):len(KV_MAGIC) + 4], "little")
+    start = int.from_bytes(raw[len(KV_MAGIC) + 4:len(KV_MAGIC) + 8], "little")
+    hdr = json.loads(raw[len(KV_MAGIC) + 8:len(KV_MAGIC) + 8 + n])
+    return hdr, start, raw
 
 
 def make_mask(N: int, offset: int, window):
