@@ -1570,17 +1570,32 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
 }
 
 // Combine the partial slots of unit blockIdx.x for query row blockIdx.y;
-// blockDim.x == D, thread d.  Slots are taken 32 at a time: every thread
-// loads the batch's (m, l) and its own o[d] in one round (coalesced across
-// d), then folds the batch into a running (M, L, o) in slot order
-// (deterministic, the same sums in every thread).
+// blockDim.x == MG * D: thread (group gi, column d).  The unit's slots are
+// cut into G <= MG contiguous runs of at least 32 (one run when there are
+// few); group gi folds run gi 32 slots at a time — every
+// thread loads the batch's (m, l) and its own o[d] in one round (coalesced
+// across d) — into a running (M, L, o) in slot order, and group 0 combines
+// the runs in run order (deterministic: the same sums in every thread and
+// on every call with these shapes).  Long units spread over many CTAs (one
+// long sequence) thus merge in a quarter of the rounds.
 constexpr int kMergeSlots = 4096;  // partial slots per unit at most (launch shape)
-template <int D, int W, int NT, bool BF>
-__global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int grid) {
+// Slot groups of the wide merge (512 threads a block, registers for the
+// 32-slot batches); the narrow merge (MG = 1, D threads) serves launches
+// whose units have few slots each, where extra groups would sit idle.
+template <int D>
+constexpr int merge_groups() {
+  return 512 / D;
+}
+constexpr int kWideMergeSlots = 64;  // slots per unit above which the wide merge runs
+template <int D, int W, int NT, bool BF, int MG>
+__global__ void __launch_bounds__(MG * D) attn_bal_merge_kernel(const Params p, int grid) {
   constexpr int HQ = 8 * NT;
   constexpr int SLOT = HQ * (D + 2);  // floats per partial slot
   __shared__ int64_t red_t[2];
+  __shared__ float run_ml[MG][2];
+  __shared__ float run_o[MG][D];
   const int u = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
+  const int gi = tid / D, d = tid - gi * D;
   const int Hkv = p.Hkv, b = u / Hkv, kvh = u - b * Hkv;
   const int64_t orow = (int64_t)b * p.Hq + kvh * p.nrep + r;
 
@@ -1598,7 +1613,7 @@ __global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int g
     // without this wait the merge could run ahead of the append.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     int64_t before = 0, all = 0;
-    for (int bb = tid; bb < p.B; bb += D) {
+    for (int bb = tid; bb < p.B; bb += blockDim.x) {
       const int n = min(max(p.seq_lens[bb], 0), p.N);
       const int64_t tb = (int64_t)Hkv * ((n + kTile - 1) / kTile);
       all += tb;
@@ -1628,42 +1643,68 @@ __global__ void __launch_bounds__(D) attn_bal_merge_kernel(const Params p, int g
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (T == 0) {  // an entry with no keys: a zero row (or an empty partial)
-    write_row<D, BF>(p, orow, tid, 0.0f, kNeg, 0.0f);
+    if (gi == 0) write_row<D, BF>(p, orow, d, 0.0f, kNeg, 0.0f);
     return;
   }
   const int C = bal_working_ctas(RT, grid);
   const int i_first = (int)(((U + 1) * C - 1) / RT);
   const int i_last = (int)(((U + T) * C - 1) / RT);
   const int nslots = (i_last - i_first + 1) * W;  // <= kMergeSlots (host launch shape)
+  const int G = min(MG, (nslots + 31) / 32);
   const float* base = p.ws_o + ((int64_t)i_first + u) * W * SLOT;
 
   float M = kNeg, L = 0.0f, acc = 0.0f;
-  for (int j0 = 0; j0 < nslots; j0 += 32) {
-    const int nj = min(32, nslots - j0);
-    float m[32], l[32], o[32];
+  if (gi < G) {
+    const int s0 = (int)((int64_t)gi * nslots / G), s1 = (int)((int64_t)(gi + 1) * nslots / G);
+    for (int j0 = s0; j0 < s1; j0 += 32) {
+      const int nj = min(32, s1 - j0);
+      float m[32], l[32], o[32];
 #pragma unroll
-    for (int k = 0; k < 32; k++) {
-      const bool v = k < nj;
-      const float* sp = base + (int64_t)(j0 + k) * SLOT;
-      m[k] = v ? __ldcg(sp + r) : kNeg;
-      l[k] = v ? __ldcg(sp + HQ + r) : 0.0f;
-      o[k] = v ? __ldcg(sp + 2 * HQ + r * D + tid) : 0.0f;
+      for (int k = 0; k < 32; k++) {
+        const bool v = k < nj;
+        const float* sp = base + (int64_t)(j0 + k) * SLOT;
+        m[k] = v ? __ldcg(sp + r) : kNeg;
+        l[k] = v ? __ldcg(sp + HQ + r) : 0.0f;
+        o[k] = v ? __ldcg(sp + 2 * HQ + r * D + d) : 0.0f;
+      }
+      float Mn = M;
+#pragma unroll
+      for (int k = 0; k < 32; k++) Mn = fmaxf(Mn, m[k]);
+      const float a = ex2((M - Mn) * kLog2e);
+      L *= a;
+      acc *= a;
+#pragma unroll
+      for (int k = 0; k < 32; k++) {
+        const float w = ex2((m[k] - Mn) * kLog2e);
+        L = fmaf(l[k], w, L);
+        acc = fmaf(o[k], w, acc);
+      }
+      M = Mn;
     }
-    float Mn = M;
-#pragma unroll
-    for (int k = 0; k < 32; k++) Mn = fmaxf(Mn, m[k]);
-    const float a = ex2((M - Mn) * kLog2e);
-    L *= a;
-    acc *= a;
-#pragma unroll
-    for (int k = 0; k < 32; k++) {
-      const float w = ex2((m[k] - Mn) * kLog2e);
-      L = fmaf(l[k], w, L);
-      acc = fmaf(o[k], w, acc);
-    }
-    M = Mn;
   }
-  write_row<D, BF>(p, orow, tid, acc, M, L);
+  if (G == 1) {
+    if (gi == 0) write_row<D, BF>(p, orow, d, acc, M, L);
+    return;
+  }
+  if (gi < G) {
+    run_o[gi][d] = acc;
+    if (d == 0) {
+      run_ml[gi][0] = M;
+      run_ml[gi][1] = L;
+    }
+  }
+  __syncthreads();
+  if (gi == 0) {
+    float Mt = kNeg;
+    for (int k = 0; k < G; k++) Mt = fmaxf(Mt, run_ml[k][0]);
+    float Lt = 0.0f, At = 0.0f;
+    for (int k = 0; k < G; k++) {
+      const float w = ex2((run_ml[k][0] - Mt) * kLog2e);
+      Lt = fmaf(run_ml[k][1], w, Lt);
+      At = fmaf(run_o[k][d], w, At);
+    }
+    write_row<D, BF>(p, orow, d, At, Mt, Lt);
+  }
 }
 
 // ------------------------------------------------------------ host side --
@@ -1779,10 +1820,16 @@ int32_t launch_rw(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* 
   if (bal) {
     // merge of the per-warp partials, a programmatic dependent of the
     // attention grid (it waits for that grid inside, with griddepcontrol)
-    void (*merge)(Params, int) = p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true>
-                                        : attn_bal_merge_kernel<D, kWarps, NT, false>;
-    KVQ_CUDA_TRY(launch_pdl(merge, dim3((unsigned)(B * p.Hkv), (unsigned)p.nrep), dim3(D), 0, st,
-                            p, s.ctas));
+    // (wide when the units have many slots each: one long sequence)
+    constexpr int MG = merge_groups<D>();
+    const bool wide = (int64_t)s.ctas * kWarps > (int64_t)kWideMergeSlots * B * p.Hkv;
+    void (*merge)(Params, int) =
+        wide ? (p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true, MG>
+                       : attn_bal_merge_kernel<D, kWarps, NT, false, MG>)
+             : (p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true, 1>
+                       : attn_bal_merge_kernel<D, kWarps, NT, false, 1>);
+    KVQ_CUDA_TRY(launch_pdl(merge, dim3((unsigned)(B * p.Hkv), (unsigned)p.nrep),
+                            dim3((wide ? MG : 1) * D), 0, st, p, s.ctas));
   }
   return KVQ_OK;
 }

@@ -19,14 +19,15 @@
 // exchange_merge_kernel, one launch per step, grid = nranks CTAs:
 //   * every CTA reads the step's epoch e = epoch + 1 (parity e & 1);
 //   * CTA t copies this rank's packed partial into slot [parity][rank] of
-//     rank t's buffer with plain 16-byte stores over NVLink, fences at
-//     system scope, and sets rank t's arrival flag [rank] to e with a
-//     release store;
+//     rank t's buffer with plain 16-byte stores over NVLink and, after a
+//     block barrier, sets rank t's arrival flag [rank] to e with one
+//     release store at system scope;
 //   * every CTA then waits (acquire loads, bounded: 2 s of %globaltimer,
 //     after which it raises the error flag) until all nranks arrival flags
 //     of its own buffer reach e, and merges rows [t*rows/n, (t+1)*rows/n)
-//     of the nranks slots in rank order — the same sums in the same order
-//     on every rank, so all ranks produce identical outputs;
+//     of the nranks slots in rank order, four columns per thread with every
+//     rank's loads in flight together — the same sums in the same order on
+//     every rank, so all ranks produce identical outputs;
 //   * the last CTA to finish (ticket) stores epoch = e.
 // Two parities make the buffers reusable without a second handshake: a
 // rank stores parity p of step e + 2 only after it has seen every rank's
@@ -51,7 +52,7 @@ namespace peer {
 constexpr int kMaxRanks = 48;
 constexpr int kHeader = 256;              // bytes before the data slots
 constexpr int kFlagOff = 64;              // arrival flags (u32 per rank)
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
 constexpr long long kWaitPolls = 1ll << 30;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
@@ -86,6 +87,48 @@ __device__ __forceinline__ uint16_t to_dt(float f) {
   }
 }
 
+// Merge of one float4 of output columns (row r, columns 4c..4c+3) over
+// the NR slots at `base` (slot stride `slot` floats), in slot order.  All
+// loads are issued before any arithmetic that needs them.
+template <int NR, bool BF>
+__device__ __forceinline__ void merge4(const float* base, int64_t slot, int rows, int D, int r,
+                                       int c, int nr, uint16_t* out) {
+  float m[NR], l[NR];
+  float4 o[NR];
+#pragma unroll
+  for (int pp = 0; pp < NR; pp++) {
+    if (pp < nr) {
+      const float* sp = base + pp * slot;
+      m[pp] = __ldcg(sp + r);
+      l[pp] = __ldcg(sp + rows + r);
+      o[pp] = __ldcg(reinterpret_cast<const float4*>(sp + 2 * rows + (int64_t)r * D) + c);
+    } else {
+      m[pp] = -1.0e30f;
+      l[pp] = 0.0f;
+      o[pp] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+  }
+  float M = -1.0e30f;
+#pragma unroll
+  for (int pp = 0; pp < NR; pp++) M = fmaxf(M, m[pp]);
+  float Ls = 0.0f;
+  float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+  for (int pp = 0; pp < NR; pp++) {
+    const float w = exp2f((m[pp] - M) * 1.4426950408889634f);
+    Ls = fmaf(l[pp], w, Ls);
+    O.x = fmaf(o[pp].x, w, O.x);
+    O.y = fmaf(o[pp].y, w, O.y);
+    O.z = fmaf(o[pp].z, w, O.z);
+    O.w = fmaf(o[pp].w, w, O.w);
+  }
+  const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
+  uint2 v;
+  v.x = (uint32_t)to_dt<BF>(O.x * inv) | ((uint32_t)to_dt<BF>(O.y * inv) << 16);
+  v.y = (uint32_t)to_dt<BF>(O.z * inv) | ((uint32_t)to_dt<BF>(O.w * inv) << 16);
+  *reinterpret_cast<uint2*>(out + (int64_t)r * D + 4 * c) = v;
+}
+
 template <bool BF>
 __global__ void __launch_bounds__(kThreads) exchange_merge_kernel(const Ptrs ptrs, int nranks,
                                                                   int rank, int rows, int D,
@@ -100,9 +143,7 @@ __global__ void __launch_bounds__(kThreads) exchange_merge_kernel(const Ptrs ptr
   const int tid = threadIdx.x, t = blockIdx.x;
   uint8_t* mine = ptrs.buf[rank];
   unsigned* hdr = reinterpret_cast<unsigned*>(mine);
-  if (tid == 0) {
-    s_epoch = *reinterpret_cast<volatile unsigned*>(hdr + 1) + 1u;
-  }
+  if (tid == 0) s_epoch = *reinterpret_cast<volatile unsigned*>(hdr + 1) + 1u;
   __syncthreads();
   const unsigned e = s_epoch;
   const int64_t par = e & 1u;
@@ -116,7 +157,9 @@ __global__ void __launch_bounds__(kThreads) exchange_merge_kernel(const Ptrs ptr
     for (int64_t k = tid; k < n4; k += kThreads)
       reinterpret_cast<float4*>(dst)[k] = __ldg(reinterpret_cast<const float4*>(local) + k);
     for (int64_t k = n4 * 4 + tid; k < P; k += kThreads) dst[k] = __ldg(local + k);
-    __threadfence_system();
+    // The barrier orders every thread's stores before thread 0's release
+    // store at system scope, which makes them visible to the rank that
+    // acquires the flag.
     __syncthreads();
     if (tid == 0)
       st_release_sys(reinterpret_cast<unsigned*>(ptrs.buf[t] + kFlagOff) + rank, e);
@@ -136,21 +179,34 @@ __global__ void __launch_bounds__(kThreads) exchange_merge_kernel(const Ptrs ptr
   }
   __syncthreads();
 
-  // ---- merge rows [r0, r1) in rank order ----
+  // ---- merge rows [r0, r1), four columns per thread, in rank order ----
   const int r0 = (int)((int64_t)t * rows / nranks), r1 = (int)((int64_t)(t + 1) * rows / nranks);
   const float* base = reinterpret_cast<const float*>(mine + kHeader) + par * nranks * slot;
-  for (int64_t i = (int64_t)r0 * D + tid; i < (int64_t)r1 * D; i += kThreads) {
-    const int r = (int)(i / D), d = (int)(i - (int64_t)r * D);
-    float M = -1.0e30f;
-    for (int pp = 0; pp < nranks; pp++) M = fmaxf(M, __ldcg(base + pp * slot + r));
-    float Ls = 0.0f, O = 0.0f;
-    for (int pp = 0; pp < nranks; pp++) {
-      const float* sp = base + pp * slot;
-      const float w = exp2f((__ldcg(sp + r) - M) * 1.4426950408889634f);
-      Ls = fmaf(__ldcg(sp + rows + r), w, Ls);
-      O = fmaf(__ldcg(sp + 2 * rows + (int64_t)r * D + d), w, O);
+  const int D4 = D / 4;
+  if ((rows & 1) == 0 && (D & 3) == 0 && nranks <= 8) {  // float4 columns stay 16-byte aligned
+    for (int64_t i = (int64_t)r0 * D4 + tid; i < (int64_t)r1 * D4; i += kThreads) {
+      const int r = (int)(i / D4), c = (int)(i - (int64_t)r * D4);
+      if (nranks <= 2)
+        merge4<2, BF>(base, slot, rows, D, r, c, nranks, out);
+      else if (nranks <= 4)
+        merge4<4, BF>(base, slot, rows, D, r, c, nranks, out);
+      else
+        merge4<8, BF>(base, slot, rows, D, r, c, nranks, out);
     }
-    out[i] = to_dt<BF>(Ls > 0.0f ? O / Ls : 0.0f);
+  } else {
+    for (int64_t i = (int64_t)r0 * D + tid; i < (int64_t)r1 * D; i += kThreads) {
+      const int r = (int)(i / D), d = (int)(i - (int64_t)r * D);
+      float M = -1.0e30f;
+      for (int pp = 0; pp < nranks; pp++) M = fmaxf(M, __ldcg(base + pp * slot + r));
+      float Ls = 0.0f, O = 0.0f;
+      for (int pp = 0; pp < nranks; pp++) {
+        const float* sp = base + pp * slot;
+        const float w = exp2f((__ldcg(sp + r) - M) * 1.4426950408889634f);
+        Ls = fmaf(__ldcg(sp + rows + r), w, Ls);
+        O = fmaf(__ldcg(sp + 2 * rows + (int64_t)r * D + d), w, O);
+      }
+      out[i] = to_dt<BF>(Ls > 0.0f ? O / Ls : 0.0f);
+    }
   }
 
   // ---- the last CTA to finish advances the epoch ----
