@@ -584,9 +584,10 @@ def prefill_flops(c):
     return 4 * c["Hq"] * c["L"] * c["D"] * (c["N_prior"] + (c["L"] + 1) / 2)
 
 
-def run_prefill(args):
+def run_prefill(args, bits=8):
     """Config 4: chunked prefill of 512 query rows (causal in the chunk) over a
-    kv8 cache of 16,384 prior rows plus the chunk, appended first.  One step =
+    kv8 cache of 16,384 prior rows plus the chunk, appended first (with
+    bits=4, the same shape over a kv4 cache: the warp-specialised kernel).  One step =
     append of the 512 K/V rows + prefill attention; both timed with CUDA
     events over graph replays of NL distinct layers; the attention alone
     (the tensor-core kernel and the merge of units cut between its CTAs) is
@@ -596,10 +597,10 @@ def run_prefill(args):
     import kvq
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    c = CFG4
+    c = dict(CFG4, bits=bits)
     B, Hq, Hkv, D, Np, L = c["B"], c["Hq"], c["Hkv"], c["D"], c["N_prior"], c["L"]
     scale = 1.0 / np.sqrt(D)
-    NL = 4  # 4 x 36.8 MB of K/V: above L2 across a replay
+    NL = 4 if bits == 8 else 8  # 147 MB of K/V cycled per replay: above L2
     g = torch.Generator(device=device)
     g.manual_seed(11)
     layers = []
@@ -662,19 +663,21 @@ def run_prefill(args):
     except Exception:
         peak, pk = 1590.0, "fallback"
     att_tf = fl / (att_ms / 1e3) / 1e12
+    kern = ("prefill_tc_kernel (tcgen05 UMMA, TMEM accumulators) + prefill_tc_merge_kernel"
+            if bits == 8 else
+            "prefill_tc2_kernel (warp-specialised tcgen05, K as fp16 hi + lo) + "
+            "prefill_tc_merge_kernel")
     print(json.dumps({
-        "metric": "quantized-KV chunked prefill TFLOP/s (config 4: B1 Hq32 Hkv8 D128, 16384 "
-                  "prior + 512-row causal chunk, kv8 gs64)",
+        "metric": f"quantized-KV chunked prefill TFLOP/s (config 4: B1 Hq32 Hkv8 D128, 16384 "
+                  f"prior + 512-row causal chunk, kv{bits} gs64)",
         "value": round(fl / (step_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": 1,
         "steps": reps * NL, "warmup": args.warmup, "ms_per_step": round(step_ms, 5),
-        "higher_is_better": True, "dtype": "u8 codes/f16", "data": "synthetic (seeded torch.randn)",
-        "config": {"workload": "config4-kv8-prefill-append", "flops_per_step": fl,
-                   "layers_cycled": NL, "l2": "4 distinct layers (147 MB of K/V) per replay"},
+        "higher_is_better": True, "dtype": f"u{bits} codes/f16", "data": "synthetic (seeded torch.randn)",
+        "config": {"workload": f"config4-kv{bits}-prefill-append", "flops_per_step": fl,
+                   "layers_cycled": NL, "l2": f"{NL} distinct layers (147 MB of K/V) per replay"},
         "roofline": {"bound": "tensor", "achieved": round(att_tf, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(att_tf / peak, 4), "peak_kind": pk,
-                     "kernel": "prefill_tc_kernel (tcgen05 UMMA, TMEM accumulators) + "
-                               "prefill_tc_merge_kernel",
-                     "kernel_us": round(att_ms * 1e3, 3)},
+                     "kernel": kern, "kernel_us": round(att_ms * 1e3, 3)},
         "gpu_launches": 3 * reps * NL, "clocks": t1.clk}))
 
 
@@ -867,10 +870,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-nested", action="store_true",
                     help="skip the nested config-2 and context-split measurements")
-    ap.add_argument("--workload", choices=["decode", "prefill", "config1", "config3"],
+    ap.add_argument("--workload", choices=["decode", "prefill", "prefill-kv4", "config1", "config3"],
                     default="decode",
                     help="decode: the config-5 line the driver reads (default); prefill: "
-                         "config 4 chunked prefill; config1 / config3: their own lines")
+                         "config 4 chunked prefill (kv8); prefill-kv4: the same shape in kv4; "
+                         "config1 / config3: their own lines")
     ap.add_argument("--profile", choices=["decode", "append", "config5"], default=None,
                     help="run only the named kernel on a small fixed workload, `--steps` "
                          "launches, no timing (for ncu captures)")
@@ -884,6 +888,8 @@ def main():
         return reference_arm(args, rank)
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "prefill-kv4":
+        return run_prefill(args, bits=4)
     if args.workload in CONFIG_DESC:
         return run_config(args)
 

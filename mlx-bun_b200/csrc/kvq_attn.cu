@@ -243,7 +243,25 @@ int32_t launch_prefill(const AttnArgs& a, int L, int mask_mode, int window, void
                        size_t ws_bytes, cudaStream_t st) {
   if (L <= 0) return fail(KVQ_ERR_ARG, "prefill: L must be positive");
   if (L > a.N) return fail(KVQ_ERR_ARG, "prefill: L exceeds the key length");
-  if (prefill_tc_supported(a.bits, a.D, a.gs, L, false) && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+  const bool tc1 = prefill_tc_supported(a.bits, a.D, a.gs, L, false) &&
+                   reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  const bool tc2 = !tc1 && prefill_tc2_supported(a.bits, a.D, a.gs, a.dtype, L) &&
+                   reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a.q) % 16 == 0;
+  if (tc2) {
+    // warp-specialised tensor-core prefill for the shapes the first one does
+    // not take: fp16, D 128, kv4, or kv8 with group 32 / 128
+    Params p;
+    int NT = 1;
+    int32_t rc = prepare(a, L, mask_mode, window, p, NT);
+    if (rc) return rc;
+    if (a.B == 0 || a.Hq == 0) return KVQ_OK;
+    p.out = static_cast<uint16_t*>(out);
+    p.mode = 0;
+    p.B = a.B;
+    return launch_prefill_tc2(p, a.B, a.bits, a.gs, ws, ws_bytes, st);
+  }
+  if (tc1) {
     // tensor-core (tcgen05) prefill; its workspace holds the error flag and,
     // for the balanced grid, the partials of units split between CTAs
     Params p;

@@ -1875,6 +1875,11 @@ int32_t pick_d(Params& p, const LaunchShape& s, int Dv, int GSv, int NT, int B, 
 // The tcgen05 chunked prefill (kvq_prefill_tc.cu): 8-bit codes, D 128, group 64.
 bool prefill_tc_supported(int bits, int D, int gs, int L, bool scores);
 int32_t launch_prefill_tc(Params& p, int B, void* ws, size_t ws_bytes, cudaStream_t st);
+// The warp-specialised tcgen05 prefill (kvq_prefill_tc2.cu): fp16 caches,
+// D 128, 4- or 8-bit codes, group 32 / 64 / 128.
+bool prefill_tc2_supported(int bits, int D, int gs, int dtype, int L);
+int32_t launch_prefill_tc2(Params& p, int B, int bits, int gs, void* ws, size_t ws_bytes,
+                           cudaStream_t st);
 
 // Per-width launchers (one translation unit each, compiled in parallel);
 // s.ctas > 0 selects the balanced kernel.  With occ != nullptr they only

@@ -141,6 +141,12 @@ PREFILL_CASES = [
     (1, 8, 2, 2000, 300, 128, 64, 8, F16, 64, 0),   # window 64: later rows' first tiles all masked
     (2, 8, 2, 650, 5, 128, 64, 8, F16, 0, 0),       # 20 query rows: one padded 128-row tile
     (1, 4, 1, 400, 400, 128, 64, 8, F16, 0, 0),     # offset 0, keys end mid-tile
+    # fp16 D 128 shapes of the warp-specialised tcgen05 prefill (kv4, kv8 group 32 / 128):
+    (1, 32, 8, 1536, 512, 128, 64, 4, F16, 0, 4),   # config 4 shape in kv4, key outliers
+    (2, 8, 2, 1000, 200, 128, 32, 4, F16, 0, 0),    # kv4 group 32, two batch entries
+    (1, 8, 2, 900, 130, 128, 128, 8, F16, 0, 0),    # kv8 group 128, 520 query rows: a padded block
+    (1, 16, 4, 1200, 300, 128, 64, 4, F16, 200, 0), # kv4 sliding window 200
+    (1, 4, 1, 77, 77, 128, 32, 8, F16, 0, 0),       # kv8 group 32, offset 0, one partial tile
 ]
 
 
