@@ -113,6 +113,70 @@ int32_t kvq_cache_free(kvq_cache* cache);
 int32_t kvq_append(kvq_cache* cache, const void* k, const void* v, int32_t S,
                    const int64_t* k_strides, const int64_t* v_strides, void* stream);
 
+/* ---- fused K/V projection + norms + RoPE + quantize-on-append ----------- */
+
+/* One MLX affine-quantized linear layer (QuantizedLinear, src/model/
+ * gemma4-base.ts:76-158; the weight triple of mlx quantize): packed codes
+ * [out_features, in_features * bits / 32] (16-byte aligned rows, LSB-first),
+ * scales and biases [out_features, in_features / group_size] in the
+ * activation dtype (biases NULL: none).  bits 4 or 8, group_size 32, 64 or
+ * 128. */
+typedef struct kvq_qlinear {
+  const uint32_t* packed;
+  const void* scales;
+  const void* biases;
+  int32_t bits, group_size;
+  int32_t in_features, out_features;
+} kvq_qlinear;
+
+/* The K/V side of one attention layer ahead of its cache (Attention.forward,
+ * src/model/gemma4.ts:234-268):
+ *   k = k_proj(x); v = v_from_k ? k : v_proj(x)   (attention_k_eq_v)
+ *   k = rope(k_norm(k), offset); v = v_norm(v)
+ * with out_features = kv_heads * head_dim.  k_norm / v_norm: apply RMSNorm
+ * (mlx fast::rms_norm: x * 1/sqrt(mean(x^2) + eps), rounded to the dtype,
+ * then times the weight, rounded; weight NULL: no multiply).  RoPE (mlx
+ * fast::rope): the first rope_dims elements of each K row rotate in pairs
+ * (i, i + rope_dims/2), or (2i, 2i + 1) with rope_traditional, by theta =
+ * rope_scale * position * inv_freq_i, inv_freq_i = rope_base^(-2i/rope_dims),
+ * or 1 / rope_freqs[i] when rope_freqs (device f32 [rope_dims / 2]) is given
+ * (ProportionalRoPE's freqs, :131-165, whose infinite entries leave their
+ * pair unrotated; the llama3 / yarn / longrope tables of
+ * src/model/universal/rope.ts); the rest of the row passes through;
+ * rope_dims 0: no RoPE.  Position of token l = the cache offset before the
+ * append + l. */
+typedef struct kvq_kv_projection {
+  kvq_qlinear k_proj;
+  kvq_qlinear v_proj;          /* ignored when v_from_k */
+  int32_t v_from_k;
+  int32_t k_norm, v_norm;
+  const void* k_norm_weight;   /* device [head_dim] dtype, nullable */
+  const void* v_norm_weight;
+  float norm_eps;
+  int32_t rope_dims;
+  int32_t rope_traditional;
+  float rope_base, rope_scale;
+  const float* rope_freqs;
+} kvq_kv_projection;
+
+/* kvq_append of the projected, normed and roped K/V rows of x (device [B,
+ * L, in_features] in the cache's dtype, B = the cache's batch): the K and V
+ * projections run from the quantized weights, the norms, RoPE and the
+ * quantize-on-append run in the same pass, and the rows land where
+ * kvq_append would put them (same growth / ring state machine).  Replaces
+ * kProj/vProj + kNorm/vNorm + rope + transposes + updateAndFetchQuantized
+ * (src/model/gemma4.ts:234-268).  k_out / v_out (nullable, device [B,
+ * kv_heads, L, head_dim] dtype) receive the rows before quantisation.
+ * workspace NULL: the library-managed scratch; else at least
+ * kvq_append_projected_workspace bytes. */
+int32_t kvq_append_projected(kvq_cache* cache, const void* x, int32_t L,
+                             const kvq_kv_projection* proj, void* k_out, void* v_out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes kvq_append_projected needs for L tokens. */
+int32_t kvq_append_projected_workspace(const kvq_cache* cache, int32_t L,
+                                       const kvq_kv_projection* proj, size_t* bytes);
+
 /* Active quantized views after the last append (the [0:offset] slices of
  * updateAndFetchQuantized, :499-506, or #activeSlices, :1097-1104). */
 int32_t kvq_cache_fetch(const kvq_cache* cache, kvq_qtensor* keys, kvq_qtensor* values);

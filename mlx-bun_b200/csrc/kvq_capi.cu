@@ -24,6 +24,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <mutex>
 #include <string>
@@ -385,6 +386,112 @@ int32_t adopt_state(const kvq_desc* desc, int32_t rows, int64_t offset, int64_t 
 
 }  // namespace
 
+namespace {
+
+// The reference's update state machine for S new rows per (batch, head):
+// growth, ring rotation, temporal re-layout; `write(dst_row)` fills rows
+// [dst_row, dst_row + S) of every (batch, head) once the layout is ready,
+// then the host state advances.  The caller selects the device.
+int32_t append_rows(kvq_cache* c, int32_t S, cudaStream_t st,
+                    const std::function<int32_t(int64_t)>& write) {
+  int32_t rc = KVQ_OK;
+
+  if (!c->ring()) {
+    // QuantizedKVCache.updateAndFetchQuantized (:452-507)
+    const int64_t prev = c->offset;
+    if (!c->allocated || prev + S > c->seq_len) {
+      const int64_t new_steps = (256 + (int64_t)S - 1) / 256 * 256;
+      const int64_t keep = c->allocated ? ((prev % 256 != 0) ? prev : c->seq_len) : 0;
+      if ((rc = grow_to(c, keep, keep + new_steps, st))) return rc;
+      c->seq_len = keep + new_steps;
+      c->allocated = true;
+    }
+    if ((rc = write(prev))) return rc;
+    c->offset += S;
+    return KVQ_OK;
+  }
+
+  const int64_t M = c->d.max_size;
+  if (S == 1) {
+    // #updateInPlace (:1026-1086)
+    const int64_t prev = c->offset;
+    if (!c->allocated || (prev >= c->seq_len && c->seq_len < M)) {
+      const int64_t new_size = std::min<int64_t>(256, M - prev);
+      if (new_size <= 0) return fail(KVQ_ERR_STATE, "rotating cache: offset beyond max_size with a short buffer");
+      const int64_t keep = c->allocated ? c->seq_len : 0;
+      if ((rc = grow_to(c, keep, keep + new_size, st))) return rc;
+      c->seq_len = keep + new_size;
+      c->allocated = true;
+      c->ring_idx = prev;
+    }
+    const int64_t trim = c->seq_len - M;
+    if (trim > 0) {
+      // drop the oldest `trim` rows: buffer = buffer[trim:]
+      if ((rc = relayout(c, round_up(std::max<int64_t>(M, c->d.reserve_rows), 16), {{trim, 0, M}}, st)))
+        return rc;
+      c->seq_len = M;
+      c->ring_idx = M;
+    }
+    if (c->ring_idx == M) c->ring_idx = 0;
+    if ((rc = write(c->ring_idx))) return rc;
+    c->offset += 1;
+    c->ring_idx += 1;
+    return KVQ_OK;
+  }
+
+  // #updateConcat (:1003-1024): temporal order, trim to max_size - 1, append S
+  if (!c->allocated) {
+    const int64_t cap = round_up(std::max<int64_t>({(int64_t)S, M, c->d.reserve_rows}), 16);
+    if (!c->base || cap > c->cap) {
+      if ((rc = relayout(c, cap, {}, st))) return rc;
+    } else if ((rc = zero_rows(c, 0, c->cap, st))) {
+      return rc;
+    }
+    c->allocated = true;
+    if ((rc = write(0))) return rc;
+    c->seq_len = S;
+  } else {
+    std::vector<Seg> order;  // temporal order of the current buffer
+    if (c->ring_idx == c->seq_len) {
+      order.push_back({0, 0, c->seq_len});
+    } else if (c->ring_idx < c->offset) {
+      order.push_back({c->ring_idx, 0, c->seq_len - c->ring_idx});
+      order.push_back({0, c->seq_len - c->ring_idx, c->ring_idx});
+    } else {
+      order.push_back({0, 0, c->ring_idx});
+    }
+    int64_t T = 0;
+    for (const Seg& s : order) T += s.rows;
+    const int64_t skip = std::max<int64_t>(0, T - M + 1);
+    // drop the first `skip` temporal rows
+    std::vector<Seg> segs;
+    int64_t dropped = 0, dst = 0;
+    for (const Seg& s : order) {
+      int64_t src = s.src_row, rows = s.rows;
+      const int64_t cut = std::min(rows, skip - dropped);
+      if (cut > 0) {
+        src += cut;
+        rows -= cut;
+        dropped += cut;
+      }
+      if (rows > 0) {
+        segs.push_back({src, dst, rows});
+        dst += rows;
+      }
+    }
+    const int64_t new_len = dst + S;
+    const int64_t cap = round_up(std::max<int64_t>({new_len, M, c->d.reserve_rows}), 16);
+    if ((rc = relayout(c, cap, segs, st))) return rc;
+    if ((rc = write(dst))) return rc;
+    c->seq_len = new_len;
+  }
+  c->offset += S;
+  c->ring_idx = c->seq_len;
+  return KVQ_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* kvq_last_error(void) { return g_last_error.c_str(); }
@@ -437,99 +544,109 @@ int32_t kvq_append(kvq_cache* c, const void* k, const void* v, int32_t S, const 
   DeviceGuard guard(c->d.device);
   if (!guard.ok) return fail(KVQ_ERR_CUDA, "cannot select the cache's device");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int32_t rc = KVQ_OK;
+  return append_rows(c, S, st, [&](int64_t dst) {
+    return quantize_into(c, k, v, S, k_strides, v_strides, dst, st);
+  });
+}
 
-  if (!c->ring()) {
-    // QuantizedKVCache.updateAndFetchQuantized (:452-507)
-    const int64_t prev = c->offset;
-    if (!c->allocated || prev + S > c->seq_len) {
-      const int64_t new_steps = (256 + (int64_t)S - 1) / 256 * 256;
-      const int64_t keep = c->allocated ? ((prev % 256 != 0) ? prev : c->seq_len) : 0;
-      if ((rc = grow_to(c, keep, keep + new_steps, st))) return rc;
-      c->seq_len = keep + new_steps;
-      c->allocated = true;
-    }
-    if ((rc = quantize_into(c, k, v, S, k_strides, v_strides, prev, st))) return rc;
-    c->offset += S;
-    return KVQ_OK;
-  }
+}  // extern "C"
 
-  const int64_t M = c->d.max_size;
-  if (S == 1) {
-    // #updateInPlace (:1026-1086)
-    const int64_t prev = c->offset;
-    if (!c->allocated || (prev >= c->seq_len && c->seq_len < M)) {
-      const int64_t new_size = std::min<int64_t>(256, M - prev);
-      if (new_size <= 0) return fail(KVQ_ERR_STATE, "rotating cache: offset beyond max_size with a short buffer");
-      const int64_t keep = c->allocated ? c->seq_len : 0;
-      if ((rc = grow_to(c, keep, keep + new_size, st))) return rc;
-      c->seq_len = keep + new_size;
-      c->allocated = true;
-      c->ring_idx = prev;
-    }
-    const int64_t trim = c->seq_len - M;
-    if (trim > 0) {
-      // drop the oldest `trim` rows: buffer = buffer[trim:]
-      if ((rc = relayout(c, round_up(std::max<int64_t>(M, c->d.reserve_rows), 16), {{trim, 0, M}}, st)))
-        return rc;
-      c->seq_len = M;
-      c->ring_idx = M;
-    }
-    if (c->ring_idx == M) c->ring_idx = 0;
-    if ((rc = quantize_into(c, k, v, 1, k_strides, v_strides, c->ring_idx, st))) return rc;
-    c->offset += 1;
-    c->ring_idx += 1;
-    return KVQ_OK;
-  }
+namespace {
 
-  // #updateConcat (:1003-1024): temporal order, trim to max_size - 1, append S
-  if (!c->allocated) {
-    const int64_t cap = round_up(std::max<int64_t>({(int64_t)S, M, c->d.reserve_rows}), 16);
-    if (!c->base || cap > c->cap) {
-      if ((rc = relayout(c, cap, {}, st))) return rc;
-    } else if ((rc = zero_rows(c, 0, c->cap, st))) {
-      return rc;
-    }
-    c->allocated = true;
-    if ((rc = quantize_into(c, k, v, S, k_strides, v_strides, 0, st))) return rc;
-    c->seq_len = S;
-  } else {
-    std::vector<Seg> order;  // temporal order of the current buffer
-    if (c->ring_idx == c->seq_len) {
-      order.push_back({0, 0, c->seq_len});
-    } else if (c->ring_idx < c->offset) {
-      order.push_back({c->ring_idx, 0, c->seq_len - c->ring_idx});
-      order.push_back({0, c->seq_len - c->ring_idx, c->ring_idx});
-    } else {
-      order.push_back({0, 0, c->ring_idx});
-    }
-    int64_t T = 0;
-    for (const Seg& s : order) T += s.rows;
-    const int64_t skip = std::max<int64_t>(0, T - M + 1);
-    // drop the first `skip` temporal rows
-    std::vector<Seg> segs;
-    int64_t dropped = 0, dst = 0;
-    for (const Seg& s : order) {
-      int64_t src = s.src_row, rows = s.rows;
-      const int64_t cut = std::min(rows, skip - dropped);
-      if (cut > 0) {
-        src += cut;
-        rows -= cut;
-        dropped += cut;
-      }
-      if (rows > 0) {
-        segs.push_back({src, dst, rows});
-        dst += rows;
-      }
-    }
-    const int64_t new_len = dst + S;
-    const int64_t cap = round_up(std::max<int64_t>({new_len, M, c->d.reserve_rows}), 16);
-    if ((rc = relayout(c, cap, segs, st))) return rc;
-    if ((rc = quantize_into(c, k, v, S, k_strides, v_strides, dst, st))) return rc;
-    c->seq_len = new_len;
+int32_t check_qlinear(const kvq_qlinear& w, const char* name, const kvq_desc& d) {
+  const std::string n(name);
+  if (!w.packed || !w.scales) return fail(KVQ_ERR_ARG, n + ": NULL packed / scales");
+  if (w.bits != 4 && w.bits != 8) return fail(KVQ_ERR_ARG, n + ": bits must be 4 or 8");
+  if (w.group_size != 32 && w.group_size != 64 && w.group_size != 128)
+    return fail(KVQ_ERR_ARG, n + ": group_size must be 32, 64 or 128");
+  if (w.in_features <= 0 || w.in_features % w.group_size)
+    return fail(KVQ_ERR_ARG, n + ": in_features must be a positive multiple of group_size");
+  if ((int64_t)w.out_features != (int64_t)d.kv_heads * d.head_dim)
+    return fail(KVQ_ERR_ARG, n + ": out_features must be kv_heads * head_dim");
+  if (reinterpret_cast<uintptr_t>(w.packed) % 16)
+    return fail(KVQ_ERR_ARG, n + ": packed must be 16-byte aligned");
+  return KVQ_OK;
+}
+
+int32_t make_proj_args(const kvq_cache* c, const void* x, int32_t L, const kvq_kv_projection* pr,
+                       kvq::ProjArgs& a) {
+  if (!c) return fail(KVQ_ERR_ARG, "cache is NULL");
+  if (!pr) return fail(KVQ_ERR_ARG, "projection is NULL");
+  if (L <= 0) return fail(KVQ_ERR_ARG, "L must be positive");
+  const kvq_desc& d = c->d;
+  if (d.head_dim > 256) return fail(KVQ_ERR_ARG, "the fused projection supports head_dim <= 256");
+  int32_t rc = check_qlinear(pr->k_proj, "k_proj", d);
+  if (rc) return rc;
+  if (!pr->v_from_k) {
+    if ((rc = check_qlinear(pr->v_proj, "v_proj", d))) return rc;
+    if (pr->v_proj.in_features != pr->k_proj.in_features)
+      return fail(KVQ_ERR_ARG, "k_proj and v_proj must share in_features");
+    if (pr->v_proj.bits != pr->k_proj.bits)
+      return fail(KVQ_ERR_ARG, "k_proj and v_proj must share a bit width");
   }
-  c->offset += S;
-  c->ring_idx = c->seq_len;
+  if (pr->rope_dims < 0 || pr->rope_dims > d.head_dim || pr->rope_dims % 2)
+    return fail(KVQ_ERR_ARG, "rope_dims must be even and within head_dim");
+  if (pr->rope_dims > 0 && !pr->rope_freqs && !(pr->rope_base > 0.0f))
+    return fail(KVQ_ERR_ARG, "rope_base must be positive (or rope_freqs given)");
+  a = kvq::ProjArgs{};
+  a.x = x;
+  a.B = d.batch;
+  a.L = L;
+  a.hidden = pr->k_proj.in_features;
+  a.wk = {pr->k_proj.packed, pr->k_proj.scales, pr->k_proj.biases, pr->k_proj.bits, pr->k_proj.group_size};
+  a.v_from_k = pr->v_from_k != 0;
+  if (!a.v_from_k)
+    a.wv = {pr->v_proj.packed, pr->v_proj.scales, pr->v_proj.biases, pr->v_proj.bits, pr->v_proj.group_size};
+  a.k_norm = pr->k_norm_weight;
+  a.v_norm = pr->v_norm_weight;
+  a.norms = (pr->k_norm ? 1 : 0) | (pr->v_norm ? 2 : 0);
+  a.eps = pr->norm_eps;
+  a.rope_dims = pr->rope_dims;
+  a.rope_traditional = pr->rope_traditional != 0;
+  a.rope_base = pr->rope_base;
+  a.rope_scale = pr->rope_scale;
+  a.rope_freqs = pr->rope_freqs;
+  a.pos0 = c->offset;
+  return KVQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t kvq_append_projected(kvq_cache* c, const void* x, int32_t L, const kvq_kv_projection* proj,
+                             void* k_out, void* v_out, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  kvq::ProjArgs a;
+  int32_t rc = make_proj_args(c, x, L, proj, a);
+  if (rc) return rc;
+  if (!x) return fail(KVQ_ERR_ARG, "x is NULL");
+  a.k_out = k_out;
+  a.v_out = v_out;
+  DeviceGuard guard(c->d.device);
+  if (!guard.ok) return fail(KVQ_ERR_CUDA, "cannot select the cache's device");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (workspace) {
+    const size_t need = kvq::project_workspace_bytes(a, c->d.kv_heads, c->d.head_dim, nullptr);
+    if (workspace_bytes < need)
+      return fail(KVQ_ERR_WORKSPACE, "workspace too small: " + std::to_string(need) + " bytes needed");
+  }
+  RowGeom g{c->d.head_dim, c->d.bits, c->d.group_size};
+  return append_rows(c, L, st, [&](int64_t dst) {
+    return kvq::launch_project_append(a, c->d.kv_heads, g, c->d.dtype, c->k, c->v, dst, workspace,
+                                      workspace_bytes, st);
+  });
+}
+
+int32_t kvq_append_projected_workspace(const kvq_cache* c, int32_t L, const kvq_kv_projection* proj,
+                                       size_t* bytes) {
+  if (!bytes) return fail(KVQ_ERR_ARG, "bytes is NULL");
+  kvq::ProjArgs a;
+  int32_t rc = make_proj_args(c, nullptr, L, proj, a);
+  if (rc) return rc;
+  DeviceGuard guard(c->d.device);
+  if (!guard.ok) return fail(KVQ_ERR_CUDA, "cannot select the cache's device");
+  *bytes = kvq::project_workspace_bytes(a, c->d.kv_heads, c->d.head_dim, nullptr);
   return KVQ_OK;
 }
 

@@ -56,6 +56,36 @@ int32_t launch_append_ragged(const void* k, const int64_t* k_strides, const void
 int32_t launch_quantize_rows(const void* x, int64_t rows, RowGeom g, int dtype, uint32_t* packed,
                              uint16_t* scales, uint16_t* biases, cudaStream_t st);
 
+// ---- fused projection + norms + RoPE + quantize-on-append (kvq_project.cu) ----
+struct ProjWeights {
+  const uint32_t* packed;  // [out, in * bits / 32]
+  const void* scales;      // [out, in / gs], the activation dtype
+  const void* biases;      // same shape, nullable
+  int bits, gs;
+};
+struct ProjArgs {
+  const void* x;  // [B, L, hidden] contiguous
+  int B, L, hidden;
+  ProjWeights wk, wv;
+  bool v_from_k;  // V is K's projection (before the norms)
+  const void* k_norm;  // [D] nullable
+  const void* v_norm;  // [D] nullable
+  int norms;           // bit 0: RMSNorm on K, bit 1: on V
+  float eps;
+  int rope_dims;       // 0: no RoPE
+  bool rope_traditional;  // pairs (2i, 2i+1) instead of (i, i + dims/2)
+  float rope_base, rope_scale;
+  const float* rope_freqs;  // [rope_dims / 2] device, nullable
+  int64_t pos0;        // position of row l = pos0 + l
+  void* k_out;         // [B, Hkv, L, D] rows before quantisation, nullable
+  void* v_out;
+};
+// Workspace bytes of one launch (and the split count it uses).
+size_t project_workspace_bytes(const ProjArgs& a, int Hkv, int D, int* splits);
+int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, TripleView dk,
+                              TripleView dv, int64_t dst_row0, void* ws, size_t ws_bytes,
+                              cudaStream_t st);
+
 // ---- attention (kvq_decode.cu / kvq_prefill.cu) ----
 struct AttnArgs {
   TripleView k, v;

@@ -26,11 +26,10 @@
 #include <cuda_fp16.h>
 
 #include "kvq_internal.h"
+#include "kvq_qrule.cuh"
 
 namespace kvq {
 namespace {
-
-constexpr float kEps = 1e-7f;  // constant-group guard shared with the oracle
 
 struct Job {
   const uint16_t* x;
@@ -126,27 +125,11 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const Jobs jobs) {
     mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
   }
-  float s0 = (mx - mn) / NB;
-  if (!(s0 >= kEps)) s0 = kEps;
-  const bool neg = fabsf(mn) > fabsf(mx);
-  const float anchor = neg ? mn : mx;
-  s0 = neg ? s0 : -s0;
-  const float q0 = roundf(anchor / s0);
   float scale, bias;
-  if (q0 != 0.0f) {
-    scale = anchor / q0;
-    bias = anchor;
-  } else {
-    scale = s0;
-    bias = 0.0f;
-  }
+  quant_params(mn, mx, NB, scale, bias);
   uint32_t out = 0;
 #pragma unroll
-  for (int i = 0; i < PER; i++) {
-    float c = roundf((w[i] - bias) / scale);
-    c = fminf(fmaxf(c, 0.0f), NB);
-    out |= (uint32_t)c << (BITS * i);
-  }
+  for (int i = 0; i < PER; i++) out |= quant_code(w[i], scale, bias, NB) << (BITS * i);
   int64_t row0 = J.dst_row0;
   if (RAG) {
     const int64_t l0 = jobs.lens[b];

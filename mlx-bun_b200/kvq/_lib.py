@@ -29,7 +29,8 @@ EXPORTS = (
     "kvq_sdpa_decode_noalloc", "kvq_debug_raise_flag", "kvq_peer_group_create",
     "kvq_peer_group_connect", "kvq_peer_exchange_merge", "kvq_peer_group_check",
     "kvq_peer_group_free", "kvq_append_ragged", "kvq_cache_fetch_all", "kvq_cache_check",
-    "kvq_cache_from_dense", "kvq_cache_export", "kvq_cache_import",
+    "kvq_cache_from_dense", "kvq_cache_export", "kvq_cache_import", "kvq_append_projected",
+    "kvq_append_projected_workspace",
 )
 
 
@@ -51,6 +52,23 @@ class QTensor(ctypes.Structure):
                 ("head_stride", ctypes.c_int64)] + \
         [(n, ctypes.c_int32) for n in ("batch", "heads", "len", "head_dim", "bits",
                                        "group_size", "dtype")]
+
+
+class QLinear(ctypes.Structure):
+    """kvq_qlinear: one MLX affine-quantized linear layer's weight triple."""
+    _fields_ = [("packed", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+                ("biases", ctypes.c_void_p)] + \
+        [(n, ctypes.c_int32) for n in ("bits", "group_size", "in_features", "out_features")]
+
+
+class KvProjection(ctypes.Structure):
+    """kvq_kv_projection: the K/V side of one attention layer."""
+    _fields_ = [("k_proj", QLinear), ("v_proj", QLinear), ("v_from_k", ctypes.c_int32),
+                ("k_norm", ctypes.c_int32), ("v_norm", ctypes.c_int32),
+                ("k_norm_weight", ctypes.c_void_p), ("v_norm_weight", ctypes.c_void_p),
+                ("norm_eps", ctypes.c_float), ("rope_dims", ctypes.c_int32),
+                ("rope_traditional", ctypes.c_int32), ("rope_base", ctypes.c_float), ("rope_scale", ctypes.c_float),
+                ("rope_freqs", ctypes.c_void_p)]
 
 
 _lib = None
@@ -102,6 +120,10 @@ def lib():
                                        P(vp)]),
         "kvq_cache_export": (i32, [vp, i64, P(vp), vp]),
         "kvq_cache_import": (i32, [P(Desc), P(vp), i32, i64, i64, vp, P(vp)]),
+        "kvq_append_projected": (i32, [vp, vp, i32, P(KvProjection), vp, vp, vp,
+                                       ctypes.c_size_t, vp]),
+        "kvq_append_projected_workspace": (i32, [vp, i32, P(KvProjection),
+                                                 P(ctypes.c_size_t)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

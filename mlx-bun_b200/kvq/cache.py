@@ -159,13 +159,23 @@ class _CacheBase:
 
     def _ensure(self, k: torch.Tensor):
         B, H, _, D = k.shape
+        self._ensure_shape(B, H, D, k.dtype, k.device.index)
+
+    def _ensure_shape(self, B, H, D, dtype, device):
         if self._h.value is None:
-            d = _lib.Desc(B, H, D, self.bits, self.group_size, dtype_code(k.dtype),
-                          self.max_size, self.reserve_rows, k.device.index)
+            d = _lib.Desc(B, H, D, self.bits, self.group_size, dtype_code(dtype),
+                          self.max_size, self.reserve_rows, device)
             check(lib().kvq_cache_create(ctypes.byref(d), ctypes.byref(self._h)))
-            self._shape = (B, H, D, k.dtype, k.device.index)
-        elif (B, H, D, k.dtype, k.device.index) != self._shape:
+            self._shape = (B, H, D, dtype, device)
+        elif (B, H, D, dtype, device) != self._shape:
             raise ValueError("k/v shape, dtype or device differ from the cache's")
+
+    def update_and_fetch_projected(self, x: torch.Tensor, proj, k_out=None, v_out=None,
+                                   stream=None):
+        """Fused K/V projection + norms + RoPE + append of x [B, L, hidden]
+        (kvq_append_projected; see kvq.project)."""
+        from .project import append_projected
+        return append_projected(self, x, proj, k_out, v_out, stream)
 
     def update_and_fetch_quantized(self, k: torch.Tensor, v: torch.Tensor, stream=None):
         """Quantize k, v ([B, H, S, D], any strides with unit d stride) into the

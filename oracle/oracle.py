@@ -462,3 +462,97 @@ def make_mask_rotating(N: int, offset: int, max_size: int, window):
             return 1, w
         return 1, 0
     return 0, 0
+
+
+# ------------------------------------------ K/V projection, norms, RoPE ---
+# The K/V side of Attention.forward (src/model/gemma4.ts:234-268) ahead of
+# the cache append: QuantizedLinear.forward (src/model/gemma4-base.ts:119-
+# 124, mlx quantized_matmul with transpose: x @ dequantize(w).T accumulated
+# in f32, the result in the activation dtype), RMSNorm (gemma4-base.ts:
+# 160-165, mlx fast::rms_norm) and RoPE (src/mlx/ops.ts:100-134, mlx
+# fast::rope), MLX 0.31.2.  Every dtype rounding point of those ops is kept;
+# sums run in f64 here (the product accumulates in f32, in another order).
+
+def round_dt(x: np.ndarray, dtype: int) -> np.ndarray:
+    """f32 values rounded (RNE) to the dtype and back."""
+    return from_dtype_bits(to_dtype_bits(x, dtype), dtype)
+
+
+def quantized_linear(x: np.ndarray, packed, scales, biases, group_size: int, bits: int,
+                     dtype: int) -> np.ndarray:
+    """x [..., in] (dtype values as f32) @ dequantize(w).T -> [..., out] in the dtype."""
+    if biases is None:
+        biases = np.zeros_like(scales)
+    w = dequantize(packed, scales, biases, group_size, bits, dtype).astype(np.float64)
+    y = np.asarray(x, np.float64) @ w.T
+    return round_dt(y.astype(np.float32), dtype)
+
+
+def rms_norm(x: np.ndarray, weight, eps: float, dtype: int) -> np.ndarray:
+    """mlx fast::rms_norm over the last axis: x / sqrt(mean(x^2) + eps)
+    rounded to the dtype, then times the weight (dtype values), rounded."""
+    x = np.asarray(x, np.float32)
+    ms = np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True).astype(np.float32)
+    n = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+    y = round_dt(x * n, dtype)
+    if weight is not None:
+        y = round_dt(y * np.asarray(weight, np.float32), dtype)
+    return y
+
+
+def rope(x: np.ndarray, dims: int, traditional: bool, base, scale: float, offset: int,
+         freqs, dtype: int) -> np.ndarray:
+    """mlx fast::rope of x [..., L, D] at positions offset + l: the first
+    `dims` elements rotate in pairs (i, i + dims/2) (or (2i, 2i+1) when
+    traditional) by theta = (scale * position) * inv_freq_i, inv_freq_i =
+    2^(-(i / (dims/2)) * log2(base)) or 1 / freqs[i]; f32, rounded to the
+    dtype.  Elements past `dims` pass through."""
+    x = np.asarray(x, np.float32)
+    L = x.shape[-2]
+    half = dims // 2
+    i = np.arange(half, dtype=np.float32)
+    if freqs is None:
+        inv = np.exp2(-(i / np.float32(half)) * np.float32(np.log2(base))).astype(np.float32)
+    else:
+        inv = (np.float32(1.0) / np.asarray(freqs, np.float32)).astype(np.float32)
+    pos = (np.float32(scale) * (offset + np.arange(L)).astype(np.float32)).astype(np.float32)
+    theta = (pos[:, None] * inv[None, :]).astype(np.float32)
+    c, s = np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+    out = x.copy()
+    if traditional:
+        x1, x2 = x[..., 0:dims:2], x[..., 1:dims:2]
+    else:
+        x1, x2 = x[..., :half], x[..., half:dims]
+    r1 = round_dt((x1 * c - x2 * s).astype(np.float32), dtype)
+    r2 = round_dt((x1 * s + x2 * c).astype(np.float32), dtype)
+    if traditional:
+        out[..., 0:dims:2], out[..., 1:dims:2] = r1, r2
+    else:
+        out[..., :half], out[..., half:dims] = r1, r2
+    return out
+
+
+def project_kv(x: np.ndarray, proj: dict, offset: int, dtype: int):
+    """K and V rows [B, H, L, D] (dtype values as f32) of x [B, L, hidden]:
+    k = rope(k_norm(k_proj(x))), v = v_norm(v_proj(x) or k_proj(x)).
+
+    proj: k_proj / v_proj = (packed, scales, biases, group_size, bits) (v_proj
+    None: attention_k_eq_v), head_dim, k_norm / v_norm (bool), k_norm_weight /
+    v_norm_weight (f32 or None), eps, rope_dims, rope_traditional, rope_base,
+    rope_scale, rope_freqs (f32 or None)."""
+    B, L, _ = x.shape
+    D = proj["head_dim"]
+    k = quantized_linear(x, *proj["k_proj"], dtype)
+    v = k if proj.get("v_proj") is None else quantized_linear(x, *proj["v_proj"], dtype)
+    H = k.shape[-1] // D
+    k = k.reshape(B, L, H, D).transpose(0, 2, 1, 3)
+    v = v.reshape(B, L, H, D).transpose(0, 2, 1, 3)
+    if proj.get("k_norm"):
+        k = rms_norm(k, proj.get("k_norm_weight"), proj["eps"], dtype)
+    if proj.get("v_norm"):
+        v = rms_norm(v, proj.get("v_norm_weight"), proj["eps"], dtype)
+    if proj.get("rope_dims", 0):
+        k = rope(k, proj["rope_dims"], proj.get("rope_traditional", False),
+                 proj.get("rope_base"), proj.get("rope_scale", 1.0), offset,
+                 proj.get("rope_freqs"), dtype)
+    return np.ascontiguousarray(k), np.ascontiguousarray(v)
