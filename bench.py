@@ -31,13 +31,19 @@ context_split
            N ranks, partials exchanged over peer memory and merged (a CUDA
            graph per pass over the layers), us per step and the exchange's
            share of it.
+kv_projection
+           nested: the fused K/V projection + RMSNorms + RoPE + quantize-on-
+           append of one decode token through 48 Gemma-4-12B sliding-layer
+           K/V weight sets (hidden 3840 -> 8 x 256, 4-bit), one replica per
+           GPU, with its HBM roofline; and a 512-token prefill chunk.
 cpu_baseline / --impl reference
            the CPU oracle (C restatement of mlx-bun's unfused op graph) with
            every host core, on a bounded sample of config 5's (sequence, kv
            head) pairs.
 
 Other workloads print their own line: `--workload prefill` (config 4,
-tensor-core chunked prefill), `config1` and `config3`.
+tensor-core chunked prefill), `prefill-kv4`, `config1`, `config3` and
+`kv-projection`.
 """
 import argparse
 import json
@@ -681,6 +687,154 @@ def run_prefill(args, bits=8):
         "gpu_launches": 3 * reps * NL, "clocks": t1.clk}))
 
 
+# ------------------------------------------- fused K/V projection --
+
+# Gemma-4-12B sliding-attention layer K/V side: hidden 3840 -> 8 kv heads x
+# 256, 4-bit group-64 weights with biases, bf16 activations, K RMSNorm with
+# weight, V RMSNorm without, default RoPE (base 10000) on all 256 dims, a
+# kv4 group-64 cache; 48 layers, as the model has.
+CFGP = dict(hidden=3840, Hkv=8, D=256, wbits=4, wgs=64, bits=4, gs=64, layers=48, chunk=512)
+
+
+def projection_bytes(c, rows):
+    """Algorithmic HBM bytes of one fused call over `rows` token rows: K and
+    V weight triples (packed codes + bf16 scales and biases), the bf16 input
+    rows, and the quantized K/V rows written to the cache."""
+    out, inn = c["Hkv"] * c["D"], c["hidden"]
+    w = 2 * (out * inn * c["wbits"] // 8 + 2 * out * (inn // c["wgs"]) * 2)
+    x = rows * inn * 2
+    row = c["D"] * c["bits"] // 8 + 2 * (c["D"] // c["gs"]) * 2
+    return w + x + 2 * rows * c["Hkv"] * row
+
+
+def projection_layers(c, n, device, g):
+    """`n` layers of random 4-bit K/V projection weights (codes uniform,
+    scales U[0.001, 0.005], biases -7.5 x scale: outputs of order one) with
+    their growing kv caches."""
+    import torch
+    import kvq
+    H, D, hid = c["Hkv"], c["D"], c["hidden"]
+    out_f = H * D
+
+    def qlinear():
+        words = hid * c["wbits"] // 32
+        packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (out_f, words), generator=g,
+                               device=device, dtype=torch.int32)
+        sc = (torch.rand(out_f, hid // c["wgs"], generator=g, device=device) * 0.004 + 0.001)
+        bi = -7.5 * sc
+        return kvq.QuantizedLinear(packed, sc.bfloat16(), bi.bfloat16(), c["wgs"], c["wbits"])
+
+    layers = []
+    for _ in range(n):
+        proj = kvq.KvProjection(qlinear(), qlinear(), D,
+                                k_norm_weight=(torch.rand(D, generator=g, device=device) + 0.5)
+                                .bfloat16(), rope_dims=D, rope_base=10000.0)
+        cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=2048)
+        layers.append(dict(proj=proj, cache=cache))
+    return layers
+
+
+def run_kv_projection(args, rank, world, local_rank):
+    """Fused K/V projection + norms + RoPE + quantize-on-append
+    (kvq_append_projected), one replica per GPU.  Decode: one token per
+    step through each of the 48 layers (a CUDA graph per pass over the
+    layers; 425 MB of weights cycled, above L2), timed with CUDA events.
+    Prefill: one 512-token chunk through one layer, timed the same way."""
+    import torch
+    c = CFGP
+    device = torch.device("cuda", local_rank)
+    hid = c["hidden"]
+    out_f = c["Hkv"] * c["D"]
+    g = torch.Generator(device=device)
+    g.manual_seed(2000 + rank)
+    layers = projection_layers(c, c["layers"], device, g)
+    x1 = torch.randn(1, 1, hid, generator=g, device=device).bfloat16()
+    xc = torch.randn(1, c["chunk"], hid, generator=g, device=device).bfloat16()
+    # every cache starts at offset 1000 (positions in range of a real decode)
+    for Ly in layers:
+        Ly["cache"].update_and_fetch_projected(torch.zeros(1, 1000, hid, device=device,
+                                                           dtype=torch.bfloat16), Ly["proj"])
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device)
+
+    def step(Ly, x):
+        Ly["cache"].update_and_fetch_projected(x, Ly["proj"])
+        Ly["cache"].trim(x.shape[1])  # host bookkeeping: every replay writes the same rows
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            for Ly in layers:
+                step(Ly, x1)
+            step(layers[0], xc)
+        torch.cuda.synchronize()
+        g_dec = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_dec, stream=stream):
+            for Ly in layers:
+                step(Ly, x1)
+        g_pre = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_pre, stream=stream):
+            step(layers[0], xc)
+        for _ in range(3):
+            g_dec.replay()
+            g_pre.replay()
+        torch.cuda.synchronize()
+    NL = c["layers"]
+    reps = max(1, math.ceil(args.steps / NL))
+    with torch.cuda.stream(stream):
+        with Timed(stream, world, device) as t1:
+            for _ in range(reps):
+                g_dec.replay()
+        preps = max(3, min(50, args.steps // 8))
+        with Timed(stream, world, device) as t2:
+            for _ in range(preps):
+                g_pre.replay()
+    dec_s = t1.ms / 1e3 / (reps * NL)
+    pre_s = t2.ms / 1e3 / preps
+    nb = projection_bytes(c, 1)
+    achieved = nb / dec_s / 1e9
+    peak, peak_kind = peaks()
+    flops = 2 * c["chunk"] * hid * 2 * out_f
+    ratio = traffic_ratio("kv_projection_decode.md")
+    res = {
+        "workload": "gemma4-12b-sliding-kv-projection: hidden 3840 -> Hkv8 x D256, 4-bit gs64 "
+                    "weights, K RMSNorm+RoPE, V RMSNorm, kv4 gs64 cache; one replica per GPU "
+                    "(weak)",
+        "decode": {"us_per_layer": round(dec_s * 1e6, 3), "layers_cycled": NL,
+                   "steps": reps * NL, "bytes_per_layer": nb,
+                   "value": round(world * nb / dec_s / 1e9, 1), "unit": UNIT,
+                   "timing": "a CUDA graph per pass over the 48 layers, CUDA events"},
+        "prefill_chunk": {"tokens": c["chunk"], "us_per_layer": round(pre_s * 1e6, 2),
+                          "tflops": round(flops / pre_s / 1e12, 2),
+                          "note": "CUDA-core FMA projection (no tensor cores on this path)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "kernel": "proj_partial_kernel<4,bf16,1> + proj_epilogue_kernel<4,bf16>",
+                     "kernel_us": round(dec_s * 1e6, 3), "bytes_per_launch": nb,
+                     "traffic": int(ratio * nb) if ratio else None},
+        "gpu_launches": 2 * reps * NL,
+    }
+    del g_dec, g_pre
+    for Ly in layers:
+        Ly["cache"].dispose()
+    return res
+
+
+def print_kv_projection(args):
+    import torch
+    torch.cuda.set_device(0)
+    r = run_kv_projection(args, 0, 1, 0)
+    print(json.dumps({
+        "metric": "fused K/V projection + norms + RoPE + quantize-on-append achieved HBM GB/s "
+                  "(decode, Gemma-4-12B sliding-layer shapes)",
+        "value": r["decode"]["value"], "unit": UNIT, "n_gpus": 1, "steps": r["decode"]["steps"],
+        "warmup": args.warmup, "ms_per_step": round(r["decode"]["us_per_layer"] / 1e3, 6),
+        "higher_is_better": True, "dtype": "u4 weights/bf16", "data": "synthetic (seeded torch)",
+        "config": {"workload": r["workload"], "l2": "48 distinct layers (425 MB of weights) "
+                   "per replay"},
+        "roofline": r["roofline"], "prefill_chunk": r["prefill_chunk"],
+        "gpu_launches": r["gpu_launches"]}))
+
+
 CONFIG_DESC = {
     "config1": "single decode step: B1 Hq16 Hkv4 D128 N2048 kv8 gs64, 64 distinct layers cycled",
     "config3": "Gemma-style window: B4 Hq8 Hkv4 D256 kv8 gs64; per step 5 rotating layers (window "
@@ -780,7 +934,9 @@ def run_config(args):
 def profile_run(args):
     """Fixed small workloads for ncu (no timing): `--steps` launches of one
     kernel.  decode / append: 3 config-2 layers (227 MB, above L2), cycled;
-    config5: the first 16 sequences of config 5, all 8 kv heads (315 MB)."""
+    config5: the first 16 sequences of config 5, all 8 kv heads (315 MB);
+    projection: one-token fused K/V projection appends through 24 layers of
+    Gemma-4-12B sliding-layer weights (213 MB), cycled."""
     import numpy as np
     import torch
     import kvq
@@ -788,6 +944,18 @@ def profile_run(args):
     torch.cuda.set_device(device)
     g = torch.Generator(device=device)
     g.manual_seed(7)
+    if args.profile == "projection":
+        c = CFGP
+        layers = projection_layers(c, 24, device, g)  # 213 MB of weights, above L2
+        x1 = torch.randn(1, 1, c["hidden"], generator=g, device=device).bfloat16()
+        for i in range(args.steps):
+            Ly = layers[i % 24]
+            Ly["cache"].update_and_fetch_projected(x1, Ly["proj"])
+            Ly["cache"].trim(1)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": "projection", "launches": args.steps,
+                          "algorithmic_bytes_per_launch": projection_bytes(c, 1)}))
+        return
     if args.profile == "config5":
         c = CFG5
         lens = config5_lens()[:16]
@@ -870,12 +1038,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-nested", action="store_true",
                     help="skip the nested config-2 and context-split measurements")
-    ap.add_argument("--workload", choices=["decode", "prefill", "prefill-kv4", "config1", "config3"],
+    ap.add_argument("--workload", choices=["decode", "prefill", "prefill-kv4", "config1", "config3",
+                                           "kv-projection"],
                     default="decode",
                     help="decode: the config-5 line the driver reads (default); prefill: "
                          "config 4 chunked prefill (kv8); prefill-kv4: the same shape in kv4; "
-                         "config1 / config3: their own lines")
-    ap.add_argument("--profile", choices=["decode", "append", "config5"], default=None,
+                         "config1 / config3: their own lines; kv-projection: the fused K/V "
+                         "projection + append alone")
+    ap.add_argument("--profile", choices=["decode", "append", "config5", "projection"],
+                    default=None,
                     help="run only the named kernel on a small fixed workload, `--steps` "
                          "launches, no timing (for ncu captures)")
     args = ap.parse_args()
@@ -892,6 +1063,8 @@ def main():
         return run_prefill(args, bits=4)
     if args.workload in CONFIG_DESC:
         return run_config(args)
+    if args.workload == "kv-projection":
+        return print_kv_projection(args)
 
     import torch
     import torch.distributed as dist
@@ -905,9 +1078,11 @@ def main():
         if not args.no_nested:
             c2 = run_config2(args, rank, world, local_rank)
             ctx = run_context_split(args, rank, world, local_rank)
+            kp = run_kv_projection(args, rank, world, local_rank)
             if res is not None:
                 res["config2"] = c2
                 res["context_split"] = ctx
+                res["kv_projection"] = kp
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
                 threads = host_cores()

@@ -168,7 +168,11 @@ typedef struct kvq_kv_projection {
  * (src/model/gemma4.ts:234-268).  k_out / v_out (nullable, device [B,
  * kv_heads, L, head_dim] dtype) receive the rows before quantisation.
  * workspace NULL: the library-managed scratch; else at least
- * kvq_append_projected_workspace bytes. */
+ * kvq_append_projected_workspace bytes.  The layer's parameters (the
+ * weight triples, norm weights, rope_freqs) are read-only here and may be
+ * read before the call's kernels wait for the kernel launched just before
+ * them on the stream (programmatic dependent launch): that kernel must not
+ * write them.  x, the cache and k_out / v_out are ordered normally. */
 int32_t kvq_append_projected(kvq_cache* cache, const void* x, int32_t L,
                              const kvq_kv_projection* proj, void* k_out, void* v_out,
                              void* workspace, size_t workspace_bytes, void* stream);

@@ -35,7 +35,10 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "kvq_attn_impl.cuh"
 #include "kvq_qrule.cuh"
@@ -145,22 +148,44 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
+// What finish_row needs besides the projected value, fetched / computed
+// ahead of it (none of it depends on the projection): thread o's norm
+// weight and, for K rows, the cosine and sine of its RoPE pair at the row's
+// position.
+struct RowConsts {
+  float wn;      // norm weight (1 without one)
+  float cs, sn;  // RoPE rotation (K, o < rope_dims)
+};
+
+template <bool BF>
+__device__ __forceinline__ RowConsts row_consts(const PP& p, int sel, int r) {
+  const int o = threadIdx.x;
+  RowConsts c{1.0f, 1.0f, 0.0f};
+  if (o >= p.D) return c;
+  const uint16_t* wn = sel ? p.v_norm : p.k_norm;
+  if ((p.norms & (1 << sel)) && wn) c.wn = dt_to_f<BF>(wn[o]);
+  const int half = p.rope_dims / 2;
+  if (sel == 0 && o < 2 * half) {
+    const int l = r % p.L;
+    const int i = p.rope_trad ? o >> 1 : (o < half ? o : o - half);
+    const float inv = p.rope_freqs ? 1.0f / p.rope_freqs[i]
+                                   : exp2f(-((float)i / (float)half) * p.rope_base);
+    const float theta = (p.rope_scale * (float)(p.pos0 + l)) * inv;
+    c.cs = cosf(theta);
+    c.sn = sinf(theta);
+  }
+  return c;
+}
+
+// Everything after the projection for one output row (token r) of kv head
+// h: `x` is thread o's projected value (the dtype-rounded sum), sel 0 / 1 =
+// K / V.  RMSNorm, RoPE (K), the checking copy, then the quantize-on-append.
+// Called by the whole CTA (it synchronises); `row` holds D floats, `red` 32.
 template <int BITS, bool BF>
-__global__ void __launch_bounds__(256) proj_epilogue_kernel(const PP p) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __shared__ float row[256];
-  __shared__ float red[8];
-  const int r = blockIdx.x, sel = blockIdx.y / p.Hkv, h = blockIdx.y - sel * p.Hkv;
+__device__ void finish_row(const PP& p, int sel, int h, int r, float x, const RowConsts& rc,
+                           float* row, float* red) {
   const int o = threadIdx.x, D = p.D;
   const int b = r / p.L, l = r - b * p.L;
-  const int src = (sel == 1 && p.v_from_k) ? 0 : sel;
-  float x = 0.0f;
-  if (o < D) {
-    const float* part = p.part + (((int64_t)src * p.Hkv + h) * p.ns * p.R + r) * D + o;
-    for (int s = 0; s < p.ns; s++) x += part[(int64_t)s * p.R * D];
-    x = round_dt<BF>(x);  // the projection's output, in the dtype
-  }
   if (p.norms & (1 << sel)) {
     // RMSNorm: x * (1 / sqrt(mean(x^2) + eps)) rounded, then * weight rounded
     const float ss = block_sum(o < D ? x * x : 0.0f, red);
@@ -168,7 +193,7 @@ __global__ void __launch_bounds__(256) proj_epilogue_kernel(const PP p) {
     const uint16_t* wn = sel ? p.v_norm : p.k_norm;
     if (o < D) {
       x = round_dt<BF>(x * n);
-      if (wn) x = round_dt<BF>(x * dt_to_f<BF>(wn[o]));
+      if (wn) x = round_dt<BF>(x * rc.wn);
     }
   }
   if (sel == 0 && p.rope_dims > 0) {
@@ -177,46 +202,295 @@ __global__ void __launch_bounds__(256) proj_epilogue_kernel(const PP p) {
     __syncthreads();
     const int half = p.rope_dims / 2;
     if (o < 2 * half) {
-      // pair index i, its two elements, and which of them this thread makes
+      // the pair's two elements, and which of them this thread makes
       const int i = p.rope_trad ? o >> 1 : (o < half ? o : o - half);
       const int e1 = p.rope_trad ? 2 * i : i, e2 = p.rope_trad ? 2 * i + 1 : i + half;
-      const bool first = o == e1;
-      const float inv = p.rope_freqs ? 1.0f / p.rope_freqs[i]
-                                     : exp2f(-((float)i / (float)half) * p.rope_base);
-      const float theta = (p.rope_scale * (float)(p.pos0 + l)) * inv;
-      const float cs = cosf(theta), sn = sinf(theta);
       const float x1 = row[e1], x2 = row[e2];
-      x = round_dt<BF>(first ? x1 * cs - x2 * sn : x1 * sn + x2 * cs);
+      x = round_dt<BF>(o == e1 ? x1 * rc.cs - x2 * rc.sn : x1 * rc.sn + x2 * rc.cs);
     }
   }
   uint16_t* dbg = sel ? p.v_out : p.k_out;
   if (dbg && o < D) dbg[(((int64_t)b * p.Hkv + h) * p.L + l) * D + o] = f_to_dt<BF>(x);
-  __syncthreads();
-  if (o < D) row[o] = x;
-  __syncthreads();
-  // quantize: thread t packs word t; the group's extremes are read from the row
+  // quantize: the group's extremes by warp shuffles (a group is gs / 32
+  // whole warps; D is a multiple of 32, so warps are wholly in or out of
+  // the row), then each thread's code, OR-ed into its word across the
+  // word's lanes
   constexpr int PER = 32 / BITS;
   constexpr float NB = (float)((1 << BITS) - 1);
-  const int words = D / PER, gs = p.gs, tpg = gs / PER;
-  if (o >= words) return;
-  const int g = o / tpg;
-  float mn = row[g * gs], mx = mn;
-  for (int j = 1; j < gs; j++) {
-    mn = fminf(mn, row[g * gs + j]);
-    mx = fmaxf(mx, row[g * gs + j]);
+  const int gs = p.gs, warp = threadIdx.x >> 5;
+  float mn = x, mx = x;
+  if (o < D) {
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    }
+  }
+  __syncthreads();  // `red` may still be read by the norm's block sum
+  if (o < D && (threadIdx.x & 31) == 0) {
+    red[warp] = mn;
+    red[16 + warp] = mx;
+  }
+  __syncthreads();
+  if (o >= D) return;
+  const int wpg = gs / 32, w0 = (o / gs) * wpg;
+  mn = red[w0];
+  mx = red[16 + w0];
+  for (int k = 1; k < wpg; k++) {
+    mn = fminf(mn, red[w0 + k]);
+    mx = fmaxf(mx, red[16 + w0 + k]);
   }
   float scale, bias;
   quant_params(mn, mx, NB, scale, bias);
-  uint32_t out = 0;
+  uint32_t word = quant_code(x, scale, bias, NB) << (BITS * (o % PER));
 #pragma unroll
-  for (int e = 0; e < PER; e++) out |= quant_code(row[o * PER + e], scale, bias, NB) << (BITS * e);
+  for (int off = 1; off < PER; off <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, off);
   const TripleView& dv = sel ? p.dv : p.dk;
   const int64_t drow = b * dv.batch_stride + h * dv.head_stride + p.dst_row0 + l;
-  dv.packed[drow * words + o] = out;
-  if (o % tpg == 0) {
-    const int groups = D / gs;
+  if (o % PER == 0) dv.packed[drow * (D / PER) + o / PER] = word;
+  if (o % gs == 0) {
+    const int groups = D / gs, g = o / gs;
     dv.scales[drow * groups + g] = f_to_dt<BF>(scale);
     dv.biases[drow * groups + g] = f_to_dt<BF>(bias);
+  }
+}
+
+template <int BITS, bool BF>
+__global__ void __launch_bounds__(256) proj_epilogue_kernel(const PP p) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float row[256];
+  __shared__ float red[32];
+  const int r = blockIdx.x, sel = blockIdx.y / p.Hkv, h = blockIdx.y - sel * p.Hkv;
+  const int o = threadIdx.x, D = p.D;
+  const int src = (sel == 1 && p.v_from_k) ? 0 : sel;
+  float x = 0.0f;
+  if (o < D) {
+    // the split partials, loaded together, summed in split order
+    const float* part = p.part + (((int64_t)src * p.Hkv + h) * p.ns * p.R + r) * D + o;
+    const int64_t ss = (int64_t)p.R * D;
+    for (int s0 = 0; s0 < p.ns; s0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[k] = s0 + k < p.ns ? part[(s0 + k) * ss] : 0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; k++) x += v[k];
+    }
+    x = round_dt<BF>(x);  // the projection's output, in the dtype
+  }
+  finish_row<BITS, BF>(p, sel, h, r, x, row_consts<BF>(p, sel, r), row, red);
+}
+
+// Decode-sized steps (R <= 4 rows): one launch.  A cluster of CS CTAs per
+// (K|V, kv head, row chunk) splits the hidden dimension; thread o owns
+// output column o.  Each thread first issues everything it will read —
+// its weight-row slice (16-byte loads), its group scales and biases, the
+// norm weight and the RoPE table before the dependency wait, its share of
+// the input slice after it — then stages the inputs in shared memory and
+// accumulates per group
+//   s * sum(code * x) + b * sum(x)
+// (the affine dequantisation factored out of the dot product; codes turned
+// into floats by one byte permute each, see code_hi / code_lo; four independent
+// partial sums).  The cluster's CTA 0 sums the CS partials from the
+// others' shared memory in rank order (deterministic) and runs finish_row.
+// With V = K's projection, the K cluster finishes both.  256 threads of at
+// most 128 registers: two CTAs fit an SM, so the next step's CTAs are
+// resident (waiting on the dependency) before this step ends.
+constexpr int kMaxG = 8;    // weight groups per CTA
+constexpr int kNB = 8;      // 16-byte weight loads per thread issued up front
+
+// Codes as floats by one byte permute each (byte K of `w` into the float's
+// bits, exponent byte 0x4B above it):
+//  * 4-bit: the word's nibbles pre-shifted to bits 3..6 of their bytes
+//    (code_hi) land in mantissa bits 19..22: 2^19 (16 + c).  Then
+//      sum(x * 2^19 (16 + c)) * 2^-19 - 16 * sum(x) = sum(x * c),
+//    exact products (fp16 / bf16 x), about 1.5 bits of the f32 sum lost to
+//    the offset — far below the dtype's precision;
+//  * 8-bit: the code lands in the low mantissa byte: 2^23 + c, and one
+//    subtraction gives c exactly (code_lo).
+template <int K>
+__device__ __forceinline__ float code_hi(uint32_t w) {
+  return __uint_as_float(__byte_perm(w, 0x4Bu, 0x4055u | (K << 8)));
+}
+template <int K>
+__device__ __forceinline__ float code_lo(uint32_t w) {
+  return __uint_as_float(__byte_perm(w, 0x4Bu, 0x4550u | K)) - 8388608.0f;
+}
+
+template <int WBITS, int BITS, bool BF, int RC, int CS>
+__global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float row[256];
+  __shared__ float red[32];
+  extern __shared__ float sm[];  // part[RC][D], sumx[RC][kMaxG], xs[RC][span]
+  const int rank = (int)cluster.block_rank();
+  const int sel = blockIdx.y / p.Hkv, h = blockIdx.y - sel * p.Hkv;
+  const W w = sel ? p.wv : p.wk;
+  const int o = threadIdx.x, D = p.D;
+  const int G = p.hidden / w.gs, gs = w.gs;
+  const int g0 = rank * G / CS, g1 = (rank + 1) * G / CS, ng = g1 - g0;
+  const int span = ng * gs;
+  float* part = sm;
+  float* sumx = sm + RC * D;
+  float* xs = sumx + RC * kMaxG;
+  const int r0 = blockIdx.z * RC, nr = min(RC, p.R - r0);
+  constexpr int PER = 32 / WBITS;
+  constexpr int E4 = 4 * PER;            // elements per 16-byte load
+  const int u4pg = gs / E4;              // 16-byte loads per group
+  const int n4 = ng * u4pg;
+  const int64_t wrow = (int64_t)h * D + o;
+  const uint4* wp = reinterpret_cast<const uint4*>(w.packed + wrow * (p.hidden / PER)) +
+                    (int64_t)g0 * u4pg;
+  // 1. the layer's parameters — weights, scales / biases (raw), norm weight,
+  //    RoPE table — are loaded before waiting for the preceding kernel (they
+  //    are not its output: the entry point requires it), so they stream in
+  //    while that kernel finishes; the input rows only after the wait
+  uint4 q[kNB];
+#pragma unroll
+  for (int j = 0; j < kNB; j++) q[j] = j < n4 ? __ldg(wp + j) : make_uint4(0, 0, 0, 0);
+  uint16_t sc16[kMaxG], bi16[kMaxG];
+  const uint16_t* sp = w.scales + wrow * G + g0;
+  const uint16_t* bp = w.biases ? w.biases + wrow * G + g0 : nullptr;
+#pragma unroll
+  for (int k = 0; k < kMaxG; k++) {
+    sc16[k] = k < ng ? __ldg(sp + k) : (uint16_t)0;
+    bi16[k] = (k < ng && bp) ? __ldg(bp + k) : (uint16_t)0;
+  }
+  RowConsts rcs[RC], rcv[RC];
+  if (rank == 0) {
+#pragma unroll
+    for (int r = 0; r < RC; r++) {
+      rcs[r] = row_consts<BF>(p, sel, r0 + r < p.R ? r0 + r : 0);
+      rcv[r] = p.v_from_k ? row_consts<BF>(p, 1, r0 + r < p.R ? r0 + r : 0) : rcs[r];
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  constexpr int kXL = RC == 1 ? 4 : 2;  // input elements per thread and row held in flight
+  uint16_t xv[RC][kXL];
+#pragma unroll
+  for (int r = 0; r < RC; r++)
+#pragma unroll
+    for (int t = 0; t < kXL; t++) {
+      const int j = o + t * D;
+      xv[r][t] = (r < nr && j < span) ? __ldg(p.x + (int64_t)(r0 + r) * p.hidden + (int64_t)g0 * gs + j)
+                                      : (uint16_t)0;
+    }
+  // 2. the input slice into shared memory (slices longer than kXL * D
+  //    elements per row take the rest with plain loads)
+#pragma unroll
+  for (int r = 0; r < RC; r++) {
+#pragma unroll
+    for (int t = 0; t < kXL; t++) {
+      const int j = o + t * D;
+      if (j < span) xs[r * span + j] = dt_to_f<BF>(xv[r][t]);
+    }
+    for (int j = o + kXL * D; j < span; j += D)
+      xs[r * span + j] = r < nr ? dt_to_f<BF>(p.x[(int64_t)(r0 + r) * p.hidden + (int64_t)g0 * gs + j])
+                                : 0.0f;
+  }
+  __syncthreads();
+  // sum(x) per (row, group) of the slice: one warp per pair
+  {
+    const int warp = o >> 5, lane = o & 31, nw = blockDim.x >> 5;
+    for (int pr = warp; pr < RC * ng; pr += nw) {
+      const int r = pr / ng, gl = pr - r * ng;
+      float t = 0.0f;
+      for (int j = lane; j < gs; j += 32) t += xs[r * span + gl * gs + j];
+#pragma unroll
+      for (int off = 16; off; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+      if (lane == 0) sumx[r * kMaxG + gl] = t;
+    }
+  }
+  __syncthreads();
+  // 3. the dot products, group by group
+  float out[RC], a[RC][4];
+#pragma unroll
+  for (int r = 0; r < RC; r++) out[r] = a[r][0] = a[r][1] = a[r][2] = a[r][3] = 0.0f;
+  auto consume = [&](const uint4& v4, int j) {
+    const uint32_t qq[4] = {v4.x, v4.y, v4.z, v4.w};
+    const float* xb = xs + j * E4;
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      // the word's codes one per byte: 4-bit words split into even / odd
+      // elements at bits 3..6 of each byte; 8-bit words are bytes already
+      float cf[PER];
+      if (WBITS == 4) {
+        const uint32_t b0 = (qq[kk] << 3) & 0x78787878u;
+        const uint32_t b1 = (qq[kk] >> 1) & 0x78787878u;
+        cf[0] = code_hi<0>(b0); cf[1] = code_hi<0>(b1);
+        cf[2] = code_hi<1>(b0); cf[3] = code_hi<1>(b1);
+        cf[4] = code_hi<2>(b0); cf[5] = code_hi<2>(b1);
+        cf[6] = code_hi<3>(b0); cf[7] = code_hi<3>(b1);
+      } else {
+        cf[0] = code_lo<0>(qq[kk]); cf[1] = code_lo<1>(qq[kk]);
+        cf[2] = code_lo<2>(qq[kk]); cf[3] = code_lo<3>(qq[kk]);
+      }
+#pragma unroll
+      for (int r = 0; r < RC; r++) {
+#pragma unroll
+        for (int e4 = 0; e4 < PER; e4 += 4) {
+          const float4 xv4 = *reinterpret_cast<const float4*>(xb + r * span + kk * PER + e4);
+          a[r][0] = fmaf(xv4.x, cf[e4], a[r][0]);
+          a[r][1] = fmaf(xv4.y, cf[e4 + 1], a[r][1]);
+          a[r][2] = fmaf(xv4.z, cf[e4 + 2], a[r][2]);
+          a[r][3] = fmaf(xv4.w, cf[e4 + 3], a[r][3]);
+        }
+      }
+    }
+    const int k = j / u4pg;
+    if (j - k * u4pg == u4pg - 1) {
+      uint16_t s16 = sc16[0], b16 = bi16[0];
+#pragma unroll
+      for (int t = 1; t < kMaxG; t++)
+        if (t == k) {
+          s16 = sc16[t];
+          b16 = bi16[t];
+        }
+      const float s = dt_to_f<BF>(s16), b = dt_to_f<BF>(b16);
+#pragma unroll
+      for (int r = 0; r < RC; r++) {
+        const float sx = sumx[r * kMaxG + k];
+        const float acc = (a[r][0] + a[r][1]) + (a[r][2] + a[r][3]);
+        const float dot = WBITS == 4 ? fmaf(acc, 1.0f / 524288.0f, -16.0f * sx)  // sum(x * code)
+                                     : acc;
+        out[r] = fmaf(s, dot, fmaf(b, sx, out[r]));
+        a[r][0] = a[r][1] = a[r][2] = a[r][3] = 0.0f;
+      }
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < kNB; j++) {
+    if (j >= n4) break;
+    consume(q[j], j);
+  }
+  for (int j = kNB; j < n4; j++) consume(__ldg(wp + j), j);
+#pragma unroll
+  for (int r = 0; r < RC; r++) part[r * D + o] = out[r];
+  cluster.sync();
+  float xsum[RC];
+#pragma unroll
+  for (int r = 0; r < RC; r++) xsum[r] = 0.0f;
+  if (rank == 0) {
+#pragma unroll
+    for (int r = 0; r < RC; r++) {
+      float v[CS];
+#pragma unroll
+      for (int c = 0; c < CS; c++) v[c] = cluster.map_shared_rank(part, c)[r * D + o];
+      float t = 0.0f;
+#pragma unroll
+      for (int c = 0; c < CS; c++) t += v[c];
+      xsum[r] = round_dt<BF>(t);  // the projection's output, in the dtype
+    }
+  }
+  cluster.sync();  // the other CTAs' shared memory stays alive until read
+  if (rank != 0) return;
+#pragma unroll
+  for (int r = 0; r < RC; r++) {
+    if (r >= nr) break;
+    finish_row<BITS, BF>(p, sel, h, r0 + r, xsum[r], rcs[r], row, red);
+    if (p.v_from_k) finish_row<BITS, BF>(p, 1, h, r0 + r, xsum[r], rcv[r], row, red);
   }
 }
 
@@ -235,7 +509,96 @@ int32_t partial_for(int RC, dim3 grid, int threads, size_t smem, cudaStream_t st
 
 using namespace proj;
 
+// Cluster size of the one-launch path on this device: 16 CTAs (a
+// non-portable size) where the device can hold such clusters of this
+// kernel, else the portable 8; queried once per device.
+static int cluster_size(int dev) {
+  static std::mutex mu;
+  static int cached[64] = {0};
+  if (dev < 0 || dev >= 64) return 8;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cached[dev]) return cached[dev];
+  int cs = 8;
+  auto kern = proj_cluster_kernel<4, 4, true, 4, 16>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(16, 16, 1);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 16 * 1024;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 16;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= 8) cs = 16;
+  }
+  cudaGetLastError();  // a refused query leaves no sticky error
+  cached[dev] = cs;
+  return cs;
+}
+
+// The one-launch cluster path: a few rows, every CTA's slice of the hidden
+// dimension within kMaxG groups, its inputs within 48 KB of shared memory.
+static bool use_cluster(const ProjArgs& a, int cs) {
+  const int R = a.B * a.L;
+  const int gk = a.hidden / a.wk.gs;
+  const int gv = a.v_from_k ? gk : a.hidden / a.wv.gs;
+  const int gmax = (std::max(gk, gv) + cs - 1) / cs;
+  const int span = gmax * std::max(a.wk.gs, a.v_from_k ? a.wk.gs : a.wv.gs);
+  return R <= 4 && gmax <= kMaxG && (size_t)4 * (256 + kMaxG + span) * 4 <= 48 * 1024;
+}
+
+template <int WBITS, int BITS, bool BF, int CS>
+static int32_t launch_cluster(const PP& p, int RC, int sely, size_t smem, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CS, sely * p.Hkv, (p.R + RC - 1) / RC);
+  cfg.blockDim = dim3(p.D);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  auto k1 = proj_cluster_kernel<WBITS, BITS, BF, 1, CS>;
+  auto k4 = proj_cluster_kernel<WBITS, BITS, BF, 4, CS>;
+  if (CS > 8) {
+    KVQ_CUDA_TRY(cudaFuncSetAttribute(RC == 1 ? k1 : k4,
+                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  }
+  KVQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, RC == 1 ? k1 : k4, p));
+  return KVQ_OK;
+}
+
+template <int WBITS, int BITS>
+static int32_t launch_cluster_dt(const PP& p, bool bf, int cs, int RC, int sely, size_t smem,
+                                 cudaStream_t st) {
+  if (cs == 16)
+    return bf ? launch_cluster<WBITS, BITS, true, 16>(p, RC, sely, smem, st)
+              : launch_cluster<WBITS, BITS, false, 16>(p, RC, sely, smem, st);
+  return bf ? launch_cluster<WBITS, BITS, true, 8>(p, RC, sely, smem, st)
+            : launch_cluster<WBITS, BITS, false, 8>(p, RC, sely, smem, st);
+}
+
+static int current_cluster_size() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 8;
+  return cluster_size(dev);
+}
+
 size_t project_workspace_bytes(const ProjArgs& a, int Hkv, int D, int* splits) {
+  const int cs = current_cluster_size();
+  if (use_cluster(a, cs)) {
+    if (splits) *splits = cs;
+    return 0;
+  }
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int R = a.B * a.L;
@@ -255,7 +618,9 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
   int ns = 1;
   const size_t need = project_workspace_bytes(a, Hkv, D, &ns);
   int32_t rc = KVQ_OK;
-  if (!ws) {
+  if (need == 0) {
+    ws = nullptr;  // the cluster path keeps its partials on chip
+  } else if (!ws) {
     int dev = 0;
     KVQ_CUDA_TRY(cudaGetDevice(&dev));
     ws = managed_workspace(dev, need, st, &rc);
@@ -277,7 +642,7 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
   p.Hkv = Hkv;
   p.D = D;
   p.ns = ns;
-  p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kPartialOff);
+  p.part = ws ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kPartialOff) : nullptr;
   p.k_norm = static_cast<const uint16_t*>(a.k_norm);
   p.v_norm = static_cast<const uint16_t*>(a.v_norm);
   p.norms = a.norms;
@@ -297,13 +662,30 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
   p.gs = g.gs;
   const bool bf = dtype == KVQ_DTYPE_BFLOAT16;
   const int threads = (D + 31) / 32 * 32;
-  // projection: one V-less launch when V is K's projection
-  const int RC = proj_rows(p.R);
-  const dim3 g1(ns, 2 * Hkv, (p.R + RC - 1) / RC);
-  const int wmax = std::max(a.wk.gs, a.v_from_k ? 0 : a.wv.gs);
-  const size_t smem = (size_t)RC * wmax * sizeof(float);
   if (a.wk.bits != (a.v_from_k ? a.wk.bits : a.wv.bits))
     return fail(KVQ_ERR_ARG, "the K and V projections must share a bit width");
+  const int cs = current_cluster_size();
+  if (use_cluster(a, cs)) {
+    const int RC = p.R <= 1 ? 1 : 4;
+    // the largest slice of either projection, in elements
+    int span = 0;
+    for (const ProjWeights* pw : {&a.wk, &a.wv}) {
+      if (pw == &a.wv && a.v_from_k) continue;
+      span = std::max(span, (a.hidden / pw->gs + cs - 1) / cs * pw->gs);
+    }
+    const size_t smem = (size_t)RC * (D + kMaxG + span) * sizeof(float);
+    const int sely = a.v_from_k ? 1 : 2;
+    switch ((a.wk.bits == 8 ? 2 : 0) + (g.bits == 8 ? 1 : 0)) {
+      case 0: return launch_cluster_dt<4, 4>(p, bf, cs, RC, sely, smem, st);
+      case 1: return launch_cluster_dt<4, 8>(p, bf, cs, RC, sely, smem, st);
+      case 2: return launch_cluster_dt<8, 4>(p, bf, cs, RC, sely, smem, st);
+      default: return launch_cluster_dt<8, 8>(p, bf, cs, RC, sely, smem, st);
+    }
+  }
+  const dim3 g1(ns, 2 * Hkv, (p.R + proj_rows(p.R) - 1) / proj_rows(p.R));
+  const int RC = proj_rows(p.R);
+  const int wmax = std::max(a.wk.gs, a.v_from_k ? 0 : a.wv.gs);
+  const size_t smem = (size_t)RC * wmax * sizeof(float);
   rc = a.wk.bits == 4 ? (bf ? partial_for<4, true>(RC, g1, threads, smem, st, p)
                             : partial_for<4, false>(RC, g1, threads, smem, st, p))
                       : (bf ? partial_for<8, true>(RC, g1, threads, smem, st, p)

@@ -9,8 +9,9 @@
 * Projection parity: random inputs and oracle-quantized weights (4 / 8
   bit, group 32 / 64 / 128, with biases), K RMSNorm with weight, V RMSNorm
   without (gemma4.ts:174-177), default / proportional / partial-traditional
-  RoPE, attention_k_eq_v, fp16 and bf16, batch 1 / 4 / 2 with 1 / 1 / 37
-  rows (the 1-, 4- and 16-row projection tiles): the rows before
+  RoPE, attention_k_eq_v, fp16 and bf16, batch 1 / 4 / 2 / 1 with 1 / 1 /
+  37 / 20 rows (the one-launch cluster path at 1 and 4 rows, the split
+  projection + epilogue pair at 16-row tiles): the rows before
   quantisation match the oracle's project_kv within 3 dtype ulps of the
   row's largest element (the product sums in f32, the oracle in f64), at
   least 90 % of them exactly; the cache rows are bit-exact with the oracle's
@@ -21,7 +22,8 @@
   chunked append through the temporal re-layout — RoPE positions follow
   the logical offset, the ring matches the oracle's bit for bit.
 * A caller workspace of the size kvq_append_projected_workspace reports
-  gives the same rows; one byte less is refused (KVQ_ERR_WORKSPACE).
+  gives the same rows; one byte less is refused (KVQ_ERR_WORKSPACE);
+  decode-sized steps (the one-launch cluster path) need none.
 """
 import ctypes
 import os
@@ -233,27 +235,31 @@ def test_caller_workspace_sized_by_query():
     import torch
     import kvq
     from kvq import _lib
-    dt, B, H, D, hidden = BF16, 1, 4, 128, 1024
+    dt, B, H, D, hidden, L = BF16, 1, 4, 128, 1024, 16
     rng = np.random.default_rng(9)
     kq, _ = make_qlinear(rng, H * D, hidden, 64, 4, dt)
     proj = kvq.KvProjection(kq, None, D, rope_dims=D)
-    x = _dev_bits(O.to_dtype_bits(rng.uniform(-1, 1, (B, 3, hidden)).astype(np.float32), dt), dt)
+    x = _dev_bits(O.to_dtype_bits(rng.uniform(-1, 1, (B, L, hidden)).astype(np.float32), dt), dt)
     ref = kvq.QuantizedKVCache(64, 8)
-    k_ref = torch.empty(B, H, 3, D, dtype=torch.bfloat16, device="cuda")
+    k_ref = torch.empty(B, H, L, D, dtype=torch.bfloat16, device="cuda")
     ref.update_and_fetch_projected(x, proj, k_out=k_ref)
     cache = kvq.QuantizedKVCache(64, 8)
     cache._ensure_shape(B, H, D, torch.bfloat16, 0)
     lib = _lib.lib()
     s = proj._struct()
     n = ctypes.c_size_t()
-    _lib.check(lib.kvq_append_projected_workspace(cache._h, 3, ctypes.byref(s), ctypes.byref(n)))
+    # decode-sized steps keep their partials on chip: no workspace
+    _lib.check(lib.kvq_append_projected_workspace(cache._h, 1, ctypes.byref(s), ctypes.byref(n)))
+    assert n.value == 0
+    _lib.check(lib.kvq_append_projected_workspace(cache._h, L, ctypes.byref(s), ctypes.byref(n)))
+    assert n.value > 0
     ws = torch.zeros(n.value, dtype=torch.uint8, device="cuda")
     k_out = torch.empty_like(k_ref)
     st = torch.cuda.current_stream().cuda_stream
-    rc = lib.kvq_append_projected(cache._h, x.data_ptr(), 3, ctypes.byref(s), k_out.data_ptr(),
+    rc = lib.kvq_append_projected(cache._h, x.data_ptr(), L, ctypes.byref(s), k_out.data_ptr(),
                                   None, ws.data_ptr(), n.value - 1, st)
     assert rc == _lib.ERR_WORKSPACE
-    _lib.check(lib.kvq_append_projected(cache._h, x.data_ptr(), 3, ctypes.byref(s),
+    _lib.check(lib.kvq_append_projected(cache._h, x.data_ptr(), L, ctypes.byref(s),
                                         k_out.data_ptr(), None, ws.data_ptr(), n.value, st))
     torch.cuda.synchronize()
     assert torch.equal(k_out.view(torch.int16), k_ref.view(torch.int16))
