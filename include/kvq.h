@@ -143,8 +143,11 @@ typedef struct kvq_qlinear {
  * (ProportionalRoPE's freqs, :131-165, whose infinite entries leave their
  * pair unrotated; the llama3 / yarn / longrope tables of
  * src/model/universal/rope.ts); the rest of the row passes through;
- * rope_dims 0: no RoPE.  Position of token l = the cache offset before the
- * append + l. */
+ * rope_dims 0: no RoPE.  rope_pre_scale (yarn's mscale, longrope's su
+ * scale; UniversalRope.apply, rope.ts:51-75) multiplies the first rope_dims
+ * elements of K, after its norm and before RoPE, by the scale rounded to
+ * the dtype, rounding the product.  Position of token l = the cache offset
+ * before the append + l. */
 typedef struct kvq_kv_projection {
   kvq_qlinear k_proj;
   kvq_qlinear v_proj;          /* ignored when v_from_k */
@@ -156,6 +159,7 @@ typedef struct kvq_kv_projection {
   int32_t rope_dims;
   int32_t rope_traditional;
   float rope_base, rope_scale;
+  float rope_pre_scale;        /* 0 or 1: none */
   const float* rope_freqs;
 } kvq_kv_projection;
 

@@ -605,6 +605,7 @@ int32_t make_proj_args(const kvq_cache* c, const void* x, int32_t L, const kvq_k
   a.rope_traditional = pr->rope_traditional != 0;
   a.rope_base = pr->rope_base;
   a.rope_scale = pr->rope_scale;
+  a.rope_pre_scale = pr->rope_pre_scale;
   a.rope_freqs = pr->rope_freqs;
   a.pos0 = c->offset;
   return KVQ_OK;

@@ -75,6 +75,7 @@ struct ProjArgs {
   int rope_dims;       // 0: no RoPE
   bool rope_traditional;  // pairs (2i, 2i+1) instead of (i, i + dims/2)
   float rope_base, rope_scale;
+  float rope_pre_scale;     // 0 or 1: none
   const float* rope_freqs;  // [rope_dims / 2] device, nullable
   int64_t pos0;        // position of row l = pos0 + l
   void* k_out;         // [B, Hkv, L, D] rows before quantisation, nullable

@@ -70,7 +70,7 @@ struct PP {
   int norms;          // bit 0: K, bit 1: V
   float eps;
   int rope_dims, rope_trad;
-  float rope_base, rope_scale;
+  float rope_base, rope_scale, rope_pre;
   const float* rope_freqs;
   int64_t pos0;
   uint16_t* k_out;    // [B, Hkv, L, D] nullable
@@ -197,6 +197,8 @@ __device__ void finish_row(const PP& p, int sel, int h, int r, float x, const Ro
     }
   }
   if (sel == 0 && p.rope_dims > 0) {
+    // the pre-rope input scale (a weak scalar: rounded to the dtype first)
+    if (p.rope_pre != 0.0f && o < p.rope_dims) x = round_dt<BF>(x * round_dt<BF>(p.rope_pre));
     __syncthreads();
     if (o < D) row[o] = x;
     __syncthreads();
@@ -651,6 +653,7 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
   p.rope_trad = a.rope_traditional ? 1 : 0;
   p.rope_base = a.rope_freqs ? 0.0f : (float)std::log2((double)a.rope_base);
   p.rope_scale = a.rope_scale;
+  p.rope_pre = (a.rope_pre_scale == 0.0f || a.rope_pre_scale == 1.0f) ? 0.0f : a.rope_pre_scale;
   p.rope_freqs = a.rope_freqs;
   p.pos0 = a.pos0;
   p.k_out = static_cast<uint16_t*>(a.k_out);

@@ -67,7 +67,8 @@ class KvProjection(ctypes.Structure):
                 ("k_norm", ctypes.c_int32), ("v_norm", ctypes.c_int32),
                 ("k_norm_weight", ctypes.c_void_p), ("v_norm_weight", ctypes.c_void_p),
                 ("norm_eps", ctypes.c_float), ("rope_dims", ctypes.c_int32),
-                ("rope_traditional", ctypes.c_int32), ("rope_base", ctypes.c_float), ("rope_scale", ctypes.c_float),
+                ("rope_traditional", ctypes.c_int32), ("rope_base", ctypes.c_float),
+                ("rope_scale", ctypes.c_float), ("rope_pre_scale", ctypes.c_float),
                 ("rope_freqs", ctypes.c_void_p)]
 
 

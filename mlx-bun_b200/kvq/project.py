@@ -54,7 +54,8 @@ class KvProjection:
     """The K/V side of one attention layer: k_proj, v_proj (None: V is K's
     projection, attention_k_eq_v), the norms and the RoPE parameters
     (rope_dims 0: none; rope_freqs: a device f32 [rope_dims / 2] table
-    replacing rope_base, as ProportionalRoPE and the scaled variants use)."""
+    replacing rope_base, as ProportionalRoPE and the scaled variants use;
+    rope_pre_scale: yarn's / longrope's input scale on K's rotated part)."""
     k_proj: QuantizedLinear
     v_proj: QuantizedLinear | None
     head_dim: int
@@ -68,6 +69,7 @@ class KvProjection:
     rope_base: float = 10000.0
     rope_scale: float = 1.0
     rope_freqs: torch.Tensor | None = None
+    rope_pre_scale: float = 1.0
 
     @property
     def kv_heads(self) -> int:
@@ -93,6 +95,7 @@ class KvProjection:
         s.rope_traditional = int(self.rope_traditional)
         s.rope_base = self.rope_base
         s.rope_scale = self.rope_scale
+        s.rope_pre_scale = self.rope_pre_scale
         s.rope_freqs = self.rope_freqs.data_ptr() if self.rope_freqs is not None else None
         return s
 

@@ -539,7 +539,7 @@ def project_kv(x: np.ndarray, proj: dict, offset: int, dtype: int):
     proj: k_proj / v_proj = (packed, scales, biases, group_size, bits) (v_proj
     None: attention_k_eq_v), head_dim, k_norm / v_norm (bool), k_norm_weight /
     v_norm_weight (f32 or None), eps, rope_dims, rope_traditional, rope_base,
-    rope_scale, rope_freqs (f32 or None)."""
+    rope_scale, rope_freqs (f32 or None), rope_pre_scale."""
     B, L, _ = x.shape
     D = proj["head_dim"]
     k = quantized_linear(x, *proj["k_proj"], dtype)
@@ -552,6 +552,12 @@ def project_kv(x: np.ndarray, proj: dict, offset: int, dtype: int):
     if proj.get("v_norm"):
         v = rms_norm(v, proj.get("v_norm_weight"), proj["eps"], dtype)
     if proj.get("rope_dims", 0):
+        pre = proj.get("rope_pre_scale", 1.0)
+        if pre not in (0.0, 1.0):  # UniversalRope.apply (rope.ts:51-75): a weak scalar
+            dims = proj["rope_dims"]
+            k = k.copy()
+            k[..., :dims] = round_dt(k[..., :dims] * round_dt(np.array([pre], np.float32),
+                                                              dtype)[0], dtype)
         k = rope(k, proj["rope_dims"], proj.get("rope_traditional", False),
                  proj.get("rope_base"), proj.get("rope_scale", 1.0), offset,
                  proj.get("rope_freqs"), dtype)

@@ -3,9 +3,11 @@
 * RoPE goldens: with identity projection weights (8-bit codes 0/1, scale 1,
   bias 0, exact) and the norms off, the rows the fused call produces before
   quantisation are mlx fast::rope of the input — checked against mlx-bun's
-  RoPE golden vectors (MLX 0.31.2, seven variants, offsets 0 and 5, the
-  offset-5 rows appended after five other rows) to at most one element per
-  case, one bf16 ulp (the oracle's own bar against the same goldens).
+  RoPE golden vectors (MLX 0.31.2, seven variants — yarn's and longrope's
+  pre-rope input scale applied by the kernel (rope_pre_scale) — offsets 0
+  and 5, the offset-5 rows appended after five other rows) to at most one
+  element per case, one bf16 ulp (the oracle's own bar against the same
+  goldens).
 * Projection parity: random inputs and oracle-quantized weights (4 / 8
   bit, group 32 / 64 / 128, with biases), K RMSNorm with weight, V RMSNorm
   without (gemma4.ts:174-177), default / proportional / partial-traditional
@@ -102,14 +104,16 @@ def test_rope_goldens_through_fused_append():
     import kvq
     z = np.load(os.path.join(HERE, "golden", "universal_rope.npz"))
     for name in [str(n) for n in z["names"]]:
-        x, dims, trad, base, scale, freqs, offsets = rope_case_inputs(z, name)
+        # the raw input; the variant's pre-rope scale goes through the kernel
+        x, dims, trad, base, scale, freqs, offsets = rope_case_inputs(z, name, prescale=False)
+        pre = float(z[f"{name}/params"][4])
         _, H, L, D = x.shape
         ident = identity_qlinear(H * D, BF16)
         fr = torch.from_numpy(np.ascontiguousarray(freqs, np.float32)).cuda() \
             if freqs is not None else None
         proj = kvq.KvProjection(ident, None, D, k_norm=False, v_norm=False, rope_dims=dims,
                                 rope_traditional=trad, rope_base=base, rope_scale=scale,
-                                rope_freqs=fr)
+                                rope_freqs=fr, rope_pre_scale=pre)
         xin = O.to_dtype_bits(x.transpose(0, 2, 1, 3).reshape(1, L, H * D), BF16)
         for off in offsets:
             cache = kvq.QuantizedKVCache(32, 8)

@@ -29,14 +29,15 @@ def _rope_cases():
     return z, [str(n) for n in z["names"]]
 
 
-def rope_case_inputs(z, name):
+def rope_case_inputs(z, name, prescale=True):
     """(x as bf16 values, dims, traditional, base, scale, freqs, offsets)
-    with the variant's pre-rope input scale already applied."""
+    with the variant's pre-rope input scale applied (unless `prescale` is
+    False)."""
     p = z[f"{name}/params"]
     dims, base, scale, trad, pre, always = p[:6]
     dims = int(dims)
     x = O.round_dt(z[f"{name}/input"], O.BF16)
-    if always or pre != 1.0:
+    if prescale and (always or pre != 1.0):
         s = O.round_dt(np.array([pre], np.float32), O.BF16)[0]
         x = x.copy()
         x[..., :dims] = O.round_dt(x[..., :dims] * s, O.BF16)
@@ -72,6 +73,47 @@ def test_rope_passes_through_past_dims_and_is_identity_at_zero():
     # infinite frequencies (ProportionalRoPE's tail) leave their pairs unrotated
     fr = np.full(32, np.inf, np.float32)
     assert np.array_equal(O.rope(x, 64, False, None, 1.0, 7, fr, O.F16), x)
+
+
+def test_project_kv_applies_pre_scale_like_the_goldens():
+    """project_kv's rope_pre_scale (identity weights, no norms) reproduces
+    the yarn and longrope goldens from the raw inputs."""
+    z, _ = _rope_cases()
+    for name in ("yarn", "longrope"):
+        x, dims, trad, base, scale, freqs, offsets = rope_case_inputs(z, name, prescale=False)
+        _, H, L, D = x.shape
+        n = H * D
+        packed = np.zeros((n, n // 4), np.uint32)
+        r = np.arange(n)
+        packed[r, r // 4] = (1 << (8 * (r % 4))).astype(np.uint32)
+        one = O.to_dtype_bits(np.ones((n, n // 32), np.float32), O.BF16)
+        spec = dict(head_dim=D, k_proj=(packed, one, np.zeros_like(one), 32, 8), v_proj=None,
+                    k_norm=False, v_norm=False, eps=1e-6, rope_dims=dims,
+                    rope_traditional=trad, rope_base=base, rope_scale=scale, rope_freqs=freqs,
+                    rope_pre_scale=float(z[f"{name}/params"][4]))
+        xin = x.transpose(0, 2, 1, 3).reshape(1, L, n)
+        for off in offsets:
+            k, _ = O.project_kv(xin, spec, off, O.BF16)
+            check_rope_golden(k, z[f"{name}/out{off}"], f"project_kv {name}@{off}")
+
+
+def test_struct_layout_matches_the_header(tmp_path):
+    """ctypes' kvq_qlinear / kvq_kv_projection match the C header's."""
+    import subprocess
+    from kvq import _lib
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "kvq.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(kvq_qlinear),'
+                   ' sizeof(kvq_kv_projection), offsetof(kvq_kv_projection, k_norm_weight),'
+                   ' offsetof(kvq_kv_projection, norm_eps), offsetof(kvq_kv_projection,'
+                   ' rope_pre_scale), offsetof(kvq_kv_projection, rope_freqs)); return 0;}\n')
+    exe = tmp_path / "sz"
+    inc = os.path.join(os.path.dirname(HERE), "include")
+    subprocess.check_call(["gcc", "-I", inc, str(src), "-o", str(exe)])
+    got = [int(v) for v in subprocess.check_output([str(exe)]).split()]
+    P = _lib.KvProjection
+    assert got == [ctypes.sizeof(_lib.QLinear), ctypes.sizeof(P), P.k_norm_weight.offset,
+                   P.norm_eps.offset, P.rope_pre_scale.offset, P.rope_freqs.offset]
 
 
 def test_rms_norm_known_answers():
