@@ -739,7 +739,8 @@ def run_kv_projection(args, rank, world, local_rank):
     (kvq_append_projected), one replica per GPU.  Decode: one token per
     step through each of the 48 layers (a CUDA graph per pass over the
     layers; 425 MB of weights cycled, above L2), timed with CUDA events.
-    Prefill: one 512-token chunk through one layer, timed the same way."""
+    Prefill: one 512-token chunk through one layer, timed the same way
+    (FLOPs: 2 x tokens x hidden x (K + V output features))."""
     import torch
     c = CFGP
     device = torch.device("cuda", local_rank)
@@ -805,7 +806,8 @@ def run_kv_projection(args, rank, world, local_rank):
                    "timing": "a CUDA graph per pass over the 48 layers, CUDA events"},
         "prefill_chunk": {"tokens": c["chunk"], "us_per_layer": round(pre_s * 1e6, 2),
                           "tflops": round(flops / pre_s / 1e12, 2),
-                          "note": "CUDA-core FMA projection (no tensor cores on this path)"},
+                          "kernels": "proj_xprep_kernel + proj_mma_kernel (mma.sync, codes as "
+                                     "exact fp16 operands) + proj_epilogue_kernel"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "kernel": "proj_partial_kernel<4,bf16,1> + proj_epilogue_kernel<4,bf16>",

@@ -49,6 +49,7 @@ namespace proj {
 using attn::dt_to_f;
 using attn::f_to_dt;
 using attn::round_dt;
+using attn::pack_h2;
 
 
 struct W {
@@ -283,6 +284,124 @@ __global__ void __launch_bounds__(256) proj_epilogue_kernel(const PP p) {
   finish_row<BITS, BF>(p, sel, h, r, x, row_consts<BF>(p, sel, r), row, red);
 }
 
+// The same per-row work with one warp per row (prefill: many rows, no
+// block barriers).  Lane l holds elements l + 32 k (k < E = D / 32): the
+// norm's sum of squares and each group's min / max are warp shuffles (a
+// group is gs / 32 of the lane's elements), RoPE reads the pair partner
+// from the warp's row in shared memory, and a packed word's lanes OR their
+// codes together by shuffles.
+template <int BITS, bool BF, int E>
+__global__ void __launch_bounds__(256) proj_epilogue_warp_kernel(const PP p) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float rows[8][32 * E];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t job = (int64_t)blockIdx.x * 8 + warp;  // (r, sel, h), h fastest
+  const int units = 2 * p.Hkv;
+  if (job >= (int64_t)p.R * units) return;
+  const int r = (int)(job / units), sh = (int)(job - (int64_t)r * units);
+  const int sel = sh / p.Hkv, h = sh - sel * p.Hkv;
+  const int D = p.D;
+  const int b = r / p.L, l = r - b * p.L;
+  const int src = (sel == 1 && p.v_from_k) ? 0 : sel;
+  float x[E];
+  const float* part = p.part + (((int64_t)src * p.Hkv + h) * p.ns * p.R + r) * D;
+#pragma unroll
+  for (int k = 0; k < E; k++) x[k] = 0.0f;
+  for (int s2 = 0; s2 < p.ns; s2++) {  // every element's load of a split in flight together
+    float v[E];
+#pragma unroll
+    for (int k = 0; k < E; k++) v[k] = part[(int64_t)s2 * p.R * D + lane + 32 * k];
+#pragma unroll
+    for (int k = 0; k < E; k++) x[k] += v[k];
+  }
+#pragma unroll
+  for (int k = 0; k < E; k++) x[k] = round_dt<BF>(x[k]);  // the projection's output, in the dtype
+  if (p.norms & (1 << sel)) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < E; k++) ss += x[k] * x[k];
+#pragma unroll
+    for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float n = 1.0f / sqrtf(ss / (float)D + p.eps);
+    const uint16_t* wn = sel ? p.v_norm : p.k_norm;
+#pragma unroll
+    for (int k = 0; k < E; k++) {
+      x[k] = round_dt<BF>(x[k] * n);
+      if (wn) x[k] = round_dt<BF>(x[k] * dt_to_f<BF>(wn[lane + 32 * k]));
+    }
+  }
+  if (sel == 0 && p.rope_dims > 0) {
+    const int half = p.rope_dims / 2;
+    float* row = rows[warp];
+#pragma unroll
+    for (int k = 0; k < E; k++) {
+      const int e = lane + 32 * k;
+      if (p.rope_pre != 0.0f && e < p.rope_dims) x[k] = round_dt<BF>(x[k] * round_dt<BF>(p.rope_pre));
+      row[e] = x[k];
+    }
+    __syncwarp();
+    const float pos = p.rope_scale * (float)(p.pos0 + l);
+#pragma unroll
+    for (int k = 0; k < E; k++) {
+      const int e = lane + 32 * k;
+      if (e < 2 * half) {
+        const int i = p.rope_trad ? e >> 1 : (e < half ? e : e - half);
+        const int e1 = p.rope_trad ? 2 * i : i, e2 = p.rope_trad ? 2 * i + 1 : i + half;
+        const float inv = p.rope_freqs ? 1.0f / p.rope_freqs[i]
+                                       : exp2f(-((float)i / (float)half) * p.rope_base);
+        float sn, cs;
+        sincosf(pos * inv, &sn, &cs);
+        const float x1 = row[e1], x2 = row[e2];
+        x[k] = round_dt<BF>(e == e1 ? x1 * cs - x2 * sn : x1 * sn + x2 * cs);
+      }
+    }
+  }
+  uint16_t* dbg = sel ? p.v_out : p.k_out;
+  if (dbg) {
+    uint16_t* drow = dbg + (((int64_t)b * p.Hkv + h) * p.L + l) * D;
+#pragma unroll
+    for (int k = 0; k < E; k++) drow[lane + 32 * k] = f_to_dt<BF>(x[k]);
+  }
+  // quantize: group j = lane elements k in [j * kpg, (j + 1) * kpg)
+  constexpr int PER = 32 / BITS;
+  constexpr float NB = (float)((1 << BITS) - 1);
+  const int gs = p.gs, kpg = gs / 32, groups = D / gs;
+  const TripleView& dv = sel ? p.dv : p.dk;
+  const int64_t drow = b * dv.batch_stride + h * dv.head_stride + p.dst_row0 + l;
+#pragma unroll
+  for (int k0 = 0; k0 < E; k0 += 1) {
+    if (k0 % kpg) continue;
+    float mn = x[k0], mx = x[k0];
+#pragma unroll
+    for (int k = 1; k < 4; k++)
+      if (k < kpg && k0 + k < E) {
+        mn = fminf(mn, x[k0 + k]);
+        mx = fmaxf(mx, x[k0 + k]);
+      }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    }
+    float scale, bias;
+    quant_params(mn, mx, NB, scale, bias);
+    const int grp = k0 / kpg;
+    if (lane == 0) {
+      dv.scales[drow * groups + grp] = f_to_dt<BF>(scale);
+      dv.biases[drow * groups + grp] = f_to_dt<BF>(bias);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      if (k < kpg && k0 + k < E) {
+        uint32_t word = quant_code(x[k0 + k], scale, bias, NB) << (BITS * (lane % PER));
+#pragma unroll
+        for (int off = 1; off < PER; off <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, off);
+        if (lane % PER == 0) dv.packed[drow * (D / PER) + (lane + 32 * (k0 + k)) / PER] = word;
+      }
+  }
+}
+
 // Decode-sized steps (R <= 4 rows): one launch.  A cluster of CS CTAs per
 // (K|V, kv head, row chunk) splits the hidden dimension; thread o owns
 // output column o.  Each thread first issues everything it will read —
@@ -496,6 +615,240 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
   }
 }
 
+// Prefill-sized steps (more than 4 token rows): the projection on tensor
+// cores, mma.sync m16n8k16 with f32 accumulation, then proj_epilogue_kernel.
+// The GEMM is W x^T: M = the output features of K (and V) — all kv heads'
+// rows, 128 per CTA — N = the token rows, 64 per CTA, K = hidden.  As in
+// the decode attention's Q K^T, the codes enter the MMA exactly: a pair of
+// codes as fp16 subnormals (units of 2^-24; one shift and mask per
+// register for 4-bit, one byte permute for 8-bit), x as fp16 (exact for
+// fp16 inputs and for bf16 inputs inside fp16's range), and per weight
+// group
+//   out += (s * 2^24) * sum(code * x 2^-24) + b * sum(x)
+// between k-steps.  The k order inside a 16-element k-step is permuted so
+// that each A register comes from one packed word: 4-bit lane t takes the
+// nibble pair (t, t+4) of the step's two words; 8-bit lane t takes word t
+// (its bytes (0, 1) and (2, 3)).  proj_xprep_kernel writes x once in that
+// order as fp16, [group][k-step][token][16 halves], with sum(x) per
+// (group, token); the GEMM then streams weights and inputs group by group
+// through a kStages-deep cp.async ring (16-byte copies, zero-filled past
+// the last row / token), so each lane reads its B fragment with one 8-byte
+// shared load and its A words with one (4-bit) or two (8-bit).
+constexpr int kMT = 128;    // output rows per CTA
+constexpr int kNT = 64;     // token rows per CTA
+constexpr int kStages = 4;  // cp.async ring depth, in weight groups
+
+struct MmaGeo {
+  int gs, wbits;
+  __host__ __device__ constexpr MmaGeo(int g, int w) : gs(g), wbits(w) {}
+  __host__ __device__ constexpr int row_bytes() const { return gs * wbits / 8; }   // codes of a row's group
+  __host__ __device__ constexpr int row_pitch() const { return row_bytes() + 16; }  // padded: no bank conflicts
+  __host__ __device__ constexpr int ksteps() const { return gs / 16; }
+  __host__ __device__ constexpr int w_bytes() const { return kMT * row_pitch(); }
+  __host__ __device__ constexpr int x_bytes() const { return ksteps() * kNT * 32; }
+  __host__ __device__ constexpr int stage_bytes() const { return w_bytes() + x_bytes() + kNT * 4 + 2 * kMT * 4; }
+};
+
+// x [R, hidden] (dtype) -> xp [G][ksteps][R][16 halves] fp16 in the MMA's k
+// order, and xsum [G][R] = sum(x) of each group.  Thread: 8 consecutive
+// elements of one token (one 16-byte load).
+template <int WBITS, bool BF>
+__global__ void __launch_bounds__(256) proj_xprep_kernel(const PP p, uint8_t* xp, float* xsum) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int gs = p.wk.gs, G = p.hidden / gs, cpg = gs / 8;  // 16-byte chunks per group
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)p.R * (p.hidden / 8);
+  const bool live = i < total;
+  const int64_t ii = live ? i : 0;
+  const int n = (int)(ii / (p.hidden / 8)), ch = (int)(ii - (int64_t)n * (p.hidden / 8));
+  const int grp = ch / cpg, c = ch - grp * cpg;
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)n * p.hidden) + ch);
+  const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+  float v[8], part = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    v[j] = dt_to_f<BF>((uint16_t)((j & 1) ? (wv[j / 2] >> 16) : (wv[j / 2] & 0xffffu)));
+    part += v[j];
+  }
+  // the cpg lanes of one (token, group) are consecutive and aligned
+  for (int off = 1; off < cpg; off <<= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+  if (!live) return;
+  if (c == 0) xsum[(int64_t)grp * ((p.R + 3) & ~3) + n] = part;
+  const int s16 = c / 2, which = c & 1;  // k-step, first / second 8 elements of it
+  uint8_t* dst = xp + (((int64_t)grp * (gs / 16) + s16) * p.R + n) * 32;
+  if (WBITS == 4) {
+    // lane t's halves: (x[t], x[t+4]) of the step's word `which`
+#pragma unroll
+    for (int tt = 0; tt < 4; tt++)
+      *reinterpret_cast<uint32_t*>(dst + tt * 8 + which * 4) = pack_h2(v[tt], v[tt + 4]);
+  } else {
+    uint4 o;
+    o.x = pack_h2(v[0], v[1]);
+    o.y = pack_h2(v[2], v[3]);
+    o.z = pack_h2(v[4], v[5]);
+    o.w = pack_h2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(dst + which * 16) = o;
+  }
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool full) {
+  const uint32_t d = attn::smem_u32(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src),
+               "r"(full ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int WBITS, bool BF, int GS>
+__global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, int sely, const uint8_t* xp,
+                                                          const float* xsum) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  extern __shared__ __align__(16) uint8_t smraw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int wm = warp & 3, wn = warp >> 2;  // 4 x 2 warps: 32 rows x 32 tokens each
+  const int HD = p.Hkv * p.D, M = sely * HD;
+  const int m0 = blockIdx.x * kMT, n0 = blockIdx.y * kNT;
+  constexpr int gs = GS;
+  const int G = p.hidden / gs;
+  constexpr MmaGeo geo{GS, WBITS};
+  constexpr int RB = geo.row_bytes(), RP = geo.row_pitch(), KS = geo.ksteps();
+  const int64_t row_stride = (int64_t)p.hidden * WBITS / 8;  // bytes per weight row
+  auto stage = [&](int b) -> uint8_t* { return smraw + (size_t)b * geo.stage_bytes(); };
+  // copies of one group into stage b (every thread commits one cp.async group)
+  auto issue = [&](int grp, int b) {
+    if (grp < G) {
+      uint8_t* st = stage(b);
+      const int nw = kMT * (RB / 16);
+      for (int i = tid; i < nw; i += 256) {
+        const int row = i / (RB / 16), c = i - row * (RB / 16);
+        const int m = m0 + row;
+        const bool ok = m < M;
+        const int mm = ok ? m : 0;
+        const W& w = mm < HD ? p.wk : p.wv;
+        const int64_t wr = mm < HD ? mm : mm - HD;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(w.packed) + wr * row_stride +
+                             (int64_t)grp * RB + c * 16;
+        cp_async16(st + row * RP + c * 16, src, ok);
+      }
+      uint8_t* sx = st + geo.w_bytes();
+      const int nx = KS * kNT * 2;  // 16-byte pieces: 2 per (k-step, token)
+      for (int i = tid; i < nx; i += 256) {
+        const int s16 = i / (kNT * 2), rem = i - s16 * kNT * 2, n = rem >> 1, half = rem & 1;
+        const bool ok = n0 + n < p.R;
+        const uint8_t* src = xp + (((int64_t)grp * KS + s16) * p.R + (ok ? n0 + n : 0)) * 32 + half * 16;
+        cp_async16(sx + ((size_t)s16 * kNT + n) * 32 + half * 16, src, ok);
+      }
+      float* ssx = reinterpret_cast<float*>(sx + geo.x_bytes());
+      if (tid < kNT / 4) {
+        const int n = tid * 4;  // 4 tokens per copy; rows padded to a multiple of 4
+        const int Rp = (p.R + 3) & ~3;
+        const bool ok = n0 + n < Rp;
+        cp_async16(ssx + n, xsum + (int64_t)grp * Rp + (ok ? n0 + n : 0), ok);
+      }
+    }
+    cp_async_commit();
+  };
+  float acc[2][4][4], out[2][4][4];
+#pragma unroll
+  for (int a = 0; a < 2; a++)
+#pragma unroll
+    for (int b = 0; b < 4; b++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) acc[a][b][c] = out[a][b][c] = 0.0f;
+  // scale (thread < kMT) or bias (thread >= kMT) of one row, one group ahead
+  const int srow = tid & (kMT - 1), sm_ = m0 + srow;
+  auto fetch_sb = [&](int grp) -> float {
+    if (grp >= G || sm_ >= M) return 0.0f;
+    const W& w = sm_ < HD ? p.wk : p.wv;
+    const int64_t wr = sm_ < HD ? sm_ : sm_ - HD;
+    const uint16_t* src = tid < kMT ? w.scales : w.biases;
+    return src ? dt_to_f<BF>(__ldg(src + wr * G + grp)) : 0.0f;
+  };
+  float sb_next = fetch_sb(0);
+#pragma unroll
+  for (int s = 0; s < kStages - 1; s++) issue(s, s);
+  for (int grp = 0; grp < G; grp++) {
+    const int b = grp % kStages;
+    uint8_t* st = stage(b);
+    float* ssb = reinterpret_cast<float*>(st + geo.w_bytes() + geo.x_bytes() + kNT * 4);
+    ssb[tid] = tid < kMT ? sb_next * 16777216.0f : sb_next;  // scales in the codes' 2^-24 unit
+    sb_next = fetch_sb(grp + 1);
+    cp_async_wait<kStages - 2>();
+    __syncthreads();
+    issue(grp + kStages - 1, (grp + kStages - 1) % kStages);
+    const uint8_t* sw = st;
+    const uint8_t* sx = st + geo.w_bytes();
+    const float* ssx = reinterpret_cast<const float*>(sx + geo.x_bytes());
+#pragma unroll
+    for (int s16 = 0; s16 < KS; s16++) {
+      uint32_t a[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; mt++) {
+        const int r0 = wm * 32 + mt * 16 + g;
+        if (WBITS == 4) {
+          const uint2 wa = *reinterpret_cast<const uint2*>(sw + r0 * RP + s16 * 8);
+          const uint2 wb = *reinterpret_cast<const uint2*>(sw + (r0 + 8) * RP + s16 * 8);
+          a[mt][0] = (wa.x >> (4 * t)) & 0x000F000Fu;
+          a[mt][1] = (wb.x >> (4 * t)) & 0x000F000Fu;
+          a[mt][2] = (wa.y >> (4 * t)) & 0x000F000Fu;
+          a[mt][3] = (wb.y >> (4 * t)) & 0x000F000Fu;
+        } else {
+          const uint32_t wa = *reinterpret_cast<const uint32_t*>(sw + r0 * RP + s16 * 16 + 4 * t);
+          const uint32_t wb = *reinterpret_cast<const uint32_t*>(sw + (r0 + 8) * RP + s16 * 16 + 4 * t);
+          a[mt][0] = attn::prmt(wa, 0u, 0x4140u);
+          a[mt][1] = attn::prmt(wb, 0u, 0x4140u);
+          a[mt][2] = attn::prmt(wa, 0u, 0x4342u);
+          a[mt][3] = attn::prmt(wb, 0u, 0x4342u);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; nt++) {
+        const int n = wn * 32 + nt * 8 + g;
+        const uint2 bf = *reinterpret_cast<const uint2*>(sx + ((size_t)s16 * kNT + n) * 32 + t * 8);
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++) attn::mma16816(acc[mt][nt], a[mt], bf.x, bf.y);
+      }
+    }
+    // the group's scale and bias, then a fresh dot product
+#pragma unroll
+    for (int mt = 0; mt < 2; mt++) {
+      const int r0 = wm * 32 + mt * 16 + g;
+      const float s0 = ssb[r0], s1 = ssb[r0 + 8], b0 = ssb[kMT + r0], b1 = ssb[kMT + r0 + 8];
+#pragma unroll
+      for (int nt = 0; nt < 4; nt++) {
+        const int n = wn * 32 + nt * 8 + 2 * t;
+        const float x0 = ssx[n], x1 = ssx[n + 1];
+        out[mt][nt][0] = fmaf(s0, acc[mt][nt][0], fmaf(b0, x0, out[mt][nt][0]));
+        out[mt][nt][1] = fmaf(s0, acc[mt][nt][1], fmaf(b0, x1, out[mt][nt][1]));
+        out[mt][nt][2] = fmaf(s1, acc[mt][nt][2], fmaf(b1, x0, out[mt][nt][2]));
+        out[mt][nt][3] = fmaf(s1, acc[mt][nt][3], fmaf(b1, x1, out[mt][nt][3]));
+        acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  // the projection rows, f32, in the epilogue's layout part[sel][h][0][r][d]
+#pragma unroll
+  for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      const int m = m0 + wm * 32 + mt * 16 + g + 8 * hh;
+      if (m >= M) continue;
+      const int sel = m / HD, rem = m - sel * HD, h = rem / p.D, d = rem - h * p.D;
+      float* dst = p.part + ((int64_t)(sel * p.Hkv + h) * p.R) * p.D + d;
+#pragma unroll
+      for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int r = n0 + wn * 32 + nt * 8 + 2 * t + e;
+          if (r < p.R) dst[(int64_t)r * p.D] = out[mt][nt][2 * hh + e];
+        }
+    }
+}
+
 // rows per projection CTA: one decode row, a small batch, or 16-row chunks
 inline int proj_rows(int R) { return R <= 1 ? 1 : R <= 4 ? 4 : 16; }
 
@@ -610,7 +963,35 @@ size_t project_workspace_bytes(const ProjArgs& a, int Hkv, int D, int* splits) {
   int ns = (2 * sms + heads * nrc - 1) / (heads * nrc);
   ns = std::max(1, std::min(ns, std::min(G, a.v_from_k ? G : a.hidden / a.wv.gs)));
   if (splits) *splits = ns;
-  return attn::kPartialOff + (size_t)2 * Hkv * ns * R * D * sizeof(float);
+  // partials (split path; one split on the tensor-core path), then the
+  // tensor-core path's fp16 inputs and their group sums
+  const size_t part = ((size_t)2 * Hkv * ns * R * D * sizeof(float) + 255) / 256 * 256;
+  const size_t xp = ((size_t)R * a.hidden * 2 + 255) / 256 * 256;
+  const size_t xs = (size_t)G * ((R + 3) & ~3) * sizeof(float);
+  return attn::kPartialOff + part + xp + xs;
+}
+
+// proj_epilogue_warp_kernel over every (row, K|V, kv head): 8 rows per CTA.
+template <int BITS, bool BF>
+static int32_t launch_epilogue_warp_b(const PP& p, cudaStream_t st) {
+  const int64_t jobs = (int64_t)p.R * 2 * p.Hkv;
+  const dim3 grid((unsigned)((jobs + 7) / 8));
+  switch (p.D / 32) {
+    case 1: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 1>, grid, dim3(256), 0, st, p)); break;
+    case 2: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 2>, grid, dim3(256), 0, st, p)); break;
+    case 3: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 3>, grid, dim3(256), 0, st, p)); break;
+    case 4: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 4>, grid, dim3(256), 0, st, p)); break;
+    case 5: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 5>, grid, dim3(256), 0, st, p)); break;
+    case 6: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 6>, grid, dim3(256), 0, st, p)); break;
+    case 7: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 7>, grid, dim3(256), 0, st, p)); break;
+    default: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 8>, grid, dim3(256), 0, st, p)); break;
+  }
+  return KVQ_OK;
+}
+
+static int32_t launch_epilogue_warp(const PP& p, int bits, bool bf, cudaStream_t st) {
+  if (bits == 4) return bf ? launch_epilogue_warp_b<4, true>(p, st) : launch_epilogue_warp_b<4, false>(p, st);
+  return bf ? launch_epilogue_warp_b<8, true>(p, st) : launch_epilogue_warp_b<8, false>(p, st);
 }
 
 int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, TripleView dk,
@@ -684,6 +1065,55 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
       case 2: return launch_cluster_dt<8, 4>(p, bf, cs, RC, sely, smem, st);
       default: return launch_cluster_dt<8, 8>(p, bf, cs, RC, sely, smem, st);
     }
+  }
+  // prefill-sized: the tensor-core projection when both projections share
+  // a group size and x is 16-byte aligned, then the epilogue
+  const bool mma_ok = (a.v_from_k || a.wv.gs == a.wk.gs) &&
+                      reinterpret_cast<uintptr_t>(a.x) % 16 == 0;
+  if (mma_ok) {
+    const int sely = a.v_from_k ? 1 : 2;
+    uint8_t* wsb = static_cast<uint8_t*>(ws);
+    const size_t part_bytes = ((size_t)2 * Hkv * ns * p.R * D * sizeof(float) + 255) / 256 * 256;
+    uint8_t* xp = wsb + attn::kPartialOff + part_bytes;
+    float* xsum = reinterpret_cast<float*>(xp + ((size_t)p.R * a.hidden * 2 + 255) / 256 * 256);
+    p.ns = 1;
+    const MmaGeo geo{a.wk.gs, a.wk.bits};
+    const int smem = kStages * geo.stage_bytes();
+    int dev = 0;
+    KVQ_CUDA_TRY(cudaGetDevice(&dev));
+    const int64_t nchunks = (int64_t)p.R * (a.hidden / 8);
+    const dim3 gx((unsigned)((nchunks + 255) / 256));
+    auto xk = [&](auto kern) -> int32_t {
+      KVQ_CUDA_TRY(launch_pdl(kern, gx, dim3(256), 0, st, p, xp, xsum));
+      return KVQ_OK;
+    };
+    rc = a.wk.bits == 4 ? (bf ? xk(proj_xprep_kernel<4, true>) : xk(proj_xprep_kernel<4, false>))
+                        : (bf ? xk(proj_xprep_kernel<8, true>) : xk(proj_xprep_kernel<8, false>));
+    if (rc) return rc;
+    const dim3 gm((sely * Hkv * D + kMT - 1) / kMT, (p.R + kNT - 1) / kNT);
+    auto mk = [&](auto kern) -> int32_t {
+      int32_t r2 = kernel_setup(reinterpret_cast<const void*>(kern), 256, smem, dev, nullptr);
+      if (r2) return r2;
+      KVQ_CUDA_TRY(launch_pdl(kern, gm, dim3(256), (size_t)smem, st, p, sely,
+                              static_cast<const uint8_t*>(xp), static_cast<const float*>(xsum)));
+      return KVQ_OK;
+    };
+    switch ((a.wk.bits == 8 ? 6 : 0) + (bf ? 3 : 0) + (a.wk.gs == 32 ? 0 : a.wk.gs == 64 ? 1 : 2)) {
+      case 0: rc = mk(proj_mma_kernel<4, false, 32>); break;
+      case 1: rc = mk(proj_mma_kernel<4, false, 64>); break;
+      case 2: rc = mk(proj_mma_kernel<4, false, 128>); break;
+      case 3: rc = mk(proj_mma_kernel<4, true, 32>); break;
+      case 4: rc = mk(proj_mma_kernel<4, true, 64>); break;
+      case 5: rc = mk(proj_mma_kernel<4, true, 128>); break;
+      case 6: rc = mk(proj_mma_kernel<8, false, 32>); break;
+      case 7: rc = mk(proj_mma_kernel<8, false, 64>); break;
+      case 8: rc = mk(proj_mma_kernel<8, false, 128>); break;
+      case 9: rc = mk(proj_mma_kernel<8, true, 32>); break;
+      case 10: rc = mk(proj_mma_kernel<8, true, 64>); break;
+      default: rc = mk(proj_mma_kernel<8, true, 128>); break;
+    }
+    if (rc) return rc;
+    return launch_epilogue_warp(p, g.bits, bf, st);
   }
   const dim3 g1(ns, 2 * Hkv, (p.R + proj_rows(p.R) - 1) / proj_rows(p.R));
   const int RC = proj_rows(p.R);

@@ -11,9 +11,10 @@
 * Projection parity: random inputs and oracle-quantized weights (4 / 8
   bit, group 32 / 64 / 128, with biases), K RMSNorm with weight, V RMSNorm
   without (gemma4.ts:174-177), default / proportional / partial-traditional
-  RoPE, attention_k_eq_v, fp16 and bf16, batch 1 / 4 / 2 / 1 with 1 / 1 /
-  37 / 20 rows (the one-launch cluster path at 1 and 4 rows, the split
-  projection + epilogue pair at 16-row tiles): the rows before
+  RoPE, attention_k_eq_v, fp16 and bf16, batch 1 / 4 / 2 / 1 / 1 / 3 with
+  1 / 1 / 37 / 20 / 300 / 70 rows (the one-launch cluster path at 1 and 4
+  rows; the tensor-core projection + epilogue pair beyond, with partial
+  128-row and 64-token tiles): the rows before
   quantisation match the oracle's project_kv within 3 dtype ulps of the
   row's largest element (the product sums in f32, the oracle in f64), at
   least 90 % of them exactly; the cache rows are bit-exact with the oracle's
@@ -145,6 +146,8 @@ CASES = [
     (BF16, 4, 64, 8, 32, 4, 1, 4, 128, 1024, True, "proportional"),
     (F16, 8, 32, 8, 64, 2, 37, 2, 128, 512, False, "default"),
     (BF16, 8, 128, 4, 128, 1, 20, 2, 256, 1024, False, "partial-traditional"),
+    (BF16, 4, 64, 4, 64, 1, 300, 4, 128, 1024, False, "default"),
+    (F16, 4, 32, 8, 32, 3, 70, 2, 64, 2048, True, "proportional"),
 ]
 
 
