@@ -39,6 +39,8 @@
 
 #include <algorithm>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "kvq_attn_impl.cuh"
 #include "kvq_qrule.cuh"
@@ -621,8 +623,9 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
 // rows, 128 per CTA — N = the token rows, 64 per CTA, K = hidden.  As in
 // the decode attention's Q K^T, the codes enter the MMA exactly: a pair of
 // codes as fp16 subnormals (units of 2^-24; one shift and mask per
-// register for 4-bit, one byte permute for 8-bit), x as fp16 (exact for
-// fp16 inputs and for bf16 inputs inside fp16's range), and per weight
+// register for 4-bit, one byte permute for 8-bit), x as fp16 (exact: bf16
+// inputs are first scaled per (group, token) block by a power of two into
+// fp16's range, and the factor comes back at the fold), and per weight
 // group
 //   out += (s * 2^24) * sum(code * x 2^-24) + b * sum(x)
 // between k-steps.  The k order inside a 16-element k-step is permuted so
@@ -646,14 +649,15 @@ struct MmaGeo {
   __host__ __device__ constexpr int ksteps() const { return gs / 16; }
   __host__ __device__ constexpr int w_bytes() const { return kMT * row_pitch(); }
   __host__ __device__ constexpr int x_bytes() const { return ksteps() * kNT * 32; }
-  __host__ __device__ constexpr int stage_bytes() const { return w_bytes() + x_bytes() + kNT * 4 + 2 * kMT * 4; }
+  __host__ __device__ constexpr int stage_bytes() const { return w_bytes() + x_bytes() + 2 * kNT * 4 + 2 * kMT * 4; }
 };
 
 // x [R, hidden] (dtype) -> xp [G][ksteps][R][16 halves] fp16 in the MMA's k
 // order, and xsum [G][R] = sum(x) of each group.  Thread: 8 consecutive
 // elements of one token (one 16-byte load).
 template <int WBITS, bool BF>
-__global__ void __launch_bounds__(256) proj_xprep_kernel(const PP p, uint8_t* xp, float* xsum) {
+__global__ void __launch_bounds__(256) proj_xprep_kernel(const PP p, uint8_t* xp, float* xsum,
+                                                         float* xfac) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int gs = p.wk.gs, G = p.hidden / gs, cpg = gs / 8;  // 16-byte chunks per group
@@ -673,8 +677,31 @@ __global__ void __launch_bounds__(256) proj_xprep_kernel(const PP p, uint8_t* xp
   }
   // the cpg lanes of one (token, group) are consecutive and aligned
   for (int off = 1; off < cpg; off <<= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+  // bf16 inputs: the block's values times a power of two 2^-e that brings
+  // its largest magnitude into [2^14, 2^15) — exact, inside fp16's range
+  // whatever the bf16 exponents; the GEMM multiplies the block's dot
+  // products by 2^e again
+  float fac = 1.0f;
+  if (BF) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
+    for (int off = 1; off < cpg; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (amax > 0.0f) {
+      int e = ((__float_as_uint(amax) >> 23) & 0xff) - 127 - 14;  // amax in [2^(e+14), 2^(e+15))
+      e = max(-126, min(126, e));
+      fac = __uint_as_float((uint32_t)(127 + e) << 23);
+      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[j] *= inv;
+    }
+  }
   if (!live) return;
-  if (c == 0) xsum[(int64_t)grp * ((p.R + 3) & ~3) + n] = part;
+  const int64_t xi = (int64_t)grp * ((p.R + 3) & ~3) + n;
+  if (c == 0) {
+    xsum[xi] = part;
+    if (BF) xfac[xi] = fac;
+  }
   const int s16 = c / 2, which = c & 1;  // k-step, first / second 8 elements of it
   uint8_t* dst = xp + (((int64_t)grp * (gs / 16) + s16) * p.R + n) * 32;
   if (WBITS == 4) {
@@ -703,7 +730,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 template <int WBITS, bool BF, int GS>
 __global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, int sely, const uint8_t* xp,
-                                                          const float* xsum) {
+                                                          const float* xsum, const float* xfac) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ __align__(16) uint8_t smraw[];
@@ -741,12 +768,13 @@ __global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, int sely, 
         const uint8_t* src = xp + (((int64_t)grp * KS + s16) * p.R + (ok ? n0 + n : 0)) * 32 + half * 16;
         cp_async16(sx + ((size_t)s16 * kNT + n) * 32 + half * 16, src, ok);
       }
-      float* ssx = reinterpret_cast<float*>(sx + geo.x_bytes());
-      if (tid < kNT / 4) {
-        const int n = tid * 4;  // 4 tokens per copy; rows padded to a multiple of 4
-        const int Rp = (p.R + 3) & ~3;
+      float* ssx = reinterpret_cast<float*>(sx + geo.x_bytes());  // sum(x) [kNT], then 2^e [kNT]
+      if (tid < (BF ? 2 : 1) * kNT / 4) {
+        const int which = tid / (kNT / 4), n = (tid % (kNT / 4)) * 4;  // 4 tokens per copy
+        const int Rp = (p.R + 3) & ~3;  // rows padded to a multiple of 4
         const bool ok = n0 + n < Rp;
-        cp_async16(ssx + n, xsum + (int64_t)grp * Rp + (ok ? n0 + n : 0), ok);
+        const float* src = which ? xfac : xsum;
+        cp_async16(ssx + which * kNT + n, src + (int64_t)grp * Rp + (ok ? n0 + n : 0), ok);
       }
     }
     cp_async_commit();
@@ -773,7 +801,7 @@ __global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, int sely, 
   for (int grp = 0; grp < G; grp++) {
     const int b = grp % kStages;
     uint8_t* st = stage(b);
-    float* ssb = reinterpret_cast<float*>(st + geo.w_bytes() + geo.x_bytes() + kNT * 4);
+    float* ssb = reinterpret_cast<float*>(st + geo.w_bytes() + geo.x_bytes() + 2 * kNT * 4);
     ssb[tid] = tid < kMT ? sb_next * 16777216.0f : sb_next;  // scales in the codes' 2^-24 unit
     sb_next = fetch_sb(grp + 1);
     cp_async_wait<kStages - 2>();
@@ -821,6 +849,13 @@ __global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, int sely, 
       for (int nt = 0; nt < 4; nt++) {
         const int n = wn * 32 + nt * 8 + 2 * t;
         const float x0 = ssx[n], x1 = ssx[n + 1];
+        if (BF) {  // the token blocks' power-of-two input scales back
+          const float f0 = ssx[kNT + n], f1 = ssx[kNT + n + 1];
+          acc[mt][nt][0] *= f0;
+          acc[mt][nt][1] *= f1;
+          acc[mt][nt][2] *= f0;
+          acc[mt][nt][3] *= f1;
+        }
         out[mt][nt][0] = fmaf(s0, acc[mt][nt][0], fmaf(b0, x0, out[mt][nt][0]));
         out[mt][nt][1] = fmaf(s0, acc[mt][nt][1], fmaf(b0, x1, out[mt][nt][1]));
         out[mt][nt][2] = fmaf(s1, acc[mt][nt][2], fmaf(b1, x0, out[mt][nt][2]));
@@ -895,6 +930,20 @@ static int cluster_size(int dev) {
   return cs;
 }
 
+// Opt `kern` in to 16-CTA clusters on the current device, once per
+// (kernel, device): the attribute is per device.
+static int32_t allow_wide_clusters(const void* kern) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  KVQ_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({kern, dev})) return KVQ_OK;
+  KVQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  done.insert({kern, dev});
+  return KVQ_OK;
+}
+
 // The one-launch cluster path: a few rows, every CTA's slice of the hidden
 // dimension within kMaxG groups, its inputs within 48 KB of shared memory.
 static bool use_cluster(const ProjArgs& a, int cs) {
@@ -925,8 +974,8 @@ static int32_t launch_cluster(const PP& p, int RC, int sely, size_t smem, cudaSt
   auto k1 = proj_cluster_kernel<WBITS, BITS, BF, 1, CS>;
   auto k4 = proj_cluster_kernel<WBITS, BITS, BF, 4, CS>;
   if (CS > 8) {
-    KVQ_CUDA_TRY(cudaFuncSetAttribute(RC == 1 ? k1 : k4,
-                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    int32_t rc = allow_wide_clusters(reinterpret_cast<const void*>(RC == 1 ? k1 : k4));
+    if (rc) return rc;
   }
   KVQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, RC == 1 ? k1 : k4, p));
   return KVQ_OK;
@@ -968,7 +1017,7 @@ size_t project_workspace_bytes(const ProjArgs& a, int Hkv, int D, int* splits) {
   const size_t part = ((size_t)2 * Hkv * ns * R * D * sizeof(float) + 255) / 256 * 256;
   const size_t xp = ((size_t)R * a.hidden * 2 + 255) / 256 * 256;
   const size_t xs = (size_t)G * ((R + 3) & ~3) * sizeof(float);
-  return attn::kPartialOff + part + xp + xs;
+  return attn::kPartialOff + part + xp + 2 * xs;  // sums, then the bf16 block scales
 }
 
 // proj_epilogue_warp_kernel over every (row, K|V, kv head): 8 rows per CTA.
@@ -1076,6 +1125,7 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
     const size_t part_bytes = ((size_t)2 * Hkv * ns * p.R * D * sizeof(float) + 255) / 256 * 256;
     uint8_t* xp = wsb + attn::kPartialOff + part_bytes;
     float* xsum = reinterpret_cast<float*>(xp + ((size_t)p.R * a.hidden * 2 + 255) / 256 * 256);
+    float* xfac = xsum + (size_t)(a.hidden / a.wk.gs) * ((p.R + 3) & ~3);
     p.ns = 1;
     const MmaGeo geo{a.wk.gs, a.wk.bits};
     const int smem = kStages * geo.stage_bytes();
@@ -1084,7 +1134,7 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
     const int64_t nchunks = (int64_t)p.R * (a.hidden / 8);
     const dim3 gx((unsigned)((nchunks + 255) / 256));
     auto xk = [&](auto kern) -> int32_t {
-      KVQ_CUDA_TRY(launch_pdl(kern, gx, dim3(256), 0, st, p, xp, xsum));
+      KVQ_CUDA_TRY(launch_pdl(kern, gx, dim3(256), 0, st, p, xp, xsum, xfac));
       return KVQ_OK;
     };
     rc = a.wk.bits == 4 ? (bf ? xk(proj_xprep_kernel<4, true>) : xk(proj_xprep_kernel<4, false>))
@@ -1095,7 +1145,8 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
       int32_t r2 = kernel_setup(reinterpret_cast<const void*>(kern), 256, smem, dev, nullptr);
       if (r2) return r2;
       KVQ_CUDA_TRY(launch_pdl(kern, gm, dim3(256), (size_t)smem, st, p, sely,
-                              static_cast<const uint8_t*>(xp), static_cast<const float*>(xsum)));
+                              static_cast<const uint8_t*>(xp), static_cast<const float*>(xsum),
+                              static_cast<const float*>(xfac)));
       return KVQ_OK;
     };
     switch ((a.wk.bits == 8 ? 6 : 0) + (bf ? 3 : 0) + (a.wk.gs == 32 ? 0 : a.wk.gs == 64 ? 1 : 2)) {

@@ -21,6 +21,9 @@
   quantize of those rows, placed as the oracle cache places them; and a
   decode over the cache matches the oracle's attention (2e-3 fp16, 2/128
   bf16, the attention tests' bars).
+* bf16 inputs from 1e-6 to 3e5 in magnitude (beyond fp16's range) pass
+  the same bar on the tensor-core path (its exact per-block power-of-two
+  input scaling).
 * Rotating caches: prefill, in-place decode steps past the wrap and a
   chunked append through the temporal re-layout — RoPE positions follow
   the logical offset, the ring matches the oracle's bit for bit.
@@ -204,6 +207,34 @@ def test_fused_projection_matches_oracle(case):
     got = from_torch(o, dt)
     record_parity(f"decode after fused append {case[11]}", got, want, dt, f"<= {TOL[dt]}")
     assert max_abs(got, want, dt) <= TOL[dt]
+    cache.dispose()
+
+
+def test_bf16_inputs_far_outside_fp16_range():
+    """bf16 token rows from 1e-6 to 3e5 in magnitude (some beyond fp16's
+    65504) through the tensor-core prefill path: every row within the bar
+    of the oracle, nothing infinite."""
+    import torch
+    import kvq
+    dt, B, L, H, D, hidden = BF16, 1, 70, 2, 128, 512
+    rng = np.random.default_rng(77)
+    kq, k_or = make_qlinear(rng, H * D, hidden, 64, 4, dt)
+    vq, v_or = make_qlinear(rng, H * D, hidden, 64, 4, dt)
+    spec = dict(head_dim=D, k_proj=k_or, v_proj=v_or, k_norm=True, k_norm_weight=None,
+                v_norm=False, eps=1e-6, rope_dims=D, rope_base=10000.0)
+    proj = kvq.KvProjection(kq, vq, D, v_norm=False, rope_dims=D, rope_base=10000.0)
+    mag = 10.0 ** rng.uniform(-6, 5, (B, L, 1))
+    mag[0, :4, 0] = [1e5, 3e5, 1e-6, 7e4]
+    x = O.to_dtype_bits((rng.uniform(-1, 1, (B, L, hidden)) * mag).astype(np.float32), dt)
+    cache = kvq.QuantizedKVCache(64, 4)
+    k_out = torch.empty(B, H, L, D, dtype=torch.bfloat16, device="cuda")
+    v_out = torch.empty_like(k_out)
+    cache.update_and_fetch_projected(_dev_bits(x, dt), proj, k_out=k_out, v_out=v_out)
+    torch.cuda.synchronize()
+    assert torch.isfinite(k_out.float()).all() and torch.isfinite(v_out.float()).all()
+    want_k, want_v = O.project_kv(O.from_dtype_bits(x, dt), spec, 0, dt)
+    check_rows(from_torch(k_out, dt), want_k, dt, "bf16 wide-range inputs K")
+    check_rows(from_torch(v_out, dt), want_v, dt, "bf16 wide-range inputs V")
     cache.dispose()
 
 
