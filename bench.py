@@ -938,7 +938,8 @@ def profile_run(args):
     kernel.  decode / append: 3 config-2 layers (227 MB, above L2), cycled;
     config5: the first 16 sequences of config 5, all 8 kv heads (315 MB);
     projection: one-token fused K/V projection appends through 24 layers of
-    Gemma-4-12B sliding-layer weights (213 MB), cycled."""
+    Gemma-4-12B sliding-layer weights (213 MB), cycled; projection-prefill:
+    512-token chunks through 2 such layers."""
     import numpy as np
     import torch
     import kvq
@@ -957,6 +958,19 @@ def profile_run(args):
         torch.cuda.synchronize()
         print(json.dumps({"profile": "projection", "launches": args.steps,
                           "algorithmic_bytes_per_launch": projection_bytes(c, 1)}))
+        return
+    if args.profile == "projection-prefill":
+        c = CFGP
+        layers = projection_layers(c, 2, device, g)
+        xc = torch.randn(1, c["chunk"], c["hidden"], generator=g, device=device).bfloat16()
+        for i in range(args.steps):
+            Ly = layers[i % 2]
+            Ly["cache"].update_and_fetch_projected(xc, Ly["proj"])
+            Ly["cache"].trim(c["chunk"])
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": "projection-prefill", "launches": args.steps,
+                          "flops_per_launch": 2 * c["chunk"] * c["hidden"] * 2 * c["Hkv"] *
+                          c["D"]}))
         return
     if args.profile == "config5":
         c = CFG5
@@ -1047,7 +1061,8 @@ def main():
                          "config 4 chunked prefill (kv8); prefill-kv4: the same shape in kv4; "
                          "config1 / config3: their own lines; kv-projection: the fused K/V "
                          "projection + append alone")
-    ap.add_argument("--profile", choices=["decode", "append", "config5", "projection"],
+    ap.add_argument("--profile", choices=["decode", "append", "config5", "projection",
+                                          "projection-prefill"],
                     default=None,
                     help="run only the named kernel on a small fixed workload, `--steps` "
                          "launches, no timing (for ncu captures)")
