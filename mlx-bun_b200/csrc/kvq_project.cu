@@ -286,25 +286,41 @@ __global__ void __launch_bounds__(256) proj_epilogue_kernel(const PP p) {
   finish_row<BITS, BF>(p, sel, h, r, x, row_consts<BF>(p, sel, r), row, red);
 }
 
-// The same per-row work with one warp per row (prefill: many rows, no
-// block barriers).  Lane l holds elements l + 32 k (k < E = D / 32): the
-// norm's sum of squares and each group's min / max are warp shuffles (a
-// group is gs / 32 of the lane's elements), RoPE reads the pair partner
-// from the warp's row in shared memory, and a packed word's lanes OR their
-// codes together by shuffles.
+// The same per-row work with one warp per row (prefill: many rows).  One
+// CTA per token, one warp per (K | V, kv head): the CTA first computes the
+// token's RoPE rotations (cos, sin of each pair's angle) once into shared
+// memory — they are the same for every kv head — then each warp works on
+// its row with no block barrier.  Lane l holds elements l + 32 k (k < E =
+// D / 32): the norm's sum of squares and each group's min / max are warp
+// shuffles (a group is gs / 32 of the lane's elements), RoPE reads the
+// pair partner from the warp's row in shared memory, and a packed word's
+// lanes OR their codes together by shuffles.
 template <int BITS, bool BF, int E>
-__global__ void __launch_bounds__(256) proj_epilogue_warp_kernel(const PP p) {
+__global__ void __launch_bounds__(1024) proj_epilogue_warp_kernel(const PP p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __shared__ float rows[8][32 * E];
+  extern __shared__ float esm[];  // cos [D/2], sin [D/2], then one row of D per warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t job = (int64_t)blockIdx.x * 8 + warp;  // (r, sel, h), h fastest
-  const int units = 2 * p.Hkv;
-  if (job >= (int64_t)p.R * units) return;
-  const int r = (int)(job / units), sh = (int)(job - (int64_t)r * units);
-  const int sel = sh / p.Hkv, h = sh - sel * p.Hkv;
+  const int r = blockIdx.x, sel = warp / p.Hkv, h = warp - sel * p.Hkv;
   const int D = p.D;
   const int b = r / p.L, l = r - b * p.L;
+  float* rcos = esm;
+  float* rsin = esm + D / 2;
+  // the token's rotations (inputs only: computed before the dependency wait)
+  const int half = p.rope_dims / 2;
+  if (p.rope_dims > 0) {
+    const float pos = p.rope_scale * (float)(p.pos0 + l);
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const float inv = p.rope_freqs ? 1.0f / p.rope_freqs[i]
+                                     : exp2f(-((float)i / (float)half) * p.rope_base);
+      float sn, cs;
+      sincosf(pos * inv, &sn, &cs);
+      rcos[i] = cs;
+      rsin[i] = sn;
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __syncthreads();
+  float* row = esm + D + warp * D;
   const int src = (sel == 1 && p.v_from_k) ? 0 : sel;
   float x[E];
   const float* part = p.part + (((int64_t)src * p.Hkv + h) * p.ns * p.R + r) * D;
@@ -334,8 +350,6 @@ __global__ void __launch_bounds__(256) proj_epilogue_warp_kernel(const PP p) {
     }
   }
   if (sel == 0 && p.rope_dims > 0) {
-    const int half = p.rope_dims / 2;
-    float* row = rows[warp];
 #pragma unroll
     for (int k = 0; k < E; k++) {
       const int e = lane + 32 * k;
@@ -343,17 +357,13 @@ __global__ void __launch_bounds__(256) proj_epilogue_warp_kernel(const PP p) {
       row[e] = x[k];
     }
     __syncwarp();
-    const float pos = p.rope_scale * (float)(p.pos0 + l);
 #pragma unroll
     for (int k = 0; k < E; k++) {
       const int e = lane + 32 * k;
       if (e < 2 * half) {
         const int i = p.rope_trad ? e >> 1 : (e < half ? e : e - half);
         const int e1 = p.rope_trad ? 2 * i : i, e2 = p.rope_trad ? 2 * i + 1 : i + half;
-        const float inv = p.rope_freqs ? 1.0f / p.rope_freqs[i]
-                                       : exp2f(-((float)i / (float)half) * p.rope_base);
-        float sn, cs;
-        sincosf(pos * inv, &sn, &cs);
+        const float cs = rcos[i], sn = rsin[i];
         const float x1 = row[e1], x2 = row[e2];
         x[k] = round_dt<BF>(e == e1 ? x1 * cs - x2 * sn : x1 * sn + x2 * cs);
       }
@@ -1020,20 +1030,21 @@ size_t project_workspace_bytes(const ProjArgs& a, int Hkv, int D, int* splits) {
   return attn::kPartialOff + part + xp + 2 * xs;  // sums, then the bf16 block scales
 }
 
-// proj_epilogue_warp_kernel over every (row, K|V, kv head): 8 rows per CTA.
+// proj_epilogue_warp_kernel: one CTA per token, one warp per (K|V, kv head).
 template <int BITS, bool BF>
 static int32_t launch_epilogue_warp_b(const PP& p, cudaStream_t st) {
-  const int64_t jobs = (int64_t)p.R * 2 * p.Hkv;
-  const dim3 grid((unsigned)((jobs + 7) / 8));
+  const dim3 grid((unsigned)p.R);
+  const int threads = 64 * p.Hkv;
+  const size_t smem = (size_t)(2 * p.Hkv + 1) * p.D * sizeof(float);
   switch (p.D / 32) {
-    case 1: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 1>, grid, dim3(256), 0, st, p)); break;
-    case 2: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 2>, grid, dim3(256), 0, st, p)); break;
-    case 3: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 3>, grid, dim3(256), 0, st, p)); break;
-    case 4: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 4>, grid, dim3(256), 0, st, p)); break;
-    case 5: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 5>, grid, dim3(256), 0, st, p)); break;
-    case 6: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 6>, grid, dim3(256), 0, st, p)); break;
-    case 7: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 7>, grid, dim3(256), 0, st, p)); break;
-    default: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 8>, grid, dim3(256), 0, st, p)); break;
+    case 1: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 1>, grid, dim3(threads), smem, st, p)); break;
+    case 2: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 2>, grid, dim3(threads), smem, st, p)); break;
+    case 3: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 3>, grid, dim3(threads), smem, st, p)); break;
+    case 4: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 4>, grid, dim3(threads), smem, st, p)); break;
+    case 5: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 5>, grid, dim3(threads), smem, st, p)); break;
+    case 6: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 6>, grid, dim3(threads), smem, st, p)); break;
+    case 7: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 7>, grid, dim3(threads), smem, st, p)); break;
+    default: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 8>, grid, dim3(threads), smem, st, p)); break;
   }
   return KVQ_OK;
 }
@@ -1164,7 +1175,18 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
       default: rc = mk(proj_mma_kernel<8, true, 128>); break;
     }
     if (rc) return rc;
-    return launch_epilogue_warp(p, g.bits, bf, st);
+    if (Hkv <= 16) return launch_epilogue_warp(p, g.bits, bf, st);  // one warp per (K|V, head)
+    const dim3 g2(p.R, 2 * Hkv);
+    auto ek = [&](auto kern) -> int32_t {
+      KVQ_CUDA_TRY(launch_pdl(kern, g2, dim3(threads), 0, st, p));
+      return KVQ_OK;
+    };
+    switch (g.bits * 2 + (bf ? 1 : 0)) {
+      case 4 * 2: return ek(proj_epilogue_kernel<4, false>);
+      case 4 * 2 + 1: return ek(proj_epilogue_kernel<4, true>);
+      case 8 * 2: return ek(proj_epilogue_kernel<8, false>);
+      default: return ek(proj_epilogue_kernel<8, true>);
+    }
   }
   const dim3 g1(ns, 2 * Hkv, (p.R + proj_rows(p.R) - 1) / proj_rows(p.R));
   const int RC = proj_rows(p.R);
