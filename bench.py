@@ -821,7 +821,7 @@ def run_kv_projection(args, rank, world, local_rank):
         "prefill_chunk": {"tokens": c["chunk"], "us_per_layer": round(pre_s * 1e6, 2),
                           "tflops": round(flops / pre_s / 1e12, 2),
                           "kernels": "proj_xprep_kernel + proj_mma_kernel (mma.sync, codes as "
-                                     "exact fp16 operands) + proj_epilogue_kernel"},
+                                     "exact fp16 operands) + proj_epilogue_warp_kernel"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "kernel": "proj_partial_kernel<4,bf16,1> + proj_epilogue_kernel<4,bf16>",
