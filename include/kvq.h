@@ -161,6 +161,14 @@ typedef struct kvq_kv_projection {
   float rope_base, rope_scale;
   float rope_pre_scale;        /* 0 or 1: none */
   const float* rope_freqs;
+  /* The query side (qProj, qNorm, Q's RoPE; gemma4.ts:224-226 and the
+   * rope of q before attention): q_proj.packed NULL for none.  q_heads
+   * query heads of head_dim, out_features = q_heads * head_dim; the same
+   * RoPE as K. */
+  kvq_qlinear q_proj;
+  int32_t q_heads;
+  int32_t q_norm;
+  const void* q_norm_weight;   /* device [head_dim] dtype, nullable */
 } kvq_kv_projection;
 
 /* kvq_append of the projected, normed and roped K/V rows of x (device [B,
@@ -169,8 +177,12 @@ typedef struct kvq_kv_projection {
  * quantize-on-append run in the same pass, and the rows land where
  * kvq_append would put them (same growth / ring state machine).  Replaces
  * kProj/vProj + kNorm/vNorm + rope + transposes + updateAndFetchQuantized
- * (src/model/gemma4.ts:234-268).  k_out / v_out (nullable, device [B,
- * kv_heads, L, head_dim] dtype) receive the rows before quantisation.
+ * (src/model/gemma4.ts:234-268), and with a query projection also qProj +
+ * qNorm + transpose + rope of q (:224-226, generated/gemma4-12b.ts:52-54,
+ * :73-74): q_out (device [B, q_heads, L, head_dim] dtype, required then)
+ * receives the query rows attention takes.  k_out / v_out (nullable,
+ * device [B, kv_heads, L, head_dim] dtype) receive the K / V rows before
+ * quantisation.
  * workspace NULL: the library-managed scratch; else at least
  * kvq_append_projected_workspace bytes.  The layer's parameters (the
  * weight triples, norm weights, rope_freqs) are read-only here and may be
@@ -178,8 +190,8 @@ typedef struct kvq_kv_projection {
  * them on the stream (programmatic dependent launch): that kernel must not
  * write them.  x, the cache and k_out / v_out are ordered normally. */
 int32_t kvq_append_projected(kvq_cache* cache, const void* x, int32_t L,
-                             const kvq_kv_projection* proj, void* k_out, void* v_out,
-                             void* workspace, size_t workspace_bytes, void* stream);
+                             const kvq_kv_projection* proj, void* q_out, void* k_out,
+                             void* v_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Workspace bytes kvq_append_projected needs for L tokens. */
 int32_t kvq_append_projected_workspace(const kvq_cache* cache, int32_t L,

@@ -562,7 +562,7 @@ int32_t check_qlinear(const kvq_qlinear& w, const char* name, const kvq_desc& d)
   if (w.in_features <= 0 || w.in_features % w.group_size)
     return fail(KVQ_ERR_ARG, n + ": in_features must be a positive multiple of group_size");
   if ((int64_t)w.out_features != (int64_t)d.kv_heads * d.head_dim)
-    return fail(KVQ_ERR_ARG, n + ": out_features must be kv_heads * head_dim");
+    return fail(KVQ_ERR_ARG, n + ": out_features must be its heads * head_dim");
   if (reinterpret_cast<uintptr_t>(w.packed) % 16)
     return fail(KVQ_ERR_ARG, n + ": packed must be 16-byte aligned");
   return KVQ_OK;
@@ -584,6 +584,17 @@ int32_t make_proj_args(const kvq_cache* c, const void* x, int32_t L, const kvq_k
     if (pr->v_proj.bits != pr->k_proj.bits)
       return fail(KVQ_ERR_ARG, "k_proj and v_proj must share a bit width");
   }
+  const bool has_q = pr->q_proj.packed != nullptr;
+  if (has_q) {
+    if (pr->q_heads <= 0) return fail(KVQ_ERR_ARG, "q_heads must be positive with a query projection");
+    kvq_desc dq = d;
+    dq.kv_heads = pr->q_heads;  // out_features = q_heads * head_dim
+    if ((rc = check_qlinear(pr->q_proj, "q_proj", dq))) return rc;
+    if (pr->q_proj.in_features != pr->k_proj.in_features)
+      return fail(KVQ_ERR_ARG, "k_proj and q_proj must share in_features");
+    if (pr->q_proj.bits != pr->k_proj.bits)
+      return fail(KVQ_ERR_ARG, "k_proj and q_proj must share a bit width");
+  }
   if (pr->rope_dims < 0 || pr->rope_dims > d.head_dim || pr->rope_dims % 2)
     return fail(KVQ_ERR_ARG, "rope_dims must be even and within head_dim");
   if (pr->rope_dims > 0 && !pr->rope_freqs && !(pr->rope_base > 0.0f))
@@ -597,9 +608,16 @@ int32_t make_proj_args(const kvq_cache* c, const void* x, int32_t L, const kvq_k
   a.v_from_k = pr->v_from_k != 0;
   if (!a.v_from_k)
     a.wv = {pr->v_proj.packed, pr->v_proj.scales, pr->v_proj.biases, pr->v_proj.bits, pr->v_proj.group_size};
+  a.has_q = has_q;
+  if (has_q) {
+    a.Hq = pr->q_heads;
+    a.wq = {pr->q_proj.packed, pr->q_proj.scales, pr->q_proj.biases, pr->q_proj.bits,
+            pr->q_proj.group_size};
+  }
   a.k_norm = pr->k_norm_weight;
   a.v_norm = pr->v_norm_weight;
-  a.norms = (pr->k_norm ? 1 : 0) | (pr->v_norm ? 2 : 0);
+  a.q_norm = pr->q_norm_weight;
+  a.norms = (pr->k_norm ? 1 : 0) | (pr->v_norm ? 2 : 0) | (has_q && pr->q_norm ? 4 : 0);
   a.eps = pr->norm_eps;
   a.rope_dims = pr->rope_dims;
   a.rope_traditional = pr->rope_traditional != 0;
@@ -616,12 +634,14 @@ int32_t make_proj_args(const kvq_cache* c, const void* x, int32_t L, const kvq_k
 extern "C" {
 
 int32_t kvq_append_projected(kvq_cache* c, const void* x, int32_t L, const kvq_kv_projection* proj,
-                             void* k_out, void* v_out, void* workspace, size_t workspace_bytes,
-                             void* stream) {
+                             void* q_out, void* k_out, void* v_out, void* workspace,
+                             size_t workspace_bytes, void* stream) {
   kvq::ProjArgs a;
   int32_t rc = make_proj_args(c, x, L, proj, a);
   if (rc) return rc;
   if (!x) return fail(KVQ_ERR_ARG, "x is NULL");
+  if (a.has_q && !q_out) return fail(KVQ_ERR_ARG, "q_out is NULL with a query projection");
+  a.q_out = q_out;
   a.k_out = k_out;
   a.v_out = v_out;
   DeviceGuard guard(c->d.device);

@@ -66,11 +66,14 @@ struct ProjWeights {
 struct ProjArgs {
   const void* x;  // [B, L, hidden] contiguous
   int B, L, hidden;
-  ProjWeights wk, wv;
+  ProjWeights wk, wv, wq;
   bool v_from_k;  // V is K's projection (before the norms)
+  bool has_q;     // a query projection (Hq heads) into q_out
+  int Hq;
   const void* k_norm;  // [D] nullable
   const void* v_norm;  // [D] nullable
-  int norms;           // bit 0: RMSNorm on K, bit 1: on V
+  const void* q_norm;  // [D] nullable
+  int norms;           // bit 0: RMSNorm on K, bit 1: on V, bit 2: on Q
   float eps;
   int rope_dims;       // 0: no RoPE
   bool rope_traditional;  // pairs (2i, 2i+1) instead of (i, i + dims/2)
@@ -80,6 +83,7 @@ struct ProjArgs {
   int64_t pos0;        // position of row l = pos0 + l
   void* k_out;         // [B, Hkv, L, D] rows before quantisation, nullable
   void* v_out;
+  void* q_out;         // [B, Hq, L, D] the query rows (with has_q)
 };
 // Workspace bytes of one launch (and the split count it uses).
 size_t project_workspace_bytes(const ProjArgs& a, int Hkv, int D, int* splits);

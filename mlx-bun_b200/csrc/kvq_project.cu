@@ -61,16 +61,23 @@ struct W {
   int bits, gs;
 };
 
+// Projections and heads.  A compute unit is one head of one projection —
+// the K heads, then the V heads (none when V is K's projection), then the
+// Q heads (none without a query projection) — and owns D output rows.  A
+// finish unit is one head's row after the projection: the K heads, the V
+// heads (finished from K's rows when V is K's projection), the Q heads.
 struct PP {
   const uint16_t* x;  // [R, hidden]
-  W wk, wv;
+  W wk, wv, wq;
   int v_from_k;
   int R, L, hidden, Hkv, D, ns;
-  float* part;        // [2][Hkv][ns][R][D]
+  int Hq, nv, nq;     // query heads; V and Q compute units (0 or Hkv, 0 or Hq)
+  float* part;        // [compute unit][ns][R][D]
   // epilogue
   const uint16_t* k_norm;
   const uint16_t* v_norm;
-  int norms;          // bit 0: K, bit 1: V
+  const uint16_t* q_norm;
+  int norms;          // bit 0: K, bit 1: V, bit 2: Q
   float eps;
   int rope_dims, rope_trad;
   float rope_base, rope_scale, rope_pre;
@@ -78,20 +85,58 @@ struct PP {
   int64_t pos0;
   uint16_t* k_out;    // [B, Hkv, L, D] nullable
   uint16_t* v_out;
+  uint16_t* q_out;    // [B, Hq, L, D] (with a query projection)
   // destination
   TripleView dk, dv;
   int64_t dst_row0;
   int bits, gs;       // cache quantisation
 };
 
+__device__ __forceinline__ int units_of(const PP& p) { return p.Hkv + p.nv + p.nq; }
+
+// compute unit u -> projection (0 K, 1 V, 2 Q) and head
+__device__ __forceinline__ void unit_of(const PP& p, int u, int& sel, int& h) {
+  if (u < p.Hkv) {
+    sel = 0;
+    h = u;
+  } else if (u < p.Hkv + p.nv) {
+    sel = 1;
+    h = u - p.Hkv;
+  } else {
+    sel = 2;
+    h = u - p.Hkv - p.nv;
+  }
+}
+
+__device__ __forceinline__ const W& w_of(const PP& p, int sel) {
+  return sel == 0 ? p.wk : sel == 1 ? p.wv : p.wq;
+}
+
+// finish unit f -> projection, head and the compute unit holding its rows
+__device__ __forceinline__ void finish_of(const PP& p, int f, int& sel, int& h, int& src) {
+  if (f < p.Hkv) {
+    sel = 0;
+    h = f;
+    src = f;
+  } else if (f < 2 * p.Hkv) {
+    sel = 1;
+    h = f - p.Hkv;
+    src = p.nv ? p.Hkv + h : h;
+  } else {
+    sel = 2;
+    h = f - 2 * p.Hkv;
+    src = p.Hkv + p.nv + h;
+  }
+}
+
 template <int WBITS, bool BF, int RC>
 __global__ void __launch_bounds__(256) proj_partial_kernel(const PP p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ float xs[];  // [RC][gs]
-  const int sel = blockIdx.y / p.Hkv, h = blockIdx.y - sel * p.Hkv;
-  if (sel == 1 && p.v_from_k) return;
-  const W w = sel ? p.wv : p.wk;
+  int sel, h;
+  unit_of(p, blockIdx.y, sel, h);
+  const W w = w_of(p, sel);
   const int tid = threadIdx.x, o = tid, D = p.D;
   const int r0 = blockIdx.z * RC, nr = min(RC, p.R - r0);
   const int G = p.hidden / w.gs;
@@ -132,7 +177,7 @@ __global__ void __launch_bounds__(256) proj_partial_kernel(const PP p) {
     }
   }
   if (o >= D) return;
-  float* dst = p.part + ((((int64_t)sel * p.Hkv + h) * p.ns + blockIdx.x) * p.R + r0) * D + o;
+  float* dst = p.part + (((int64_t)blockIdx.y * p.ns + blockIdx.x) * p.R + r0) * D + o;
 #pragma unroll
   for (int r = 0; r < RC; r++)
     if (r < nr) dst[(int64_t)r * D] = acc[r];
@@ -165,10 +210,10 @@ __device__ __forceinline__ RowConsts row_consts(const PP& p, int sel, int r) {
   const int o = threadIdx.x;
   RowConsts c{1.0f, 1.0f, 0.0f};
   if (o >= p.D) return c;
-  const uint16_t* wn = sel ? p.v_norm : p.k_norm;
+  const uint16_t* wn = sel == 0 ? p.k_norm : sel == 1 ? p.v_norm : p.q_norm;
   if ((p.norms & (1 << sel)) && wn) c.wn = dt_to_f<BF>(wn[o]);
   const int half = p.rope_dims / 2;
-  if (sel == 0 && o < 2 * half) {
+  if (sel != 1 && o < 2 * half) {
     const int l = r % p.L;
     const int i = p.rope_trad ? o >> 1 : (o < half ? o : o - half);
     const float inv = p.rope_freqs ? 1.0f / p.rope_freqs[i]
@@ -180,9 +225,10 @@ __device__ __forceinline__ RowConsts row_consts(const PP& p, int sel, int r) {
   return c;
 }
 
-// Everything after the projection for one output row (token r) of kv head
-// h: `x` is thread o's projected value (the dtype-rounded sum), sel 0 / 1 =
-// K / V.  RMSNorm, RoPE (K), the checking copy, then the quantize-on-append.
+// Everything after the projection for one output row (token r) of head h:
+// `x` is thread o's projected value (the dtype-rounded sum), sel 0 / 1 / 2
+// = K / V / Q.  RMSNorm, RoPE (K and Q), then for Q the row into q_out, for
+// K and V the checking copy and the quantize-on-append.
 // Called by the whole CTA (it synchronises); `row` holds D floats, `red` 32.
 template <int BITS, bool BF>
 __device__ void finish_row(const PP& p, int sel, int h, int r, float x, const RowConsts& rc,
@@ -193,13 +239,13 @@ __device__ void finish_row(const PP& p, int sel, int h, int r, float x, const Ro
     // RMSNorm: x * (1 / sqrt(mean(x^2) + eps)) rounded, then * weight rounded
     const float ss = block_sum(o < D ? x * x : 0.0f, red);
     const float n = 1.0f / sqrtf(ss / (float)D + p.eps);
-    const uint16_t* wn = sel ? p.v_norm : p.k_norm;
+    const uint16_t* wn = sel == 0 ? p.k_norm : sel == 1 ? p.v_norm : p.q_norm;
     if (o < D) {
       x = round_dt<BF>(x * n);
       if (wn) x = round_dt<BF>(x * rc.wn);
     }
   }
-  if (sel == 0 && p.rope_dims > 0) {
+  if (sel != 1 && p.rope_dims > 0) {
     // the pre-rope input scale (a weak scalar: rounded to the dtype first)
     if (p.rope_pre != 0.0f && o < p.rope_dims) x = round_dt<BF>(x * round_dt<BF>(p.rope_pre));
     __syncthreads();
@@ -213,6 +259,10 @@ __device__ void finish_row(const PP& p, int sel, int h, int r, float x, const Ro
       const float x1 = row[e1], x2 = row[e2];
       x = round_dt<BF>(o == e1 ? x1 * rc.cs - x2 * rc.sn : x1 * rc.sn + x2 * rc.cs);
     }
+  }
+  if (sel == 2) {  // the query row, in the layout attention reads
+    if (o < D) p.q_out[(((int64_t)b * p.Hq + h) * p.L + l) * D + o] = f_to_dt<BF>(x);
+    return;
   }
   uint16_t* dbg = sel ? p.v_out : p.k_out;
   if (dbg && o < D) dbg[(((int64_t)b * p.Hkv + h) * p.L + l) * D + o] = f_to_dt<BF>(x);
@@ -266,13 +316,14 @@ __global__ void __launch_bounds__(256) proj_epilogue_kernel(const PP p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float row[256];
   __shared__ float red[32];
-  const int r = blockIdx.x, sel = blockIdx.y / p.Hkv, h = blockIdx.y - sel * p.Hkv;
+  const int r = blockIdx.x;
+  int sel, h, src;
+  finish_of(p, blockIdx.y, sel, h, src);
   const int o = threadIdx.x, D = p.D;
-  const int src = (sel == 1 && p.v_from_k) ? 0 : sel;
   float x = 0.0f;
   if (o < D) {
     // the split partials, loaded together, summed in split order
-    const float* part = p.part + (((int64_t)src * p.Hkv + h) * p.ns * p.R + r) * D + o;
+    const float* part = p.part + ((int64_t)src * p.ns * p.R + r) * D + o;
     const int64_t ss = (int64_t)p.R * D;
     for (int s0 = 0; s0 < p.ns; s0 += 8) {
       float v[8];
@@ -287,7 +338,7 @@ __global__ void __launch_bounds__(256) proj_epilogue_kernel(const PP p) {
 }
 
 // The same per-row work with one warp per row (prefill: many rows).  One
-// CTA per token, one warp per (K | V, kv head): the CTA first computes the
+// CTA per token, one warp per finish unit (a K, V or Q head): the CTA first computes the
 // token's RoPE rotations (cos, sin of each pair's angle) once into shared
 // memory — they are the same for every kv head — then each warp works on
 // its row with no block barrier.  Lane l holds elements l + 32 k (k < E =
@@ -300,7 +351,9 @@ __global__ void __launch_bounds__(1024) proj_epilogue_warp_kernel(const PP p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ float esm[];  // cos [D/2], sin [D/2], then one row of D per warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x, sel = warp / p.Hkv, h = warp - sel * p.Hkv;
+  const int r = blockIdx.x;
+  int sel, h, src;
+  finish_of(p, warp, sel, h, src);
   const int D = p.D;
   const int b = r / p.L, l = r - b * p.L;
   float* rcos = esm;
@@ -321,9 +374,8 @@ __global__ void __launch_bounds__(1024) proj_epilogue_warp_kernel(const PP p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
   float* row = esm + D + warp * D;
-  const int src = (sel == 1 && p.v_from_k) ? 0 : sel;
   float x[E];
-  const float* part = p.part + (((int64_t)src * p.Hkv + h) * p.ns * p.R + r) * D;
+  const float* part = p.part + ((int64_t)src * p.ns * p.R + r) * D;
 #pragma unroll
   for (int k = 0; k < E; k++) x[k] = 0.0f;
   for (int s2 = 0; s2 < p.ns; s2++) {  // every element's load of a split in flight together
@@ -342,14 +394,14 @@ __global__ void __launch_bounds__(1024) proj_epilogue_warp_kernel(const PP p) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     const float n = 1.0f / sqrtf(ss / (float)D + p.eps);
-    const uint16_t* wn = sel ? p.v_norm : p.k_norm;
+    const uint16_t* wn = sel == 0 ? p.k_norm : sel == 1 ? p.v_norm : p.q_norm;
 #pragma unroll
     for (int k = 0; k < E; k++) {
       x[k] = round_dt<BF>(x[k] * n);
       if (wn) x[k] = round_dt<BF>(x[k] * dt_to_f<BF>(wn[lane + 32 * k]));
     }
   }
-  if (sel == 0 && p.rope_dims > 0) {
+  if (sel != 1 && p.rope_dims > 0) {
 #pragma unroll
     for (int k = 0; k < E; k++) {
       const int e = lane + 32 * k;
@@ -368,6 +420,12 @@ __global__ void __launch_bounds__(1024) proj_epilogue_warp_kernel(const PP p) {
         x[k] = round_dt<BF>(e == e1 ? x1 * cs - x2 * sn : x1 * sn + x2 * cs);
       }
     }
+  }
+  if (sel == 2) {  // the query row, in the layout attention reads
+    uint16_t* qrow = p.q_out + (((int64_t)b * p.Hq + h) * p.L + l) * D;
+#pragma unroll
+    for (int k = 0; k < E; k++) qrow[lane + 32 * k] = f_to_dt<BF>(x[k]);
+    return;
   }
   uint16_t* dbg = sel ? p.v_out : p.k_out;
   if (dbg) {
@@ -459,8 +517,9 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
   __shared__ float red[32];
   extern __shared__ float sm[];  // part[RC][D], sumx[RC][kMaxG], xs[RC][span]
   const int rank = (int)cluster.block_rank();
-  const int sel = blockIdx.y / p.Hkv, h = blockIdx.y - sel * p.Hkv;
-  const W w = sel ? p.wv : p.wk;
+  int sel, h;
+  unit_of(p, blockIdx.y, sel, h);
+  const W w = w_of(p, sel);
   const int o = threadIdx.x, D = p.D;
   const int G = p.hidden / w.gs, gs = w.gs;
   const int g0 = rank * G / CS, g1 = (rank + 1) * G / CS, ng = g1 - g0;
@@ -496,7 +555,7 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
 #pragma unroll
     for (int r = 0; r < RC; r++) {
       rcs[r] = row_consts<BF>(p, sel, r0 + r < p.R ? r0 + r : 0);
-      rcv[r] = p.v_from_k ? row_consts<BF>(p, 1, r0 + r < p.R ? r0 + r : 0) : rcs[r];
+      rcv[r] = (p.v_from_k && sel == 0) ? row_consts<BF>(p, 1, r0 + r < p.R ? r0 + r : 0) : rcs[r];
     }
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -623,7 +682,7 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
   for (int r = 0; r < RC; r++) {
     if (r >= nr) break;
     finish_row<BITS, BF>(p, sel, h, r0 + r, xsum[r], rcs[r], row, red);
-    if (p.v_from_k) finish_row<BITS, BF>(p, 1, h, r0 + r, xsum[r], rcv[r], row, red);
+    if (p.v_from_k && sel == 0) finish_row<BITS, BF>(p, 1, h, r0 + r, xsum[r], rcv[r], row, red);
   }
 }
 
@@ -739,37 +798,54 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int WBITS, bool BF, int GS>
-__global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, int sely, const uint8_t* xp,
+__global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, const uint8_t* xp,
                                                           const float* xsum, const float* xfac) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ __align__(16) uint8_t smraw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wm = warp & 3, wn = warp >> 2;  // 4 x 2 warps: 32 rows x 32 tokens each
-  const int HD = p.Hkv * p.D, M = sely * HD;
+  const int M = units_of(p) * p.D;  // rows of every compute unit, unit by unit
   const int m0 = blockIdx.x * kMT, n0 = blockIdx.y * kNT;
+  // output row m -> its projection's weights and the weight row
+  auto row_w = [&](int m, int64_t& wr) -> const W& {
+    const int u = m / p.D;
+    int sel, h;
+    unit_of(p, u, sel, h);
+    wr = (int64_t)h * p.D + (m - u * p.D);
+    return w_of(p, sel);
+  };
   constexpr int gs = GS;
   const int G = p.hidden / gs;
   constexpr MmaGeo geo{GS, WBITS};
   constexpr int RB = geo.row_bytes(), RP = geo.row_pitch(), KS = geo.ksteps();
   const int64_t row_stride = (int64_t)p.hidden * WBITS / 8;  // bytes per weight row
   auto stage = [&](int b) -> uint8_t* { return smraw + (size_t)b * geo.stage_bytes(); };
+  // this thread's weight copies (the same rows for every group): where each
+  // row's codes start, worked out once
+  constexpr int kCp = (kMT * (RB / 16) + 255) / 256;
+  const uint8_t* wsrc[kCp];
+  int wdst[kCp];
+  bool wok[kCp];
+#pragma unroll
+  for (int k = 0; k < kCp; k++) {
+    const int i = tid + k * 256;
+    const int row = i / (RB / 16), c = i - row * (RB / 16);
+    const int m = m0 + row;
+    wok[k] = i < kMT * (RB / 16) && m < M;
+    int64_t wr;
+    const W& w = row_w(wok[k] ? m : 0, wr);
+    wsrc[k] = reinterpret_cast<const uint8_t*>(w.packed) + wr * row_stride + c * 16;
+    wdst[k] = row * RP + c * 16;
+  }
   // copies of one group into stage b (every thread commits one cp.async group)
   auto issue = [&](int grp, int b) {
     if (grp < G) {
       uint8_t* st = stage(b);
-      const int nw = kMT * (RB / 16);
-      for (int i = tid; i < nw; i += 256) {
-        const int row = i / (RB / 16), c = i - row * (RB / 16);
-        const int m = m0 + row;
-        const bool ok = m < M;
-        const int mm = ok ? m : 0;
-        const W& w = mm < HD ? p.wk : p.wv;
-        const int64_t wr = mm < HD ? mm : mm - HD;
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(w.packed) + wr * row_stride +
-                             (int64_t)grp * RB + c * 16;
-        cp_async16(st + row * RP + c * 16, src, ok);
-      }
+#pragma unroll
+      for (int k = 0; k < kCp; k++)
+        if (tid + k * 256 < kMT * (RB / 16))
+          cp_async16(st + wdst[k], wsrc[k] + (int64_t)grp * RB, wok[k]);
       uint8_t* sx = st + geo.w_bytes();
       const int nx = KS * kNT * 2;  // 16-byte pieces: 2 per (k-step, token)
       for (int i = tid; i < nx; i += 256) {
@@ -798,12 +874,15 @@ __global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, int sely, 
       for (int c = 0; c < 4; c++) acc[a][b][c] = out[a][b][c] = 0.0f;
   // scale (thread < kMT) or bias (thread >= kMT) of one row, one group ahead
   const int srow = tid & (kMT - 1), sm_ = m0 + srow;
-  auto fetch_sb = [&](int grp) -> float {
-    if (grp >= G || sm_ >= M) return 0.0f;
-    const W& w = sm_ < HD ? p.wk : p.wv;
-    const int64_t wr = sm_ < HD ? sm_ : sm_ - HD;
+  const uint16_t* sbrow = nullptr;
+  if (sm_ < M) {
+    int64_t wr;
+    const W& w = row_w(sm_, wr);
     const uint16_t* src = tid < kMT ? w.scales : w.biases;
-    return src ? dt_to_f<BF>(__ldg(src + wr * G + grp)) : 0.0f;
+    if (src) sbrow = src + wr * G;
+  }
+  auto fetch_sb = [&](int grp) -> float {
+    return (grp < G && sbrow) ? dt_to_f<BF>(__ldg(sbrow + grp)) : 0.0f;
   };
   float sb_next = fetch_sb(0);
 #pragma unroll
@@ -875,15 +954,15 @@ __global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, int sely, 
     }
   }
   cp_async_wait<0>();
-  // the projection rows, f32, in the epilogue's layout part[sel][h][0][r][d]
+  // the projection rows, f32, in the epilogue's layout part[unit][0][r][d]
 #pragma unroll
   for (int mt = 0; mt < 2; mt++)
 #pragma unroll
     for (int hh = 0; hh < 2; hh++) {
       const int m = m0 + wm * 32 + mt * 16 + g + 8 * hh;
       if (m >= M) continue;
-      const int sel = m / HD, rem = m - sel * HD, h = rem / p.D, d = rem - h * p.D;
-      float* dst = p.part + ((int64_t)(sel * p.Hkv + h) * p.R) * p.D + d;
+      const int u = m / p.D, d = m - u * p.D;
+      float* dst = p.part + (int64_t)u * p.R * p.D + d;
 #pragma unroll
       for (int nt = 0; nt < 4; nt++)
 #pragma unroll
@@ -956,19 +1035,37 @@ static int32_t allow_wide_clusters(const void* kern) {
 
 // The one-launch cluster path: a few rows, every CTA's slice of the hidden
 // dimension within kMaxG groups, its inputs within 48 KB of shared memory.
+// The projections a call runs (K always; V unless it is K's; Q if given).
+static int projections(const ProjArgs& a, const ProjWeights* (&w)[3]) {
+  int n = 0;
+  w[n++] = &a.wk;
+  if (!a.v_from_k) w[n++] = &a.wv;
+  if (a.has_q) w[n++] = &a.wq;
+  return n;
+}
+// compute units (heads of the projections run) and finish units (K, V, Q heads)
+static int compute_units(const ProjArgs& a, int Hkv) {
+  return Hkv + (a.v_from_k ? 0 : Hkv) + (a.has_q ? a.Hq : 0);
+}
+static int finish_units(const ProjArgs& a, int Hkv) { return 2 * Hkv + (a.has_q ? a.Hq : 0); }
+
 static bool use_cluster(const ProjArgs& a, int cs) {
   const int R = a.B * a.L;
-  const int gk = a.hidden / a.wk.gs;
-  const int gv = a.v_from_k ? gk : a.hidden / a.wv.gs;
-  const int gmax = (std::max(gk, gv) + cs - 1) / cs;
-  const int span = gmax * std::max(a.wk.gs, a.v_from_k ? a.wk.gs : a.wv.gs);
+  const ProjWeights* w[3];
+  const int n = projections(a, w);
+  int gmax = 0, gsmax = 0;
+  for (int i = 0; i < n; i++) {
+    gmax = std::max(gmax, (a.hidden / w[i]->gs + cs - 1) / cs);
+    gsmax = std::max(gsmax, w[i]->gs);
+  }
+  const int span = gmax * gsmax;
   return R <= 4 && gmax <= kMaxG && (size_t)4 * (256 + kMaxG + span) * 4 <= 48 * 1024;
 }
 
 template <int WBITS, int BITS, bool BF, int CS>
-static int32_t launch_cluster(const PP& p, int RC, int sely, size_t smem, cudaStream_t st) {
+static int32_t launch_cluster(const PP& p, int RC, int units, size_t smem, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(CS, sely * p.Hkv, (p.R + RC - 1) / RC);
+  cfg.gridDim = dim3(CS, units, (p.R + RC - 1) / RC);
   cfg.blockDim = dim3(p.D);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -992,13 +1089,13 @@ static int32_t launch_cluster(const PP& p, int RC, int sely, size_t smem, cudaSt
 }
 
 template <int WBITS, int BITS>
-static int32_t launch_cluster_dt(const PP& p, bool bf, int cs, int RC, int sely, size_t smem,
+static int32_t launch_cluster_dt(const PP& p, bool bf, int cs, int RC, int units, size_t smem,
                                  cudaStream_t st) {
   if (cs == 16)
-    return bf ? launch_cluster<WBITS, BITS, true, 16>(p, RC, sely, smem, st)
-              : launch_cluster<WBITS, BITS, false, 16>(p, RC, sely, smem, st);
-  return bf ? launch_cluster<WBITS, BITS, true, 8>(p, RC, sely, smem, st)
-            : launch_cluster<WBITS, BITS, false, 8>(p, RC, sely, smem, st);
+    return bf ? launch_cluster<WBITS, BITS, true, 16>(p, RC, units, smem, st)
+              : launch_cluster<WBITS, BITS, false, 16>(p, RC, units, smem, st);
+  return bf ? launch_cluster<WBITS, BITS, true, 8>(p, RC, units, smem, st)
+            : launch_cluster<WBITS, BITS, false, 8>(p, RC, units, smem, st);
 }
 
 static int current_cluster_size() {
@@ -1018,24 +1115,29 @@ size_t project_workspace_bytes(const ProjArgs& a, int Hkv, int D, int* splits) {
   const int R = a.B * a.L;
   const int G = a.hidden / a.wk.gs;
   const int nrc = (R + proj_rows(R) - 1) / proj_rows(R);
-  const int heads = a.v_from_k ? Hkv : 2 * Hkv;
-  int ns = (2 * sms + heads * nrc - 1) / (heads * nrc);
-  ns = std::max(1, std::min(ns, std::min(G, a.v_from_k ? G : a.hidden / a.wv.gs)));
+  const int units = compute_units(a, Hkv);
+  const ProjWeights* w[3];
+  const int n = projections(a, w);
+  int gmin = G;
+  for (int i = 0; i < n; i++) gmin = std::min(gmin, a.hidden / w[i]->gs);
+  int ns = (2 * sms + units * nrc - 1) / (units * nrc);
+  ns = std::max(1, std::min(ns, gmin));
   if (splits) *splits = ns;
   // partials (split path; one split on the tensor-core path), then the
   // tensor-core path's fp16 inputs and their group sums
-  const size_t part = ((size_t)2 * Hkv * ns * R * D * sizeof(float) + 255) / 256 * 256;
+  const size_t part = ((size_t)units * ns * R * D * sizeof(float) + 255) / 256 * 256;
   const size_t xp = ((size_t)R * a.hidden * 2 + 255) / 256 * 256;
   const size_t xs = (size_t)G * ((R + 3) & ~3) * sizeof(float);
   return attn::kPartialOff + part + xp + 2 * xs;  // sums, then the bf16 block scales
 }
 
-// proj_epilogue_warp_kernel: one CTA per token, one warp per (K|V, kv head).
+// proj_epilogue_warp_kernel: one CTA per token, one warp per finish unit.
 template <int BITS, bool BF>
 static int32_t launch_epilogue_warp_b(const PP& p, cudaStream_t st) {
   const dim3 grid((unsigned)p.R);
-  const int threads = 64 * p.Hkv;
-  const size_t smem = (size_t)(2 * p.Hkv + 1) * p.D * sizeof(float);
+  const int fu = 2 * p.Hkv + p.nq;
+  const int threads = 32 * fu;
+  const size_t smem = (size_t)(fu + 1) * p.D * sizeof(float);
   switch (p.D / 32) {
     case 1: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 1>, grid, dim3(threads), smem, st, p)); break;
     case 2: KVQ_CUDA_TRY(launch_pdl(proj_epilogue_warp_kernel<BITS, BF, 2>, grid, dim3(threads), smem, st, p)); break;
@@ -1078,7 +1180,15 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
   p.wv = a.v_from_k ? p.wk
                     : W{a.wv.packed, static_cast<const uint16_t*>(a.wv.scales),
                         static_cast<const uint16_t*>(a.wv.biases), a.wv.bits, a.wv.gs};
+  p.wq = a.has_q ? W{a.wq.packed, static_cast<const uint16_t*>(a.wq.scales),
+                      static_cast<const uint16_t*>(a.wq.biases), a.wq.bits, a.wq.gs}
+                 : p.wk;
   p.v_from_k = a.v_from_k ? 1 : 0;
+  p.Hq = a.has_q ? a.Hq : 0;
+  p.nv = a.v_from_k ? 0 : Hkv;
+  p.nq = a.has_q ? a.Hq : 0;
+  p.q_norm = static_cast<const uint16_t*>(a.q_norm);
+  p.q_out = static_cast<uint16_t*>(a.q_out);
   p.R = a.B * a.L;
   p.L = a.L;
   p.hidden = a.hidden;
@@ -1106,34 +1216,48 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
   p.gs = g.gs;
   const bool bf = dtype == KVQ_DTYPE_BFLOAT16;
   const int threads = (D + 31) / 32 * 32;
-  if (a.wk.bits != (a.v_from_k ? a.wk.bits : a.wv.bits))
-    return fail(KVQ_ERR_ARG, "the K and V projections must share a bit width");
+  const ProjWeights* pw[3];
+  const int nproj = projections(a, pw);
+  bool same_gs = true;
+  for (int i = 0; i < nproj; i++) {
+    if (pw[i]->bits != a.wk.bits) return fail(KVQ_ERR_ARG, "the projections must share a bit width");
+    same_gs = same_gs && pw[i]->gs == a.wk.gs;
+  }
+  const int units = compute_units(a, Hkv), fu = finish_units(a, Hkv);
+  auto block_epilogue = [&]() -> int32_t {
+    const dim3 g2(p.R, fu);
+    auto ek = [&](auto kern) -> int32_t {
+      KVQ_CUDA_TRY(launch_pdl(kern, g2, dim3(threads), 0, st, p));
+      return KVQ_OK;
+    };
+    switch (g.bits * 2 + (bf ? 1 : 0)) {
+      case 4 * 2: return ek(proj_epilogue_kernel<4, false>);
+      case 4 * 2 + 1: return ek(proj_epilogue_kernel<4, true>);
+      case 8 * 2: return ek(proj_epilogue_kernel<8, false>);
+      default: return ek(proj_epilogue_kernel<8, true>);
+    }
+  };
   const int cs = current_cluster_size();
   if (use_cluster(a, cs)) {
     const int RC = p.R <= 1 ? 1 : 4;
-    // the largest slice of either projection, in elements
+    // the largest slice of any projection, in elements
     int span = 0;
-    for (const ProjWeights* pw : {&a.wk, &a.wv}) {
-      if (pw == &a.wv && a.v_from_k) continue;
-      span = std::max(span, (a.hidden / pw->gs + cs - 1) / cs * pw->gs);
-    }
+    for (int i = 0; i < nproj; i++)
+      span = std::max(span, (a.hidden / pw[i]->gs + cs - 1) / cs * pw[i]->gs);
     const size_t smem = (size_t)RC * (D + kMaxG + span) * sizeof(float);
-    const int sely = a.v_from_k ? 1 : 2;
     switch ((a.wk.bits == 8 ? 2 : 0) + (g.bits == 8 ? 1 : 0)) {
-      case 0: return launch_cluster_dt<4, 4>(p, bf, cs, RC, sely, smem, st);
-      case 1: return launch_cluster_dt<4, 8>(p, bf, cs, RC, sely, smem, st);
-      case 2: return launch_cluster_dt<8, 4>(p, bf, cs, RC, sely, smem, st);
-      default: return launch_cluster_dt<8, 8>(p, bf, cs, RC, sely, smem, st);
+      case 0: return launch_cluster_dt<4, 4>(p, bf, cs, RC, units, smem, st);
+      case 1: return launch_cluster_dt<4, 8>(p, bf, cs, RC, units, smem, st);
+      case 2: return launch_cluster_dt<8, 4>(p, bf, cs, RC, units, smem, st);
+      default: return launch_cluster_dt<8, 8>(p, bf, cs, RC, units, smem, st);
     }
   }
-  // prefill-sized: the tensor-core projection when both projections share
-  // a group size and x is 16-byte aligned, then the epilogue
-  const bool mma_ok = (a.v_from_k || a.wv.gs == a.wk.gs) &&
-                      reinterpret_cast<uintptr_t>(a.x) % 16 == 0;
+  // prefill-sized: the tensor-core projection when the projections share a
+  // group size and x is 16-byte aligned, then the epilogue
+  const bool mma_ok = same_gs && reinterpret_cast<uintptr_t>(a.x) % 16 == 0;
   if (mma_ok) {
-    const int sely = a.v_from_k ? 1 : 2;
     uint8_t* wsb = static_cast<uint8_t*>(ws);
-    const size_t part_bytes = ((size_t)2 * Hkv * ns * p.R * D * sizeof(float) + 255) / 256 * 256;
+    const size_t part_bytes = ((size_t)units * ns * p.R * D * sizeof(float) + 255) / 256 * 256;
     uint8_t* xp = wsb + attn::kPartialOff + part_bytes;
     float* xsum = reinterpret_cast<float*>(xp + ((size_t)p.R * a.hidden * 2 + 255) / 256 * 256);
     float* xfac = xsum + (size_t)(a.hidden / a.wk.gs) * ((p.R + 3) & ~3);
@@ -1151,11 +1275,11 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
     rc = a.wk.bits == 4 ? (bf ? xk(proj_xprep_kernel<4, true>) : xk(proj_xprep_kernel<4, false>))
                         : (bf ? xk(proj_xprep_kernel<8, true>) : xk(proj_xprep_kernel<8, false>));
     if (rc) return rc;
-    const dim3 gm((sely * Hkv * D + kMT - 1) / kMT, (p.R + kNT - 1) / kNT);
+    const dim3 gm((units * D + kMT - 1) / kMT, (p.R + kNT - 1) / kNT);
     auto mk = [&](auto kern) -> int32_t {
       int32_t r2 = kernel_setup(reinterpret_cast<const void*>(kern), 256, smem, dev, nullptr);
       if (r2) return r2;
-      KVQ_CUDA_TRY(launch_pdl(kern, gm, dim3(256), (size_t)smem, st, p, sely,
+      KVQ_CUDA_TRY(launch_pdl(kern, gm, dim3(256), (size_t)smem, st, p,
                               static_cast<const uint8_t*>(xp), static_cast<const float*>(xsum),
                               static_cast<const float*>(xfac)));
       return KVQ_OK;
@@ -1175,39 +1299,22 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
       default: rc = mk(proj_mma_kernel<8, true, 128>); break;
     }
     if (rc) return rc;
-    if (Hkv <= 16) return launch_epilogue_warp(p, g.bits, bf, st);  // one warp per (K|V, head)
-    const dim3 g2(p.R, 2 * Hkv);
-    auto ek = [&](auto kern) -> int32_t {
-      KVQ_CUDA_TRY(launch_pdl(kern, g2, dim3(threads), 0, st, p));
-      return KVQ_OK;
-    };
-    switch (g.bits * 2 + (bf ? 1 : 0)) {
-      case 4 * 2: return ek(proj_epilogue_kernel<4, false>);
-      case 4 * 2 + 1: return ek(proj_epilogue_kernel<4, true>);
-      case 8 * 2: return ek(proj_epilogue_kernel<8, false>);
-      default: return ek(proj_epilogue_kernel<8, true>);
-    }
+    // one warp per finish unit while they fit a CTA and its shared memory
+    if (fu <= 32 && (size_t)(fu + 1) * D * sizeof(float) <= 48 * 1024)
+      return launch_epilogue_warp(p, g.bits, bf, st);
+    return block_epilogue();
   }
-  const dim3 g1(ns, 2 * Hkv, (p.R + proj_rows(p.R) - 1) / proj_rows(p.R));
+  const dim3 g1(ns, units, (p.R + proj_rows(p.R) - 1) / proj_rows(p.R));
   const int RC = proj_rows(p.R);
-  const int wmax = std::max(a.wk.gs, a.v_from_k ? 0 : a.wv.gs);
+  int wmax = 0;
+  for (int i = 0; i < nproj; i++) wmax = std::max(wmax, pw[i]->gs);
   const size_t smem = (size_t)RC * wmax * sizeof(float);
   rc = a.wk.bits == 4 ? (bf ? partial_for<4, true>(RC, g1, threads, smem, st, p)
                             : partial_for<4, false>(RC, g1, threads, smem, st, p))
                       : (bf ? partial_for<8, true>(RC, g1, threads, smem, st, p)
                             : partial_for<8, false>(RC, g1, threads, smem, st, p));
   if (rc) return rc;
-  const dim3 g2(p.R, 2 * Hkv);
-  auto ek = [&](auto kern) -> int32_t {
-    KVQ_CUDA_TRY(launch_pdl(kern, g2, dim3(threads), 0, st, p));
-    return KVQ_OK;
-  };
-  switch (g.bits * 2 + (bf ? 1 : 0)) {
-    case 4 * 2: return ek(proj_epilogue_kernel<4, false>);
-    case 4 * 2 + 1: return ek(proj_epilogue_kernel<4, true>);
-    case 8 * 2: return ek(proj_epilogue_kernel<8, false>);
-    default: return ek(proj_epilogue_kernel<8, true>);
-  }
+  return block_epilogue();
 }
 
 }  // namespace kvq

@@ -69,7 +69,8 @@ class KvProjection(ctypes.Structure):
                 ("norm_eps", ctypes.c_float), ("rope_dims", ctypes.c_int32),
                 ("rope_traditional", ctypes.c_int32), ("rope_base", ctypes.c_float),
                 ("rope_scale", ctypes.c_float), ("rope_pre_scale", ctypes.c_float),
-                ("rope_freqs", ctypes.c_void_p)]
+                ("rope_freqs", ctypes.c_void_p), ("q_proj", QLinear), ("q_heads", ctypes.c_int32),
+                ("q_norm", ctypes.c_int32), ("q_norm_weight", ctypes.c_void_p)]
 
 
 _lib = None
@@ -121,7 +122,7 @@ def lib():
                                        P(vp)]),
         "kvq_cache_export": (i32, [vp, i64, P(vp), vp]),
         "kvq_cache_import": (i32, [P(Desc), P(vp), i32, i64, i64, vp, P(vp)]),
-        "kvq_append_projected": (i32, [vp, vp, i32, P(KvProjection), vp, vp, vp,
+        "kvq_append_projected": (i32, [vp, vp, i32, P(KvProjection), vp, vp, vp, vp,
                                        ctypes.c_size_t, vp]),
         "kvq_append_projected_workspace": (i32, [vp, i32, P(KvProjection),
                                                  P(ctypes.c_size_t)]),

@@ -171,11 +171,11 @@ class _CacheBase:
             raise ValueError("k/v shape, dtype or device differ from the cache's")
 
     def update_and_fetch_projected(self, x: torch.Tensor, proj, k_out=None, v_out=None,
-                                   stream=None):
-        """Fused K/V projection + norms + RoPE + append of x [B, L, hidden]
-        (kvq_append_projected; see kvq.project)."""
+                                   stream=None, q_out=None):
+        """Fused K/V (and Q) projection + norms + RoPE + append of x [B, L,
+        hidden] (kvq_append_projected; see kvq.project)."""
         from .project import append_projected
-        return append_projected(self, x, proj, k_out, v_out, stream)
+        return append_projected(self, x, proj, k_out, v_out, stream, q_out)
 
     def update_and_fetch_quantized(self, k: torch.Tensor, v: torch.Tensor, stream=None):
         """Quantize k, v ([B, H, S, D], any strides with unit d stride) into the

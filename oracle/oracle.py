@@ -562,3 +562,29 @@ def project_kv(x: np.ndarray, proj: dict, offset: int, dtype: int):
                  proj.get("rope_base"), proj.get("rope_scale", 1.0), offset,
                  proj.get("rope_freqs"), dtype)
     return np.ascontiguousarray(k), np.ascontiguousarray(v)
+
+
+def project_q(x: np.ndarray, proj: dict, offset: int, dtype: int) -> np.ndarray:
+    """The query rows [B, Hq, L, D] of x [B, L, hidden] (Attention.forward,
+    src/model/gemma4.ts:224-226 and q's rope, generated/gemma4-12b.ts:
+    73-74): q = rope(q_norm(q_proj(x))) with K's RoPE parameters.  proj as
+    for project_kv plus q_proj = (packed, scales, biases, group_size, bits),
+    q_norm (bool), q_norm_weight (f32 or None)."""
+    B, L, _ = x.shape
+    D = proj["head_dim"]
+    q = quantized_linear(x, *proj["q_proj"], dtype)
+    H = q.shape[-1] // D
+    q = q.reshape(B, L, H, D).transpose(0, 2, 1, 3)
+    if proj.get("q_norm"):
+        q = rms_norm(q, proj.get("q_norm_weight"), proj["eps"], dtype)
+    if proj.get("rope_dims", 0):
+        pre = proj.get("rope_pre_scale", 1.0)
+        if pre not in (0.0, 1.0):
+            dims = proj["rope_dims"]
+            q = q.copy()
+            q[..., :dims] = round_dt(q[..., :dims] * round_dt(np.array([pre], np.float32),
+                                                              dtype)[0], dtype)
+        q = rope(q, proj["rope_dims"], proj.get("rope_traditional", False),
+                 proj.get("rope_base"), proj.get("rope_scale", 1.0), offset,
+                 proj.get("rope_freqs"), dtype)
+    return np.ascontiguousarray(q)

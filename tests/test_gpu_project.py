@@ -11,7 +11,9 @@
 * Projection parity: random inputs and oracle-quantized weights (4 / 8
   bit, group 32 / 64 / 128, with biases), K RMSNorm with weight, V RMSNorm
   without (gemma4.ts:174-177), default / proportional / partial-traditional
-  RoPE, attention_k_eq_v, fp16 and bf16, batch 1 / 4 / 2 / 1 / 1 / 3 with
+  RoPE, attention_k_eq_v, the query side (its projection, q_norm and RoPE
+  into q_out; the decode then reads the fused query rows), fp16 and bf16,
+  batch 1 / 4 / 2 / 1 / 1 / 3 with
   1 / 1 / 37 / 20 / 300 / 70 rows (the one-launch cluster path at 1 and 4
   rows; the tensor-core projection + epilogue pair beyond, with partial
   128-row and 64-token tiles): the rows before
@@ -152,6 +154,8 @@ CASES = [
     (BF16, 4, 64, 4, 64, 1, 300, 4, 128, 1024, False, "default"),
     (F16, 4, 32, 8, 32, 3, 70, 2, 64, 2048, True, "proportional"),
 ]
+# query heads of the cases that also run the query side (the rest: none)
+QHEADS = {0: 16, 1: 8, 2: 4, 4: 8, 5: 4}
 
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"{'f16' if c[0] == F16 else 'bf16'}"
@@ -177,10 +181,18 @@ def test_fused_projection_matches_oracle(case):
         fr_dev = torch.from_numpy(fr).cuda()
     else:
         spec.update(rope_dims=D // 2, rope_traditional=True, rope_base=500000.0)
+    Hq = QHEADS.get(CASES.index(case), 0)
+    qkw = {}
+    if Hq:
+        qq, q_or = make_qlinear(rng, Hq * D, hidden, wgs, wbits, dt)
+        qw = O.round_dt(rng.uniform(0.5, 1.5, D).astype(np.float32), dt)
+        spec.update(q_proj=q_or, q_norm=True, q_norm_weight=qw)
+        qkw = dict(q_proj=qq, q_heads=Hq, q_norm=True,
+                   q_norm_weight=_dev_bits(O.to_dtype_bits(qw, dt), dt))
     proj = kvq.KvProjection(kq, vq, D, k_norm=True, k_norm_weight=kw_dev, v_norm=True, eps=1e-6,
                             rope_dims=spec["rope_dims"],
                             rope_traditional=spec.get("rope_traditional", False),
-                            rope_base=spec.get("rope_base", 10000.0), rope_freqs=fr_dev)
+                            rope_base=spec.get("rope_base", 10000.0), rope_freqs=fr_dev, **qkw)
     cache = kvq.QuantizedKVCache(kvgs, kvbits)
     oc = O.QuantizedKVCache(kvgs, kvbits, dt)
     offset = 0
@@ -188,9 +200,14 @@ def test_fused_projection_matches_oracle(case):
         x = O.to_dtype_bits(rng.uniform(-1, 1, (B, n, hidden)).astype(np.float32), dt)
         k_out = torch.empty(B, H, n, D, dtype=tdt, device="cuda")
         v_out = torch.empty_like(k_out)
-        K, V = cache.update_and_fetch_projected(_dev_bits(x, dt), proj, k_out=k_out, v_out=v_out)
+        q_out = torch.empty(B, Hq, n, D, dtype=tdt, device="cuda") if Hq else None
+        K, V = cache.update_and_fetch_projected(_dev_bits(x, dt), proj, k_out=k_out, v_out=v_out,
+                                                q_out=q_out)
         torch.cuda.synchronize()
         want_k, want_v = O.project_kv(O.from_dtype_bits(x, dt), spec, offset, dt)
+        if Hq:
+            want_q = O.project_q(O.from_dtype_bits(x, dt), spec, offset, dt)
+            check_rows(from_torch(q_out, dt), want_q, dt, f"fused projection Q {case[11]} step {step}")
         kb, vb = from_torch(k_out, dt), from_torch(v_out, dt)
         check_rows(kb, want_k, dt, f"fused projection K {case[11]} step {step}")
         check_rows(vb, want_v, dt, f"fused projection V {case[11]} step {step}")
@@ -198,11 +215,15 @@ def test_fused_projection_matches_oracle(case):
         offset += n
         assert cache.offset == offset
         _cache_rows_match(K, V, oc, offset, f"cache rows step {step}")
-    # attention over the cache the fused path filled
-    Hq = 2 * H
-    q = O.to_dtype_bits(rng.standard_normal((B, Hq, 1, D)).astype(np.float32), dt)
+    # attention over the cache the fused path filled: with the query side,
+    # the last step's fused query rows (the oracle's own query for the oracle)
     scale = 1.0 / np.sqrt(D)
-    o = kvq.sdpa_decode(_dev_bits(q, dt), K, V, scale)
+    if Hq:
+        q = O.to_dtype_bits(want_q, dt)
+        o = kvq.sdpa_decode(q_out, K, V, scale)
+    else:
+        q = O.to_dtype_bits(rng.standard_normal((B, 2 * H, 1, D)).astype(np.float32), dt)
+        o = kvq.sdpa_decode(_dev_bits(q, dt), K, V, scale)
     want = O.sdpa_unfused(q, *oc.fetch(), scale, kvgs, kvbits, dt)
     got = from_torch(o, dt)
     record_parity(f"decode after fused append {case[11]}", got, want, dt, f"<= {TOL[dt]}")
@@ -294,10 +315,10 @@ def test_caller_workspace_sized_by_query():
     ws = torch.zeros(n.value, dtype=torch.uint8, device="cuda")
     k_out = torch.empty_like(k_ref)
     st = torch.cuda.current_stream().cuda_stream
-    rc = lib.kvq_append_projected(cache._h, x.data_ptr(), L, ctypes.byref(s), k_out.data_ptr(),
-                                  None, ws.data_ptr(), n.value - 1, st)
+    rc = lib.kvq_append_projected(cache._h, x.data_ptr(), L, ctypes.byref(s), None,
+                                  k_out.data_ptr(), None, ws.data_ptr(), n.value - 1, st)
     assert rc == _lib.ERR_WORKSPACE
-    _lib.check(lib.kvq_append_projected(cache._h, x.data_ptr(), L, ctypes.byref(s),
+    _lib.check(lib.kvq_append_projected(cache._h, x.data_ptr(), L, ctypes.byref(s), None,
                                         k_out.data_ptr(), None, ws.data_ptr(), n.value, st))
     torch.cuda.synchronize()
     assert torch.equal(k_out.view(torch.int16), k_ref.view(torch.int16))

@@ -103,17 +103,20 @@ def test_struct_layout_matches_the_header(tmp_path):
     from kvq import _lib
     src = tmp_path / "sz.c"
     src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "kvq.h"\n'
-                   'int main(void){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(kvq_qlinear),'
+                   'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(kvq_qlinear),'
                    ' sizeof(kvq_kv_projection), offsetof(kvq_kv_projection, k_norm_weight),'
                    ' offsetof(kvq_kv_projection, norm_eps), offsetof(kvq_kv_projection,'
-                   ' rope_pre_scale), offsetof(kvq_kv_projection, rope_freqs)); return 0;}\n')
+                   ' rope_pre_scale), offsetof(kvq_kv_projection, rope_freqs),'
+                   ' offsetof(kvq_kv_projection, q_proj), offsetof(kvq_kv_projection,'
+                   ' q_norm_weight)); return 0;}\n')
     exe = tmp_path / "sz"
     inc = os.path.join(os.path.dirname(HERE), "include")
     subprocess.check_call(["gcc", "-I", inc, str(src), "-o", str(exe)])
     got = [int(v) for v in subprocess.check_output([str(exe)]).split()]
     P = _lib.KvProjection
     assert got == [ctypes.sizeof(_lib.QLinear), ctypes.sizeof(P), P.k_norm_weight.offset,
-                   P.norm_eps.offset, P.rope_pre_scale.offset, P.rope_freqs.offset]
+                   P.norm_eps.offset, P.rope_pre_scale.offset, P.rope_freqs.offset,
+                   P.q_proj.offset, P.q_norm_weight.offset]
 
 
 def test_rms_norm_known_answers():
@@ -178,7 +181,8 @@ def test_append_projected_rejects_malformed_projection(field, value, needle):
         rc = lib.kvq_append_projected_workspace(h, 1, ctypes.byref(s), ctypes.byref(n))
         assert rc == _lib.ERR_ARG
         assert needle in lib.kvq_last_error().decode()
-        rc = lib.kvq_append_projected(h, 64, 1, ctypes.byref(s), None, None, None, 0, None)
+        rc = lib.kvq_append_projected(h, 64, 1, ctypes.byref(s), None, None, None, None, 0,
+                                      None)
         assert rc == _lib.ERR_ARG
     finally:
         assert lib.kvq_cache_free(h) == 0
@@ -199,7 +203,7 @@ def test_append_projected_rejects_mismatched_v_proj_and_head_dim():
         s.v_proj = _lib.QLinear(16, 32, 0, 4, 64, 512, 256)  # in_features differ
         assert lib.kvq_append_projected_workspace(h, 1, ctypes.byref(s), ctypes.byref(n)) == \
             _lib.ERR_ARG
-        assert lib.kvq_append_projected(None, 64, 1, ctypes.byref(s), None, None, None, 0,
+        assert lib.kvq_append_projected(None, 64, 1, ctypes.byref(s), None, None, None, None, 0,
                                         None) == _lib.ERR_ARG
     finally:
         assert lib.kvq_cache_free(h) == 0
@@ -212,3 +216,32 @@ def test_append_projected_rejects_mismatched_v_proj_and_head_dim():
         assert "head_dim" in lib.kvq_last_error().decode()
     finally:
         assert lib.kvq_cache_free(h2) == 0
+
+
+def test_append_projected_rejects_malformed_query_side():
+    from kvq import _lib
+    lib = _lib.lib()
+    h = _cache(lib, _lib.Desc)  # 2 kv heads of 128
+    try:
+        n = ctypes.c_size_t()
+        s = _proj(_lib)
+        s.q_proj = _lib.QLinear(16, 32, 0, 4, 64, 256, 512)
+        s.q_heads = 0  # a query projection needs its heads
+        assert lib.kvq_append_projected_workspace(h, 1, ctypes.byref(s), ctypes.byref(n)) == \
+            _lib.ERR_ARG
+        assert "q_heads" in lib.kvq_last_error().decode()
+        s.q_heads = 3  # 3 x 128 != 512 output features
+        assert lib.kvq_append_projected_workspace(h, 1, ctypes.byref(s), ctypes.byref(n)) == \
+            _lib.ERR_ARG
+        assert "q_proj" in lib.kvq_last_error().decode()
+        s.q_heads = 4
+        s.q_proj = _lib.QLinear(16, 32, 0, 4, 64, 512, 512)  # in_features differ from k_proj's
+        assert lib.kvq_append_projected_workspace(h, 1, ctypes.byref(s), ctypes.byref(n)) == \
+            _lib.ERR_ARG
+        s.q_proj = _lib.QLinear(16, 32, 0, 4, 64, 256, 512)
+        # a well-formed query side, but no q_out: refused before any CUDA call
+        assert lib.kvq_append_projected(h, 64, 1, ctypes.byref(s), None, None, None, None, 0,
+                                        None) == _lib.ERR_ARG
+        assert "q_out" in lib.kvq_last_error().decode()
+    finally:
+        assert lib.kvq_cache_free(h) == 0
