@@ -35,10 +35,11 @@ context_split
            graph per pass over the layers), us per step and the exchange's
            share of it.
 kv_projection
-           nested: the fused K/V projection + RMSNorms + RoPE + quantize-on-
-           append of one decode token through 48 Gemma-4-12B sliding-layer
-           K/V weight sets (hidden 3840 -> 8 x 256, 4-bit), one replica per
-           GPU, with its HBM roofline; and a 512-token prefill chunk.
+           nested: the fused Q/K/V projection + RMSNorms + RoPE + quantize-
+           on-append of one decode token through 48 Gemma-4-12B sliding-layer
+           weight sets (hidden 3840 -> 16 query + 2 x 8 kv heads of 256,
+           4-bit), one replica per GPU, with its HBM roofline; and a
+           512-token prefill chunk.
 cpu_baseline / --impl reference
            the CPU oracle (C restatement of mlx-bun's unfused op graph) with
            every host core, on a bounded sample of config 5's (sequence, kv
@@ -701,36 +702,44 @@ def run_prefill(args, bits=8):
         "gpu_launches": 3 * reps * NL, "clocks": t1.clk}))
 
 
-# ------------------------------------------- fused K/V projection --
+# ------------------------------------------- fused Q/K/V projection --
 
-# Gemma-4-12B sliding-attention layer K/V side: hidden 3840 -> 8 kv heads x
-# 256, 4-bit group-64 weights with biases, bf16 activations, K RMSNorm with
-# weight, V RMSNorm without, default RoPE (base 10000) on all 256 dims, a
-# kv4 group-64 cache; 48 layers, as the model has.
-CFGP = dict(hidden=3840, Hkv=8, D=256, wbits=4, wgs=64, bits=4, gs=64, layers=48, chunk=512)
+# Gemma-4-12B sliding-attention layer, query and K/V sides: hidden 3840 ->
+# 16 query heads and 8 kv heads of 256, 4-bit group-64 weights with biases,
+# bf16 activations, Q and K RMSNorm with weights, V RMSNorm without, default
+# RoPE (base 10000) on all 256 dims of Q and K, a kv4 group-64 cache; 48
+# layers, as the model has.
+CFGP = dict(hidden=3840, Hq=16, Hkv=8, D=256, wbits=4, wgs=64, bits=4, gs=64, layers=48,
+            chunk=512)
+
+
+def projection_out_features(c):
+    """Output features of one call: Q, K and V."""
+    return (c["Hq"] + 2 * c["Hkv"]) * c["D"]
 
 
 def projection_bytes(c, rows):
-    """Algorithmic HBM bytes of one fused call over `rows` token rows: K and
-    V weight triples (packed codes + bf16 scales and biases), the bf16 input
-    rows, and the quantized K/V rows written to the cache."""
-    out, inn = c["Hkv"] * c["D"], c["hidden"]
-    w = 2 * (out * inn * c["wbits"] // 8 + 2 * out * (inn // c["wgs"]) * 2)
+    """Algorithmic HBM bytes of one fused call over `rows` token rows: the
+    Q, K and V weight triples (packed codes + bf16 scales and biases), the
+    bf16 input rows, the bf16 query rows written out and the quantized K/V
+    rows written to the cache."""
+    out, inn = projection_out_features(c), c["hidden"]
+    w = out * inn * c["wbits"] // 8 + 2 * out * (inn // c["wgs"]) * 2
     x = rows * inn * 2
+    q = rows * c["Hq"] * c["D"] * 2
     row = c["D"] * c["bits"] // 8 + 2 * (c["D"] // c["gs"]) * 2
-    return w + x + 2 * rows * c["Hkv"] * row
+    return w + x + q + 2 * rows * c["Hkv"] * row
 
 
 def projection_layers(c, n, device, g):
-    """`n` layers of random 4-bit K/V projection weights (codes uniform,
+    """`n` layers of random 4-bit Q/K/V projection weights (codes uniform,
     scales U[0.001, 0.005], biases -7.5 x scale: outputs of order one) with
     their growing kv caches."""
     import torch
     import kvq
     H, D, hid = c["Hkv"], c["D"], c["hidden"]
-    out_f = H * D
 
-    def qlinear():
+    def qlinear(out_f):
         words = hid * c["wbits"] // 32
         packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (out_f, words), generator=g,
                                device=device, dtype=torch.int32)
@@ -738,42 +747,53 @@ def projection_layers(c, n, device, g):
         bi = -7.5 * sc
         return kvq.QuantizedLinear(packed, sc.bfloat16(), bi.bfloat16(), c["wgs"], c["wbits"])
 
+    def norm_w():
+        return (torch.rand(D, generator=g, device=device) + 0.5).bfloat16()
+
     layers = []
     for _ in range(n):
-        proj = kvq.KvProjection(qlinear(), qlinear(), D,
-                                k_norm_weight=(torch.rand(D, generator=g, device=device) + 0.5)
-                                .bfloat16(), rope_dims=D, rope_base=10000.0)
+        proj = kvq.KvProjection(qlinear(H * D), qlinear(H * D), D, k_norm_weight=norm_w(),
+                                rope_dims=D, rope_base=10000.0, q_proj=qlinear(c["Hq"] * D),
+                                q_heads=c["Hq"], q_norm_weight=norm_w())
         cache = kvq.QuantizedKVCache(c["gs"], c["bits"], reserve_rows=2048)
         layers.append(dict(proj=proj, cache=cache))
     return layers
 
 
+def projection_q_out(c, tokens, device):
+    """The query rows' buffer of one call over `tokens` tokens."""
+    import torch
+    return torch.empty(1, c["Hq"], tokens, c["D"], dtype=torch.bfloat16, device=device)
+
+
 def run_kv_projection(args, rank, world, local_rank):
-    """Fused K/V projection + norms + RoPE + quantize-on-append
+    """Fused Q/K/V projection + norms + RoPE + quantize-on-append
     (kvq_append_projected), one replica per GPU.  Decode: one token per
     step through each of the 48 layers (a CUDA graph per pass over the
-    layers; 425 MB of weights cycled, above L2), timed with CUDA events.
+    layers; 850 MB of weights cycled, above L2), timed with CUDA events.
     Prefill: one 512-token chunk through one layer, timed the same way
-    (FLOPs: 2 x tokens x hidden x (K + V output features))."""
+    (FLOPs: 2 x tokens x hidden x (Q + K + V output features))."""
     import torch
     c = CFGP
     device = torch.device("cuda", local_rank)
     hid = c["hidden"]
-    out_f = c["Hkv"] * c["D"]
+    out_f = projection_out_features(c)
     g = torch.Generator(device=device)
     g.manual_seed(2000 + rank)
     layers = projection_layers(c, c["layers"], device, g)
     x1 = torch.randn(1, 1, hid, generator=g, device=device).bfloat16()
     xc = torch.randn(1, c["chunk"], hid, generator=g, device=device).bfloat16()
+    q1, qc, q0 = (projection_q_out(c, n, device) for n in (1, c["chunk"], 1000))
     # every cache starts at offset 1000 (positions in range of a real decode)
     for Ly in layers:
         Ly["cache"].update_and_fetch_projected(torch.zeros(1, 1000, hid, device=device,
-                                                           dtype=torch.bfloat16), Ly["proj"])
+                                                           dtype=torch.bfloat16), Ly["proj"],
+                                               q_out=q0)
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device)
 
     def step(Ly, x):
-        Ly["cache"].update_and_fetch_projected(x, Ly["proj"])
+        Ly["cache"].update_and_fetch_projected(x, Ly["proj"], q_out=q1 if x.shape[1] == 1 else qc)
         Ly["cache"].trim(x.shape[1])  # host bookkeeping: every replay writes the same rows
 
     with torch.cuda.stream(stream):
@@ -808,12 +828,12 @@ def run_kv_projection(args, rank, world, local_rank):
     nb = projection_bytes(c, 1)
     achieved = nb / dec_s / 1e9
     peak, peak_kind = peaks()
-    flops = 2 * c["chunk"] * hid * 2 * out_f
+    flops = 2 * c["chunk"] * hid * out_f
     ratio = traffic_ratio("kv_projection_decode.md")
     res = {
-        "workload": "gemma4-12b-sliding-kv-projection: hidden 3840 -> Hkv8 x D256, 4-bit gs64 "
-                    "weights, K RMSNorm+RoPE, V RMSNorm, kv4 gs64 cache; one replica per GPU "
-                    "(weak)",
+        "workload": "gemma4-12b-sliding-qkv-projection: hidden 3840 -> Hq16 + Hkv8 + Hkv8 x "
+                    "D256, 4-bit gs64 weights, Q and K RMSNorm+RoPE, V RMSNorm, kv4 gs64 "
+                    "cache; one replica per GPU (weak)",
         "decode": {"us_per_layer": round(dec_s * 1e6, 3), "layers_cycled": NL,
                    "steps": reps * NL, "bytes_per_layer": nb,
                    "value": round(world * nb / dec_s / 1e9, 1), "unit": UNIT,
@@ -824,10 +844,10 @@ def run_kv_projection(args, rank, world, local_rank):
                                      "exact fp16 operands) + proj_epilogue_warp_kernel"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "kernel": "proj_partial_kernel<4,bf16,1> + proj_epilogue_kernel<4,bf16>",
+                     "kernel": "proj_cluster_kernel<4,4,bf16,1,16> (one launch per layer)",
                      "kernel_us": round(dec_s * 1e6, 3), "bytes_per_launch": nb,
                      "traffic": int(ratio * nb) if ratio else None},
-        "gpu_launches": 2 * reps * NL,
+        "gpu_launches": reps * NL,
     }
     del g_dec, g_pre
     for Ly in layers:
@@ -840,12 +860,12 @@ def print_kv_projection(args):
     torch.cuda.set_device(0)
     r = run_kv_projection(args, 0, 1, 0)
     print(json.dumps({
-        "metric": "fused K/V projection + norms + RoPE + quantize-on-append achieved HBM GB/s "
+        "metric": "fused Q/K/V projection + norms + RoPE + quantize-on-append achieved HBM GB/s "
                   "(decode, Gemma-4-12B sliding-layer shapes)",
         "value": r["decode"]["value"], "unit": UNIT, "n_gpus": 1, "steps": r["decode"]["steps"],
         "warmup": args.warmup, "ms_per_step": round(r["decode"]["us_per_layer"] / 1e3, 6),
         "higher_is_better": True, "dtype": "u4 weights/bf16", "data": "synthetic (seeded torch)",
-        "config": {"workload": r["workload"], "l2": "48 distinct layers (425 MB of weights) "
+        "config": {"workload": r["workload"], "l2": "48 distinct layers (850 MB of weights) "
                    "per replay"},
         "roofline": r["roofline"], "prefill_chunk": r["prefill_chunk"],
         "gpu_launches": r["gpu_launches"]}))
@@ -963,11 +983,12 @@ def profile_run(args):
     g.manual_seed(7)
     if args.profile == "projection":
         c = CFGP
-        layers = projection_layers(c, 24, device, g)  # 213 MB of weights, above L2
+        layers = projection_layers(c, 24, device, g)  # 425 MB of weights, above L2
         x1 = torch.randn(1, 1, c["hidden"], generator=g, device=device).bfloat16()
+        q1 = projection_q_out(c, 1, device)
         for i in range(args.steps):
             Ly = layers[i % 24]
-            Ly["cache"].update_and_fetch_projected(x1, Ly["proj"])
+            Ly["cache"].update_and_fetch_projected(x1, Ly["proj"], q_out=q1)
             Ly["cache"].trim(1)
         torch.cuda.synchronize()
         print(json.dumps({"profile": "projection", "launches": args.steps,
@@ -977,14 +998,15 @@ def profile_run(args):
         c = CFGP
         layers = projection_layers(c, 2, device, g)
         xc = torch.randn(1, c["chunk"], c["hidden"], generator=g, device=device).bfloat16()
+        qc = projection_q_out(c, c["chunk"], device)
         for i in range(args.steps):
             Ly = layers[i % 2]
-            Ly["cache"].update_and_fetch_projected(xc, Ly["proj"])
+            Ly["cache"].update_and_fetch_projected(xc, Ly["proj"], q_out=qc)
             Ly["cache"].trim(c["chunk"])
         torch.cuda.synchronize()
         print(json.dumps({"profile": "projection-prefill", "launches": args.steps,
-                          "flops_per_launch": 2 * c["chunk"] * c["hidden"] * 2 * c["Hkv"] *
-                          c["D"]}))
+                          "flops_per_launch": 2 * c["chunk"] * c["hidden"] *
+                          projection_out_features(c)}))
         return
     if args.profile == "config5":
         c = CFG5
