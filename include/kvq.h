@@ -129,8 +129,8 @@ typedef struct kvq_qlinear {
   int32_t in_features, out_features;
 } kvq_qlinear;
 
-/* The K/V side of one attention layer ahead of its cache (Attention.forward,
- * src/model/gemma4.ts:234-268):
+/* The K/V side of one attention layer ahead of its cache, and optionally its
+ * query side (q_proj below) (Attention.forward, src/model/gemma4.ts:234-268):
  *   k = k_proj(x); v = v_from_k ? k : v_proj(x)   (attention_k_eq_v)
  *   k = rope(k_norm(k), offset); v = v_norm(v)
  * with out_features = kv_heads * head_dim.  k_norm / v_norm: apply RMSNorm

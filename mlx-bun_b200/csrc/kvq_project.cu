@@ -1,13 +1,15 @@
-// kvq_project.cu — the step before the append, fused: K/V projection of the
-// layer input through MLX affine-quantized weights, the K and V RMSNorms,
-// RoPE of K at the cache position, and the quantize-on-append into the
-// cache rows the cache's state machine picks.  Replaces mlx-bun's
-//   k = kProj(x); v = vProj(x) (or k, attention_k_eq_v);
+// kvq_project.cu — the step before the append, fused: K/V (and Q)
+// projection of the layer input through MLX affine-quantized weights, the
+// K, V (and Q) RMSNorms, RoPE of K (and Q) at the cache position, the
+// quantize-on-append of K and V into the cache rows the cache's state
+// machine picks, and the query rows into the caller's buffer.  Replaces
+// mlx-bun's
+//   q = qNorm(qProj(x)); k = kProj(x); v = vProj(x) (or k, attention_k_eq_v);
 //   k = rope(kNorm(k), offset); v = vNorm(v);
-//   cache.updateAndFetchQuantized(k, v)
-// (src/model/gemma4.ts:234-268; QuantizedLinear.forward,
-// src/model/gemma4-base.ts:120-157; generated/gemma4-12b.ts:52-66), which
-// runs as a quantized matmul per projection, two norms, a rope, two
+//   cache.updateAndFetchQuantized(k, v); q = rope(transpose(q), offset)
+// (src/model/gemma4.ts:224-268; QuantizedLinear.forward,
+// src/model/gemma4-base.ts:120-157; generated/gemma4-12b.ts:52-74), which
+// runs as a quantized matmul per projection, three norms, two ropes, three
 // transposes and two quantize dispatches.
 //
 // Two launches, chained by programmatic dependent launch:
