@@ -844,7 +844,7 @@ def run_kv_projection(args, rank, world, local_rank):
                                      "exact fp16 operands) + proj_epilogue_warp_kernel"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "kernel": "proj_cluster_kernel<4,4,bf16,1,16> (one launch per layer)",
+                     "kernel": "proj_cluster_kernel<4,4,bf16,1,8> (one launch per layer)",
                      "kernel_us": round(dec_s * 1e6, 3), "bytes_per_launch": nb,
                      "traffic": int(ratio * nb) if ratio else None},
         "gpu_launches": reps * NL,

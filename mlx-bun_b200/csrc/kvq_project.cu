@@ -1100,14 +1100,24 @@ static int32_t launch_cluster_dt(const PP& p, bool bf, int cs, int RC, int units
             : launch_cluster<WBITS, BITS, false, 8>(p, RC, units, smem, st);
 }
 
-static int current_cluster_size() {
-  int dev = 0;
+// The cluster size of one launch: the device's (16 where it holds such
+// clusters), down to 8 when 16-CTA clusters of every compute unit and row
+// chunk would not all be resident at once (two CTAs per SM) and 8-CTA
+// clusters can take the launch.
+static int launch_cluster_size(const ProjArgs& a, int Hkv) {
+  int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess) return 8;
-  return cluster_size(dev);
+  int cs = cluster_size(dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int R = a.B * a.L, chunks = R <= 1 ? 1 : (R + 3) / 4;
+  if (cs > 8 && (int64_t)compute_units(a, Hkv) * chunks * cs > 2 * (int64_t)sms &&
+      use_cluster(a, 8))
+    cs = 8;
+  return cs;
 }
 
 size_t project_workspace_bytes(const ProjArgs& a, int Hkv, int D, int* splits) {
-  const int cs = current_cluster_size();
+  const int cs = launch_cluster_size(a, Hkv);
   if (use_cluster(a, cs)) {
     if (splits) *splits = cs;
     return 0;
@@ -1239,7 +1249,7 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
       default: return ek(proj_epilogue_kernel<8, true>);
     }
   };
-  const int cs = current_cluster_size();
+  const int cs = launch_cluster_size(a, Hkv);
   if (use_cluster(a, cs)) {
     const int RC = p.R <= 1 ? 1 : 4;
     // the largest slice of any projection, in elements
