@@ -92,6 +92,7 @@ struct PP {
   TripleView dk, dv;
   int64_t dst_row0;
   int bits, gs;       // cache quantisation
+  int nb2;            // cluster path: weight loads per thread staged in shared memory
 };
 
 __device__ __forceinline__ int units_of(const PP& p) { return p.Hkv + p.nv + p.nq; }
@@ -474,10 +475,20 @@ __global__ void __launch_bounds__(1024) proj_epilogue_warp_kernel(const PP p) {
   }
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool full) {
+  const uint32_t d = attn::smem_u32(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src),
+               "r"(full ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // Decode-sized steps (R <= 4 rows): one launch.  A cluster of CS CTAs per
 // (K|V, kv head, row chunk) splits the hidden dimension; thread o owns
 // output column o.  Each thread first issues everything it will read —
-// its weight-row slice (16-byte loads), its group scales and biases, the
+// its weight-row slice (16-byte loads: the first kNB into registers, up to
+// nb2 more by cp.async into shared memory), its group scales and biases, the
 // norm weight and the RoPE table before the dependency wait, its share of
 // the input slice after it — then stages the inputs in shared memory and
 // accumulates per group
@@ -491,6 +502,7 @@ __global__ void __launch_bounds__(1024) proj_epilogue_warp_kernel(const PP p) {
 // resident (waiting on the dependency) before this step ends.
 constexpr int kMaxG = 8;    // weight groups per CTA
 constexpr int kNB = 8;      // 16-byte weight loads per thread issued up front
+constexpr int kNB2 = 8;     // further ones staged in shared memory (up to 32 KB per CTA)
 
 // Codes as floats by one byte permute each (byte K of `w` into the float's
 // bits, exponent byte 0x4B above it):
@@ -517,7 +529,7 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float row[256];
   __shared__ float red[32];
-  extern __shared__ float sm[];  // part[RC][D], sumx[RC][kMaxG], xs[RC][span]
+  extern __shared__ __align__(16) float sm[];  // wsm[nb2][D], part[RC][D], sumx[RC][kMaxG], xs[RC][span]
   const int rank = (int)cluster.block_rank();
   int sel, h;
   unit_of(p, blockIdx.y, sel, h);
@@ -526,8 +538,9 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
   const int G = p.hidden / w.gs, gs = w.gs;
   const int g0 = rank * G / CS, g1 = (rank + 1) * G / CS, ng = g1 - g0;
   const int span = ng * gs;
-  float* part = sm;
-  float* sumx = sm + RC * D;
+  uint4* wsm = reinterpret_cast<uint4*>(sm);
+  float* part = sm + p.nb2 * D * 4;
+  float* sumx = part + RC * D;
   float* xs = sumx + RC * kMaxG;
   const int r0 = blockIdx.z * RC, nr = min(RC, p.R - r0);
   constexpr int PER = 32 / WBITS;
@@ -544,6 +557,11 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
   uint4 q[kNB];
 #pragma unroll
   for (int j = 0; j < kNB; j++) q[j] = j < n4 ? __ldg(wp + j) : make_uint4(0, 0, 0, 0);
+  const int nb2 = max(0, min(n4 - kNB, p.nb2));
+#pragma unroll
+  for (int j = 0; j < kNB2; j++)
+    if (j < nb2) cp_async16(wsm + j * D + o, wp + kNB + j, true);
+  cp_async_commit();
   uint16_t sc16[kMaxG], bi16[kMaxG];
   const uint16_t* sp = w.scales + wrow * G + g0;
   const uint16_t* bp = w.biases ? w.biases + wrow * G + g0 : nullptr;
@@ -659,7 +677,9 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
     if (j >= n4) break;
     consume(q[j], j);
   }
-  for (int j = kNB; j < n4; j++) consume(__ldg(wp + j), j);
+  cp_async_wait<0>();  // this thread's own copies: visible to it past the wait
+  for (int j = 0; j < nb2; j++) consume(wsm[j * D + o], kNB + j);
+  for (int j = kNB + nb2; j < n4; j++) consume(__ldg(wp + j), j);
 #pragma unroll
   for (int r = 0; r < RC; r++) part[r * D + o] = out[r];
   cluster.sync();
@@ -789,15 +809,6 @@ __global__ void __launch_bounds__(256) proj_xprep_kernel(const PP p, uint8_t* xp
     *reinterpret_cast<uint4*>(dst + which * 16) = o;
   }
 }
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool full) {
-  const uint32_t d = attn::smem_u32(dst);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src),
-               "r"(full ? 16 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int WBITS, bool BF, int GS>
 __global__ void __launch_bounds__(256, 2) proj_mma_kernel(const PP p, const uint8_t* xp,
@@ -1256,7 +1267,18 @@ int32_t launch_project_append(const ProjArgs& a, int Hkv, RowGeom g, int dtype, 
     int span = 0;
     for (int i = 0; i < nproj; i++)
       span = std::max(span, (a.hidden / pw[i]->gs + cs - 1) / cs * pw[i]->gs);
-    const size_t smem = (size_t)RC * (D + kMaxG + span) * sizeof(float);
+    size_t smem = (size_t)RC * (D + kMaxG + span) * sizeof(float);
+    // weight loads per thread beyond the kNB held in registers: staged in
+    // shared memory by cp.async before the dependency wait, as many as fit
+    // the default 48 KB of dynamic shared memory
+    const int e4 = 4 * (32 / a.wk.bits);
+    int n4max = 0;
+    for (int i = 0; i < nproj; i++)
+      n4max = std::max(n4max, (a.hidden / pw[i]->gs + cs - 1) / cs * (pw[i]->gs / e4));
+    int nb2 = std::min(std::max(n4max - kNB, 0), kNB2);
+    while (nb2 > 0 && smem + (size_t)nb2 * D * 16 > 48 * 1024) nb2--;
+    p.nb2 = nb2;
+    smem += (size_t)nb2 * D * 16;
     switch ((a.wk.bits == 8 ? 2 : 0) + (g.bits == 8 ? 1 : 0)) {
       case 0: return launch_cluster_dt<4, 4>(p, bf, cs, RC, units, smem, st);
       case 1: return launch_cluster_dt<4, 8>(p, bf, cs, RC, units, smem, st);
