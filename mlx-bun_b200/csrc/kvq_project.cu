@@ -545,7 +545,8 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
   const int r0 = blockIdx.z * RC, nr = min(RC, p.R - r0);
   constexpr int PER = 32 / WBITS;
   constexpr int E4 = 4 * PER;            // elements per 16-byte load
-  const int u4pg = gs / E4;              // 16-byte loads per group
+  const int u4pg = gs / E4;              // 16-byte loads per group: 1, 2, 4 or 8
+  const int lg = __ffs(u4pg) - 1;        // log2(u4pg)
   const int n4 = ng * u4pg;
   const int64_t wrow = (int64_t)h * D + o;
   const uint4* wp = reinterpret_cast<const uint4*>(w.packed + wrow * (p.hidden / PER)) +
@@ -562,13 +563,16 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
   for (int j = 0; j < kNB2; j++)
     if (j < nb2) cp_async16(wsm + j * D + o, wp + kNB + j, true);
   cp_async_commit();
-  uint16_t sc16[kMaxG], bi16[kMaxG];
+  // (scale | bias << 16) of the slice's groups, in order: each group's fold
+  // takes sb[0] and shifts the rest down, so no index is computed
+  uint32_t sb[kMaxG];
   const uint16_t* sp = w.scales + wrow * G + g0;
   const uint16_t* bp = w.biases ? w.biases + wrow * G + g0 : nullptr;
 #pragma unroll
   for (int k = 0; k < kMaxG; k++) {
-    sc16[k] = k < ng ? __ldg(sp + k) : (uint16_t)0;
-    bi16[k] = (k < ng && bp) ? __ldg(bp + k) : (uint16_t)0;
+    const uint32_t s16 = k < ng ? __ldg(sp + k) : (uint16_t)0;
+    const uint32_t b16 = (k < ng && bp) ? __ldg(bp + k) : (uint16_t)0;
+    sb[k] = s16 | (b16 << 16);
   }
   RowConsts rcs[RC], rcv[RC];
   if (rank == 0) {
@@ -651,16 +655,12 @@ __global__ void __launch_bounds__(256, 2) proj_cluster_kernel(const PP p) {
         }
       }
     }
-    const int k = j / u4pg;
-    if (j - k * u4pg == u4pg - 1) {
-      uint16_t s16 = sc16[0], b16 = bi16[0];
+    if (((j + 1) & (u4pg - 1)) == 0) {  // the group's last load (u4pg: a power of two)
+      const int k = j >> lg;
+      const uint32_t v = sb[0];
 #pragma unroll
-      for (int t = 1; t < kMaxG; t++)
-        if (t == k) {
-          s16 = sc16[t];
-          b16 = bi16[t];
-        }
-      const float s = dt_to_f<BF>(s16), b = dt_to_f<BF>(b16);
+      for (int t = 0; t + 1 < kMaxG; t++) sb[t] = sb[t + 1];
+      const float s = dt_to_f<BF>((uint16_t)(v & 0xffffu)), b = dt_to_f<BF>((uint16_t)(v >> 16));
 #pragma unroll
       for (int r = 0; r < RC; r++) {
         const float sx = sumx[r * kMaxG + k];
