@@ -153,9 +153,16 @@ CASES = [
     (BF16, 8, 128, 4, 128, 1, 20, 2, 256, 1024, False, "partial-traditional"),
     (BF16, 4, 64, 4, 64, 1, 300, 4, 128, 1024, False, "default"),
     (F16, 4, 32, 8, 32, 3, 70, 2, 64, 2048, True, "proportional"),
+    # decode launches whose threads hold more than 8 weight loads: the
+    # Gemma-4-12B sliding layer (8-CTA clusters, 14-16 loads, the rest of
+    # them staged in shared memory) and 8-bit group-128 weights over a
+    # hidden of 8192 (32 loads: registers, shared memory, then plain loads;
+    # two rows per launch)
+    (F16, 4, 64, 4, 64, 1, 1, 8, 256, 3840, False, "default"),
+    (BF16, 8, 128, 8, 64, 2, 1, 2, 128, 8192, False, "default"),
 ]
 # query heads of the cases that also run the query side (the rest: none)
-QHEADS = {0: 16, 1: 8, 2: 4, 4: 8, 5: 4}
+QHEADS = {0: 16, 1: 8, 2: 4, 4: 8, 5: 4, 6: 16, 7: 4}
 
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"{'f16' if c[0] == F16 else 'bf16'}"
