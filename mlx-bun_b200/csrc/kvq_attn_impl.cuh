@@ -1569,33 +1569,40 @@ __global__ void __launch_bounds__((W + 1) * 32, NT == 1 ? 3 : 1) attn_bal_kernel
   if (hung && lane == 0) atomicExch(p.err, 1);
 }
 
-// Combine the partial slots of unit blockIdx.x for query row blockIdx.y;
-// blockDim.x == MG * D: thread (group gi, column d).  The unit's slots are
-// cut into G <= MG contiguous runs of at least 32 (one run when there are
-// few); group gi folds run gi 32 slots at a time — every
-// thread loads the batch's (m, l) and its own o[d] in one round (coalesced
-// across d) — into a running (M, L, o) in slot order, and group 0 combines
-// the runs in run order (deterministic: the same sums in every thread and
-// on every call with these shapes).  Long units spread over many CTAs (one
-// long sequence) thus merge in a quarter of the rounds.
+// Combine the partial slots of unit blockIdx.x for query row blockIdx.y,
+// columns [blockIdx.z * D / DC, (blockIdx.z + 1) * D / DC); blockDim.x ==
+// MG * D / DC: thread (group gi, column d).  The unit's slots are cut into
+// G <= MG contiguous runs of at least 16 (one run when there are few);
+// group gi folds run gi 32 (wide: 16) slots at a time — every thread loads the
+// batch's (m, l) and its own o[d] in one round (coalesced across d) — into
+// a running (M, L, o) in slot order, and group 0 combines the runs in run
+// order (deterministic: the same sums in every thread and on every call
+// with these shapes).  Long units spread over many CTAs (one long
+// sequence) thus merge in one or two rounds on D / 32 blocks per row.
 constexpr int kMergeSlots = 4096;  // partial slots per unit at most (launch shape)
-// Slot groups of the wide merge (512 threads a block, registers for the
-// 32-slot batches); the narrow merge (MG = 1, D threads) serves launches
-// whose units have few slots each, where extra groups would sit idle.
+// The wide merge: 16 slot groups of one warp each (512 threads a block),
+// each lane one d of a 32-wide slice of the row, the slices spread over
+// gridDim.z = D / 32 blocks, so a long unit's merge runs on D / 32 times
+// more SMs and folds a sixteenth of the slots per thread.  The narrow merge
+// (MG = 1, DC = 1, D threads) serves launches whose units have few slots
+// each, where extra groups would sit idle.
+constexpr int kWideMergeGroups = 16;
 template <int D>
-constexpr int merge_groups() {
-  return 512 / D;
+constexpr int wide_merge_chunks() {
+  return D / 32;
 }
 constexpr int kWideMergeSlots = 64;  // slots per unit above which the wide merge runs
-template <int D, int W, int NT, bool BF, int MG>
-__global__ void __launch_bounds__(MG * D) attn_bal_merge_kernel(const Params p, int grid) {
+template <int D, int W, int NT, bool BF, int MG, int DC>
+__global__ void __launch_bounds__(MG * (D / DC)) attn_bal_merge_kernel(const Params p, int grid) {
   constexpr int HQ = 8 * NT;
   constexpr int SLOT = HQ * (D + 2);  // floats per partial slot
+  constexpr int DW = D / DC;          // d per block: one per thread of a group
+  static_assert(D % DC == 0 && DW % 32 == 0, "merge slices are whole warps");
   __shared__ int64_t red_t[2];
   __shared__ float run_ml[MG][2];
-  __shared__ float run_o[MG][D];
+  __shared__ float run_o[MG][DW];
   const int u = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
-  const int gi = tid / D, d = tid - gi * D;
+  const int gi = tid / DW, dl = tid - gi * DW, d = blockIdx.z * DW + dl;
   const int Hkv = p.Hkv, b = u / Hkv, kvh = u - b * Hkv;
   const int64_t orow = (int64_t)b * p.Hq + kvh * p.nrep + r;
 
@@ -1650,17 +1657,20 @@ __global__ void __launch_bounds__(MG * D) attn_bal_merge_kernel(const Params p, 
   const int i_first = (int)(((U + 1) * C - 1) / RT);
   const int i_last = (int)(((U + T) * C - 1) / RT);
   const int nslots = (i_last - i_first + 1) * W;  // <= kMergeSlots (host launch shape)
-  const int G = min(MG, (nslots + 31) / 32);
+  const int G = min(MG, (nslots + 15) / 16);  // groups of at least 16 slots
   const float* base = p.ws_o + ((int64_t)i_first + u) * W * SLOT;
 
   float M = kNeg, L = 0.0f, acc = 0.0f;
   if (gi < G) {
     const int s0 = (int)((int64_t)gi * nslots / G), s1 = (int)((int64_t)(gi + 1) * nslots / G);
-    for (int j0 = s0; j0 < s1; j0 += 32) {
-      const int nj = min(32, s1 - j0);
-      float m[32], l[32], o[32];
+    // slots per round: 32 in the narrow merge, 16 in the wide one (whose
+    // groups hold about 16 slots each, within 128 registers a thread)
+    constexpr int NB = MG > 1 ? 16 : 32;
+    for (int j0 = s0; j0 < s1; j0 += NB) {
+      const int nj = min(NB, s1 - j0);
+      float m[NB], l[NB], o[NB];
 #pragma unroll
-      for (int k = 0; k < 32; k++) {
+      for (int k = 0; k < NB; k++) {
         const bool v = k < nj;
         const float* sp = base + (int64_t)(j0 + k) * SLOT;
         m[k] = v ? __ldcg(sp + r) : kNeg;
@@ -1669,12 +1679,12 @@ __global__ void __launch_bounds__(MG * D) attn_bal_merge_kernel(const Params p, 
       }
       float Mn = M;
 #pragma unroll
-      for (int k = 0; k < 32; k++) Mn = fmaxf(Mn, m[k]);
+      for (int k = 0; k < NB; k++) Mn = fmaxf(Mn, m[k]);
       const float a = ex2((M - Mn) * kLog2e);
       L *= a;
       acc *= a;
 #pragma unroll
-      for (int k = 0; k < 32; k++) {
+      for (int k = 0; k < NB; k++) {
         const float w = ex2((m[k] - Mn) * kLog2e);
         L = fmaf(l[k], w, L);
         acc = fmaf(o[k], w, acc);
@@ -1687,8 +1697,8 @@ __global__ void __launch_bounds__(MG * D) attn_bal_merge_kernel(const Params p, 
     return;
   }
   if (gi < G) {
-    run_o[gi][d] = acc;
-    if (d == 0) {
+    run_o[gi][dl] = acc;
+    if (dl == 0) {
       run_ml[gi][0] = M;
       run_ml[gi][1] = L;
     }
@@ -1701,7 +1711,7 @@ __global__ void __launch_bounds__(MG * D) attn_bal_merge_kernel(const Params p, 
     for (int k = 0; k < G; k++) {
       const float w = ex2((run_ml[k][0] - Mt) * kLog2e);
       Lt = fmaf(run_ml[k][1], w, Lt);
-      At = fmaf(run_o[k][d], w, At);
+      At = fmaf(run_o[k][dl], w, At);
     }
     write_row<D, BF>(p, orow, d, At, Mt, Lt);
   }
@@ -1821,15 +1831,15 @@ int32_t launch_rw(Params& p, const LaunchShape& s, int B, cudaStream_t st, int* 
     // merge of the per-warp partials, a programmatic dependent of the
     // attention grid (it waits for that grid inside, with griddepcontrol)
     // (wide when the units have many slots each: one long sequence)
-    constexpr int MG = merge_groups<D>();
+    constexpr int MG = kWideMergeGroups, DC = wide_merge_chunks<D>();
     const bool wide = (int64_t)s.ctas * kWarps > (int64_t)kWideMergeSlots * B * p.Hkv;
     void (*merge)(Params, int) =
-        wide ? (p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true, MG>
-                       : attn_bal_merge_kernel<D, kWarps, NT, false, MG>)
-             : (p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true, 1>
-                       : attn_bal_merge_kernel<D, kWarps, NT, false, 1>);
-    KVQ_CUDA_TRY(launch_pdl(merge, dim3((unsigned)(B * p.Hkv), (unsigned)p.nrep),
-                            dim3((wide ? MG : 1) * D), 0, st, p, s.ctas));
+        wide ? (p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true, MG, DC>
+                       : attn_bal_merge_kernel<D, kWarps, NT, false, MG, DC>)
+             : (p.bf16 ? attn_bal_merge_kernel<D, kWarps, NT, true, 1, 1>
+                       : attn_bal_merge_kernel<D, kWarps, NT, false, 1, 1>);
+    KVQ_CUDA_TRY(launch_pdl(merge, dim3((unsigned)(B * p.Hkv), (unsigned)p.nrep, wide ? DC : 1),
+                            dim3(wide ? MG * (D / DC) : D), 0, st, p, s.ctas));
   }
   return KVQ_OK;
 }
