@@ -107,6 +107,21 @@ def test_decode_one_long_unit_many_holders():
     assert max_abs(got, want, F16) <= TOL[F16]
 
 
+@pytest.mark.parametrize("case", [
+    (1, 8, 2, 20000, 64, 64, 4, F16),     # two row slices per merge row
+    (1, 4, 1, 12000, 256, 64, 8, BF16),   # eight slices, bf16
+    (1, 8, 1, 20000, 128, 32, 4, BF16),   # four slices, bf16, group 32
+], ids=lambda c: "-".join(map(str, c)))
+def test_decode_long_units_wide_merge(case):
+    """Units with hundreds of partial slots each take the wide merge: D / 32
+    blocks per (unit, query row), one-warp slot groups; every head size's
+    slicing against the oracle."""
+    B, Hq, Hkv, N, D, gs, bits, dt = case
+    got, want = run_decode(B, Hq, Hkv, N, D, gs, bits, dt, seed=60 + D)
+    record_parity(f"decode, long units, wide merge {case}", got, want, dt, f"<= {TOL[dt]}")
+    assert max_abs(got, want, dt) <= TOL[dt]
+
+
 def test_decode_through_ring_cache_config3():
     """Config 3 local layer: window 1024 ring after 4096 writes (3 wraps), kv8 D256."""
     import kvq
